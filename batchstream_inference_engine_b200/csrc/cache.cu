@@ -1,0 +1,267 @@
+// Paged-KV bookkeeping kernels: the per-step metadata builder and the K/V slot
+// write.
+//
+// Metadata.  The reference assembles every step on the host: positions per
+// sequence (src/server/torch_model.py:234-236), the flat-batch slices (:239) and,
+// per token, (block, offset) = BlockAllocator.locate (src/server/block_allocator.py:28-30),
+// which PagedKVCache.append turns into one indexed store per token (torch_model.py:149-153).
+// Here the block tables live on the device and one launch derives, for a ragged
+// batch of R rows with n_new[r] new tokens each:
+//     cu_q[r]      = sum_{j<r} n_new[j]                     (R + 1 entries)
+//     positions[t] = start_pos[r] + (t - cu_q[r])
+//     slots[t]     = table[row][pos / bs] * bs + pos % bs    (locate, flattened)
+//     context[r]   = start_pos[r] + n_new[r]
+// bit-exact with the reference allocator's locate().
+//
+// Slot write.  k/v rows [T, Hkv, D] (any token stride) land at
+// pool[h, slot / bs, slot % bs, :] with 16-byte vector loads and stores; an fp32
+// input into a bf16 pool is rounded to nearest-even, as torch's indexed
+// assignment into a bf16 tensor does.  Negative slots are padding and skipped.
+#include "common.cuh"
+
+namespace bsb {
+namespace {
+
+constexpr int kMetaThreads = 256;
+constexpr int kMaxMetaRows = 8192;
+
+__global__ void __launch_bounds__(kMetaThreads)
+    step_metadata_kernel(const int32_t* __restrict__ seq_rows, const int32_t* __restrict__ start_pos,
+                         const int32_t* __restrict__ n_new, int32_t R,
+                         const int32_t* __restrict__ block_tables, int64_t bt_stride,
+                         int32_t bt_rows, int32_t max_blocks, int32_t block_size,
+                         int32_t num_blocks, int32_t T, int32_t* __restrict__ cu_q,
+                         int32_t* __restrict__ positions, int32_t* __restrict__ slots,
+                         int32_t* __restrict__ context_lens, uint32_t* status) {
+  __shared__ int32_t cu[kMaxMetaRows + 1];
+  __shared__ int32_t warp_tot[kMetaThreads / 32];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+
+  // Block-wide exclusive scan of n_new in chunks of kMetaThreads.
+  int32_t carry = 0;
+  for (int32_t base = 0; base < R; base += kMetaThreads) {
+    const int32_t r = base + tid;
+    const int32_t v = (r < R) ? max(0, n_new[r]) : 0;
+    int32_t incl = v;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int32_t n = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += n;
+    }
+    if (lane == 31) warp_tot[warp] = incl;
+    __syncthreads();
+    int32_t before = carry, total = 0;
+    for (int w = 0; w < kMetaThreads / 32; ++w) {
+      if (w < warp) before += warp_tot[w];
+      total += warp_tot[w];
+    }
+    if (r < R) cu[r] = before + incl - v;
+    __syncthreads();
+    carry += total;
+  }
+  if (tid == 0) cu[R] = carry;
+  __syncthreads();
+
+  if (blockIdx.x == 0) {
+    for (int32_t r = tid; r <= R; r += kMetaThreads) cu_q[r] = cu[r];
+    for (int32_t r = tid; r < R; r += kMetaThreads) context_lens[r] = start_pos[r] + max(0, n_new[r]);
+  }
+
+  const int32_t t = blockIdx.x * kMetaThreads + tid;
+  if (t >= T) return;
+  if (t >= cu[R]) {  // more tokens requested than rows provide
+    positions[t] = 0;
+    slots[t] = -1;
+    return;
+  }
+  // Last row r with cu[r] <= t (rows with n_new == 0 are skipped by '<=').
+  int32_t lo = 0, hi = R - 1;
+  while (lo < hi) {
+    const int32_t mid = (lo + hi + 1) >> 1;
+    if (cu[mid] <= t) lo = mid; else hi = mid - 1;
+  }
+  const int32_t r = lo;
+  const int32_t pos = start_pos[r] + (t - cu[r]);
+  positions[t] = pos;
+  const int32_t row = seq_rows != nullptr ? seq_rows[r] : r;
+  const int32_t bi = pos / block_size;
+  if (row < 0 || row >= bt_rows || pos < 0 || bi >= max_blocks) {
+    set_status(status, row < 0 || row >= bt_rows ? kStatusBadRow : kStatusBadLength);
+    slots[t] = -1;
+    return;
+  }
+  const int32_t blk = block_tables[static_cast<int64_t>(row) * bt_stride + bi];
+  if (blk < 0 || blk >= num_blocks) {
+    set_status(status, kStatusBadBlock);
+    slots[t] = -1;
+    return;
+  }
+  slots[t] = blk * block_size + pos % block_size;
+}
+
+// 8 elements per thread: 16-byte accesses on the bf16 side, 2 x 16 on fp32.
+__device__ __forceinline__ void load8(const __nv_bfloat16* p, float (&v)[8]) {
+  const uint4 raw = *reinterpret_cast<const uint4*>(p);
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 f = __bfloat1622float2(h[i]);
+    v[2 * i] = f.x;
+    v[2 * i + 1] = f.y;
+  }
+}
+__device__ __forceinline__ void load8(const float* p, float (&v)[8]) {
+  const float4 a = reinterpret_cast<const float4*>(p)[0];
+  const float4 b = reinterpret_cast<const float4*>(p)[1];
+  v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+  v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+}
+__device__ __forceinline__ void store8(__nv_bfloat16* p, const float (&v)[8]) {
+  uint4 raw;
+  uint32_t* w = reinterpret_cast<uint32_t*>(&raw);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) w[i] = pack_bf16x2(v[2 * i], v[2 * i + 1]);
+  *reinterpret_cast<uint4*>(p) = raw;
+}
+__device__ __forceinline__ void store8(float* p, const float (&v)[8]) {
+  reinterpret_cast<float4*>(p)[0] = make_float4(v[0], v[1], v[2], v[3]);
+  reinterpret_cast<float4*>(p)[1] = make_float4(v[4], v[5], v[6], v[7]);
+}
+
+// bf16 -> bf16 keeps the raw bits (no float round trip needed, but it is exact).
+template <typename Tin, typename Tpool>
+__global__ void __launch_bounds__(256)
+    slot_write_vec_kernel(const Tin* __restrict__ k, const Tin* __restrict__ v, int64_t k_stride,
+                          int64_t v_stride, const int32_t* __restrict__ slots, int32_t T,
+                          int32_t Hkv, int32_t D, Tpool* __restrict__ k_pool,
+                          Tpool* __restrict__ v_pool, int64_t pool_slots, uint32_t* status) {
+  const int32_t vecs = D >> 3;
+  const int64_t per_tensor = static_cast<int64_t>(T) * Hkv * vecs;
+  const int64_t total = 2 * per_tensor;
+  for (int64_t idx = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; idx < total;
+       idx += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const bool is_v = idx >= per_tensor;
+    const int64_t e = is_v ? idx - per_tensor : idx;
+    const int32_t j = static_cast<int32_t>(e % vecs);
+    const int64_t th = e / vecs;
+    const int32_t h = static_cast<int32_t>(th % Hkv);
+    const int32_t t = static_cast<int32_t>(th / Hkv);
+    const int32_t slot = __ldg(slots + t);
+    if (slot < 0) continue;
+    if (slot >= pool_slots) {
+      set_status(status, kStatusBadSlot);
+      continue;
+    }
+    const Tin* src = (is_v ? v + t * v_stride : k + t * k_stride) + h * D + 8 * j;
+    Tpool* dst = (is_v ? v_pool : k_pool) + (h * pool_slots + slot) * D + 8 * j;
+    float x[8];
+    load8(src, x);
+    store8(dst, x);
+  }
+}
+
+template <typename T>
+__device__ __forceinline__ float as_float(T x);
+template <>
+__device__ __forceinline__ float as_float<float>(float x) { return x; }
+template <>
+__device__ __forceinline__ float as_float<__nv_bfloat16>(__nv_bfloat16 x) {
+  return __bfloat162float(x);
+}
+template <typename T>
+__device__ __forceinline__ T from_float(float x);
+template <>
+__device__ __forceinline__ float from_float<float>(float x) { return x; }
+template <>
+__device__ __forceinline__ __nv_bfloat16 from_float<__nv_bfloat16>(float x) {
+  return __float2bfloat16_rn(x);
+}
+
+// One element per thread, for head sizes that are not a multiple of 8.
+template <typename Tin, typename Tpool>
+__global__ void __launch_bounds__(256)
+    slot_write_scalar_kernel(const Tin* __restrict__ k, const Tin* __restrict__ v, int64_t k_stride,
+                             int64_t v_stride, const int32_t* __restrict__ slots, int32_t T,
+                             int32_t Hkv, int32_t D, Tpool* __restrict__ k_pool,
+                             Tpool* __restrict__ v_pool, int64_t pool_slots, uint32_t* status) {
+  const int64_t per_tensor = static_cast<int64_t>(T) * Hkv * D;
+  for (int64_t idx = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
+       idx < 2 * per_tensor; idx += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const bool is_v = idx >= per_tensor;
+    const int64_t e = is_v ? idx - per_tensor : idx;
+    const int32_t d = static_cast<int32_t>(e % D);
+    const int64_t th = e / D;
+    const int32_t h = static_cast<int32_t>(th % Hkv);
+    const int32_t t = static_cast<int32_t>(th / Hkv);
+    const int32_t slot = __ldg(slots + t);
+    if (slot < 0) continue;
+    if (slot >= pool_slots) {
+      set_status(status, kStatusBadSlot);
+      continue;
+    }
+    const Tin* src = (is_v ? v + t * v_stride : k + t * k_stride) + h * D + d;
+    Tpool* dst = (is_v ? v_pool : k_pool) + (h * pool_slots + slot) * D + d;
+    *dst = from_float<Tpool>(as_float<Tin>(*src));
+  }
+}
+
+template <typename Tin, typename Tpool>
+int launch_slot_write_t(const void* k, const void* v, int64_t ks, int64_t vs, const int32_t* slots,
+                        int32_t T, int32_t Hkv, int32_t D, void* kp, void* vp, int64_t pool_slots,
+                        bool vec, int sms, uint32_t* status, cudaStream_t stream) {
+  const int64_t work = 2ll * T * Hkv * (vec ? D / 8 : D);
+  if (work == 0) return 0;
+  int64_t blocks = (work + 255) / 256;
+  const int64_t cap = static_cast<int64_t>(sms) * 8;
+  if (blocks > cap) blocks = cap;
+  if (vec) {
+    slot_write_vec_kernel<Tin, Tpool><<<static_cast<int>(blocks), 256, 0, stream>>>(
+        static_cast<const Tin*>(k), static_cast<const Tin*>(v), ks, vs, slots, T, Hkv, D,
+        static_cast<Tpool*>(kp), static_cast<Tpool*>(vp), pool_slots, status);
+  } else {
+    slot_write_scalar_kernel<Tin, Tpool><<<static_cast<int>(blocks), 256, 0, stream>>>(
+        static_cast<const Tin*>(k), static_cast<const Tin*>(v), ks, vs, slots, T, Hkv, D,
+        static_cast<Tpool*>(kp), static_cast<Tpool*>(vp), pool_slots, status);
+  }
+  return static_cast<int>(cudaGetLastError());
+}
+
+}  // namespace
+
+int max_metadata_rows() { return kMaxMetaRows; }
+
+int launch_step_metadata(const int32_t* seq_rows, const int32_t* start_pos, const int32_t* n_new,
+                         int32_t R, const int32_t* block_tables, int64_t bt_stride,
+                         int32_t bt_rows, int32_t max_blocks, int32_t block_size,
+                         int32_t num_blocks, int32_t T, int32_t* cu_q, int32_t* positions,
+                         int32_t* slots, int32_t* context_lens, uint32_t* status,
+                         cudaStream_t stream) {
+  const int grid = T > 0 ? (T + kMetaThreads - 1) / kMetaThreads : 1;
+  step_metadata_kernel<<<grid, kMetaThreads, 0, stream>>>(
+      seq_rows, start_pos, n_new, R, block_tables, bt_stride, bt_rows, max_blocks, block_size,
+      num_blocks, T, cu_q, positions, slots, context_lens, status);
+  return static_cast<int>(cudaGetLastError());
+}
+
+// in_bf16 / pool_bf16: element types of the k/v rows and of the pool.
+int launch_slot_write(const void* k, const void* v, int64_t k_stride, int64_t v_stride,
+                      int in_bf16, const int32_t* slots, int32_t T, int32_t Hkv, int32_t D,
+                      void* k_pool, void* v_pool, int pool_bf16, int64_t pool_slots, bool vec,
+                      int sms, uint32_t* status, cudaStream_t stream) {
+  if (in_bf16 && pool_bf16)
+    return launch_slot_write_t<__nv_bfloat16, __nv_bfloat16>(k, v, k_stride, v_stride, slots, T,
+                                                            Hkv, D, k_pool, v_pool, pool_slots,
+                                                            vec, sms, status, stream);
+  if (in_bf16)
+    return launch_slot_write_t<__nv_bfloat16, float>(k, v, k_stride, v_stride, slots, T, Hkv, D,
+                                                     k_pool, v_pool, pool_slots, vec, sms, status,
+                                                     stream);
+  if (pool_bf16)
+    return launch_slot_write_t<float, __nv_bfloat16>(k, v, k_stride, v_stride, slots, T, Hkv, D,
+                                                     k_pool, v_pool, pool_slots, vec, sms, status,
+                                                     stream);
+  return launch_slot_write_t<float, float>(k, v, k_stride, v_stride, slots, T, Hkv, D, k_pool,
+                                           v_pool, pool_slots, vec, sms, status, stream);
+}
+
+}  // namespace bsb

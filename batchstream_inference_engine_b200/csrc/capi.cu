@@ -1,0 +1,540 @@
+// C ABI of the paged-attention path (declared in include/batchstream_b200.h).
+//
+// Host-side validation mirrors the reference op's check_inputs
+// (csrc/paged_attention.cpp:22-44): every malformed input is an error code plus a
+// message, never a crash and never a device fault.  Kernel launches go on the
+// caller's stream; nothing here allocates device memory.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "../../include/batchstream_b200.h"
+#include "decode.cuh"
+
+namespace bsb {
+int max_metadata_rows();
+int launch_step_metadata(const int32_t* seq_rows, const int32_t* start_pos, const int32_t* n_new,
+                         int32_t R, const int32_t* block_tables, int64_t bt_stride,
+                         int32_t bt_rows, int32_t max_blocks, int32_t block_size,
+                         int32_t num_blocks, int32_t T, int32_t* cu_q, int32_t* positions,
+                         int32_t* slots, int32_t* context_lens, uint32_t* status,
+                         cudaStream_t stream);
+int launch_slot_write(const void* k, const void* v, int64_t k_stride, int64_t v_stride,
+                      int in_bf16, const int32_t* slots, int32_t T, int32_t Hkv, int32_t D,
+                      void* k_pool, void* v_pool, int pool_bf16, int64_t pool_slots, bool vec,
+                      int sms, uint32_t* status, cudaStream_t stream);
+}  // namespace bsb
+
+namespace {
+
+thread_local std::string g_error;
+
+int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_error = buf;
+  return code;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+  return fail(BS_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+#define BS_CHECK(cond, ...)                      \
+  do {                                           \
+    if (!(cond)) return fail(BS_ERR_INVALID, __VA_ARGS__); \
+  } while (0)
+
+constexpr int64_t kMaxHeadDim = 256;
+constexpr int64_t kMaxGroups = 16;
+constexpr int64_t kInt32Max = 2147483647ll;
+
+struct DeviceInfo {
+  int sms = 0;
+  int occ_mma[2][2] = {{0, 0}, {0, 0}};  // [d128][g16]
+  int occ_simt[2][2][2] = {};           // [bf16][d>64 bucket][g16] (coarse cache)
+};
+
+std::mutex g_mu;
+std::vector<DeviceInfo> g_devices;
+
+int current_device_info(DeviceInfo** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  std::lock_guard<std::mutex> lock(g_mu);
+  if (static_cast<int>(g_devices.size()) <= dev) g_devices.resize(dev + 1);
+  DeviceInfo& d = g_devices[dev];
+  if (d.sms == 0) {
+    int sms = 0;
+    e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceGetAttribute");
+    d.sms = sms;
+  }
+  *out = &d;
+  return BS_OK;
+}
+
+bool use_mma_path(int32_t dtype, int64_t block_size, int64_t head_dim, int64_t groups) {
+  return dtype == BS_BF16 && block_size == 16 && (head_dim == 64 || head_dim == 128) &&
+         groups <= kMaxGroups;
+}
+
+// Persistent grid size for the chosen decode kernel on the current device.
+int decode_grid(bool mma, int32_t dtype, int64_t head_dim, int64_t groups, int* grid) {
+  DeviceInfo* d = nullptr;
+  if (int rc = current_device_info(&d)) return rc;
+  int occ = 0;
+  {
+    std::lock_guard<std::mutex> lock(g_mu);
+    int* slot = mma ? &d->occ_mma[head_dim == 128][groups > 8]
+                    : &d->occ_simt[dtype == BS_BF16][head_dim > 64][groups > 8];
+    if (*slot == 0) {
+      const int n = mma ? bsb::decode_mma_ctas_per_sm(static_cast<int>(head_dim),
+                                                      static_cast<int>(groups))
+                        : bsb::decode_simt_ctas_per_sm(static_cast<int>(head_dim),
+                                                       static_cast<int>(groups),
+                                                       dtype == BS_BF16);
+      if (n <= 0) {
+        return fail(BS_ERR_CUDA, "occupancy query for the decode kernel failed (%d)", n);
+      }
+      *slot = n;
+    }
+    occ = *slot;
+  }
+  *grid = d->sms * occ;
+  return BS_OK;
+}
+
+int64_t round_up(int64_t x, int64_t m) { return (x + m - 1) / m * m; }
+
+int32_t record_stride(int64_t groups, int64_t head_dim) {
+  return static_cast<int32_t>(round_up(groups * head_dim + 2 * groups, 4));
+}
+
+// Workspace layout: [status 256 B][counters][staging ints][partial records].
+struct WsLayout {
+  int64_t counters, staging, partials, total;
+};
+
+WsLayout ws_layout(int64_t segments, int64_t staging_ints, int64_t grid, int64_t rec_stride) {
+  WsLayout w;
+  w.counters = 256;
+  w.staging = w.counters + round_up(segments * 4, 256);
+  w.partials = w.staging + round_up(staging_ints * 4, 256);
+  w.total = w.partials + round_up(2 * grid * rec_stride * 4, 256);
+  return w;
+}
+
+// ------------------------------------------------------------------ tensor maps
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+int get_encode_fn(EncodeTiledFn* fn) {
+  static EncodeTiledFn cached = nullptr;
+  static std::once_flag once;
+  static cudaError_t err = cudaSuccess;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    err = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q);
+    if (err == cudaSuccess && q == cudaDriverEntryPointSuccess) cached = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  if (cached == nullptr) {
+    return fail(BS_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable (%s)", cudaGetErrorString(err));
+  }
+  *fn = cached;
+  return BS_OK;
+}
+
+// [rows, head_dim] bf16 view of one pool, boxes of 16 rows x 64 columns,
+// 128-byte swizzle (the layout the decode kernel's ldmatrix addressing expects).
+int encode_pool_map(CUtensorMap* map, const void* base, int64_t rows, int64_t head_dim) {
+  EncodeTiledFn fn = nullptr;
+  if (int rc = get_encode_fn(&fn)) return rc;
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(head_dim), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(head_dim * 2)};
+  cuuint32_t box[2] = {64, 16};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides,
+                  box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(BS_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", static_cast<int>(r));
+  return BS_OK;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// The pointer must be device (or managed) memory of the current device, so that
+// a host tensor passed by mistake is an error instead of a device fault.
+int require_device(const void* p, const char* what) {
+  cudaPointerAttributes attr;
+  cudaError_t e = cudaPointerGetAttributes(&attr, p);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return cuda_fail(e, what);
+  }
+  if (attr.type != cudaMemoryTypeDevice && attr.type != cudaMemoryTypeManaged) {
+    return fail(BS_ERR_INVALID, "%s must be CUDA device memory", what);
+  }
+  int dev = 0;
+  e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if (attr.type == cudaMemoryTypeDevice && attr.device != dev) {
+    return fail(BS_ERR_INVALID, "%s is on device %d but the current device is %d", what,
+                attr.device, dev);
+  }
+  return BS_OK;
+}
+
+bool is_contiguous(int32_t ndim, const int64_t* shape, const int64_t* strides) {
+  int64_t expect = 1;
+  for (int32_t d = ndim - 1; d >= 0; --d) {
+    if (shape[d] != 1 && strides[d] != expect) return false;
+    expect *= shape[d];
+  }
+  return true;
+}
+
+// Shared launch of the decode kernels once everything is validated.
+int launch_decode(bsb::DecodeArgs& a, int32_t dtype, int grid, cudaStream_t stream) {
+  const bool mma = use_mma_path(dtype, a.block_size, a.head_dim, a.groups);
+  int rc;
+  if (mma) {
+    CUtensorMap kmap, vmap;
+    const int64_t rows = static_cast<int64_t>(a.num_kv_heads) * a.num_blocks * a.block_size;
+    if ((rc = encode_pool_map(&kmap, a.k_pool, rows, a.head_dim))) return rc;
+    if ((rc = encode_pool_map(&vmap, a.v_pool, rows, a.head_dim))) return rc;
+    rc = bsb::launch_decode_mma(a, kmap, vmap, grid, stream);
+  } else {
+    rc = bsb::launch_decode_simt(a, dtype == BS_BF16, grid, stream);
+  }
+  if (rc != 0) return cuda_fail(static_cast<cudaError_t>(rc), "decode kernel launch");
+  return BS_OK;
+}
+
+int dtype_size(int32_t dtype) { return dtype == BS_BF16 ? 2 : 4; }
+
+}  // namespace
+
+extern "C" {
+
+const char* bs_last_error(void) { return g_error.c_str(); }
+
+const char* bs_version(void) { return "batchstream_b200 0.1 (sm_100a)"; }
+
+int bs_paged_attention_workspace_bytes(int64_t num_heads, int64_t num_kv_heads, int64_t head_dim,
+                                       int64_t block_table_len, int32_t dtype,
+                                       int64_t block_size, uint64_t* bytes_out) {
+  BS_CHECK(bytes_out != nullptr, "bytes_out is null");
+  BS_CHECK(num_kv_heads > 0 && num_heads % num_kv_heads == 0, "heads must equal kv_heads * groups");
+  const int64_t groups = num_heads / num_kv_heads;
+  int grid = 0;
+  if (int rc = decode_grid(use_mma_path(dtype, block_size, head_dim, groups), dtype, head_dim,
+                           groups, &grid))
+    return rc;
+  const WsLayout w = ws_layout(num_kv_heads, 1 + block_table_len, grid,
+                               record_stride(groups, head_dim));
+  *bytes_out = static_cast<uint64_t>(w.total);
+  return BS_OK;
+}
+
+int bs_paged_attention(const void* query, int32_t query_dtype, int32_t query_ndim,
+                       const int64_t* query_shape, const int64_t* query_strides,
+                       const void* keys, int32_t keys_dtype, int32_t keys_ndim,
+                       const int64_t* keys_shape, const int64_t* keys_strides,
+                       const void* values, int32_t values_dtype, int32_t values_ndim,
+                       const int64_t* values_shape, const int64_t* values_strides,
+                       const int64_t* block_table, int64_t block_table_len, int64_t length,
+                       int64_t block_size, int64_t groups, double scaling, void* output,
+                       void* workspace, uint64_t workspace_bytes, void* stream) {
+  // The reference's checks, in its order (csrc/paged_attention.cpp:25-43).
+  BS_CHECK((query_dtype == BS_BF16 || query_dtype == BS_F32) && keys_dtype == query_dtype &&
+               values_dtype == query_dtype,
+           "query, keys and values must all be bfloat16 or all float32");
+  BS_CHECK(query_ndim == 2, "query must have shape (heads, head_dim)");
+  BS_CHECK(keys_ndim == 4, "keys must have shape (kv_heads, blocks, block_size, head_dim)");
+  bool same = values_ndim == keys_ndim;
+  for (int d = 0; same && d < 4; ++d) same = keys_shape[d] == values_shape[d];
+  BS_CHECK(same, "keys and values must have the same shape");
+  BS_CHECK(is_contiguous(4, keys_shape, keys_strides) &&
+               is_contiguous(4, values_shape, values_strides),
+           "keys and values must be contiguous");
+  BS_CHECK(block_size > 0 && block_size == keys_shape[2], "block_size does not match keys");
+  BS_CHECK(query_shape[1] == keys_shape[3], "query and keys disagree on head_dim");
+  BS_CHECK(groups > 0 && query_shape[0] == keys_shape[0] * groups,
+           "heads must equal kv_heads * groups");
+  BS_CHECK(length > 0, "length must be positive");
+  const int64_t blocks_needed = (length + block_size - 1) / block_size;
+  BS_CHECK(block_table != nullptr || blocks_needed == 0, "block table is null");
+  BS_CHECK(block_table_len >= blocks_needed, "block table is too short for length");
+  const int64_t num_blocks = keys_shape[1];
+  for (int64_t i = 0; i < blocks_needed; ++i) {
+    BS_CHECK(block_table[i] >= 0 && block_table[i] < num_blocks, "block table entry out of range");
+  }
+  // This library's own requirements.
+  const int64_t heads = query_shape[0], head_dim = query_shape[1], kv_heads = keys_shape[0];
+  BS_CHECK(is_contiguous(2, query_shape, query_strides),
+           "query must be contiguous (the binding copies it first)");
+  if (head_dim > kMaxHeadDim || groups > kMaxGroups) {
+    return fail(BS_ERR_UNSUPPORTED, "head_dim <= %lld and groups <= %lld are supported",
+                static_cast<long long>(kMaxHeadDim), static_cast<long long>(kMaxGroups));
+  }
+  if (kv_heads * num_blocks * block_size > kInt32Max) {
+    return fail(BS_ERR_UNSUPPORTED, "pool has more than 2^31 rows");
+  }
+  BS_CHECK(query != nullptr && keys != nullptr && values != nullptr && output != nullptr,
+           "null tensor pointer");
+  if (int rc = require_device(query, "query")) return rc;
+  if (int rc = require_device(keys, "keys")) return rc;
+  if (int rc = require_device(values, "values")) return rc;
+  if (int rc = require_device(output, "output")) return rc;
+
+  int grid_max = 0;
+  const bool mma = use_mma_path(query_dtype, block_size, head_dim, groups);
+  if (int rc = decode_grid(mma, query_dtype, head_dim, groups, &grid_max)) return rc;
+  const WsLayout w = ws_layout(kv_heads, 1 + blocks_needed, grid_max,
+                               record_stride(groups, head_dim));
+  if (workspace == nullptr || workspace_bytes < static_cast<uint64_t>(w.total)) {
+    return fail(BS_ERR_WORKSPACE, "workspace of %llu bytes is smaller than the %lld needed",
+                static_cast<unsigned long long>(workspace_bytes), static_cast<long long>(w.total));
+  }
+  if (mma && (!aligned16(query) || !aligned16(keys) || !aligned16(values))) {
+    return fail(BS_ERR_INVALID, "query, keys and values must be 16-byte aligned");
+  }
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+
+  // Stage [length, table...] as int32 into the workspace.
+  std::vector<int32_t> staged(static_cast<size_t>(1 + blocks_needed));
+  staged[0] = static_cast<int32_t>(length);
+  for (int64_t i = 0; i < blocks_needed; ++i) staged[1 + i] = static_cast<int32_t>(block_table[i]);
+  int32_t* dev_staged = reinterpret_cast<int32_t*>(ws + w.staging);
+  cudaError_t e = cudaMemcpyAsync(dev_staged, staged.data(), staged.size() * sizeof(int32_t),
+                                  cudaMemcpyHostToDevice, st);
+  if (e != cudaSuccess) return cuda_fail(e, "staging the block table");
+
+  bsb::DecodeArgs a{};
+  a.q = query;
+  a.q_stride_seq = heads * head_dim;
+  a.out = output;
+  a.o_stride_seq = heads * head_dim;
+  a.k_pool = keys;
+  a.v_pool = values;
+  a.block_tables = dev_staged + 1;
+  a.bt_stride = blocks_needed;
+  a.bt_rows = 1;
+  a.seq_rows = nullptr;
+  a.context_lens = dev_staged;
+  a.num_seqs = 1;
+  a.num_heads = static_cast<int32_t>(heads);
+  a.num_kv_heads = static_cast<int32_t>(kv_heads);
+  a.groups = static_cast<int32_t>(groups);
+  a.head_dim = static_cast<int32_t>(head_dim);
+  a.block_size = static_cast<int32_t>(block_size);
+  a.num_blocks = static_cast<int32_t>(num_blocks);
+  a.max_blocks = static_cast<int32_t>(blocks_needed);
+  a.scale = static_cast<float>(scaling);
+  a.partials = reinterpret_cast<float*>(ws + w.partials);
+  a.rec_stride = record_stride(groups, head_dim);
+  a.seg_counters = reinterpret_cast<int32_t*>(ws + w.counters);
+  a.status = reinterpret_cast<uint32_t*>(ws);
+  // A few blocks per CTA keeps the cross-CTA merge short for one sequence.
+  const int64_t units = kv_heads * blocks_needed;
+  int64_t grid = (units + 7) / 8;
+  if (grid < 1) grid = 1;
+  if (grid > grid_max) grid = grid_max;
+  return launch_decode(a, query_dtype, static_cast<int>(grid), st);
+}
+
+int bs_paged_attention_batched_workspace_bytes(int64_t num_seqs, int64_t num_heads,
+                                               int64_t num_kv_heads, int64_t head_dim,
+                                               int64_t block_size, int32_t dtype,
+                                               uint64_t* bytes_out) {
+  BS_CHECK(bytes_out != nullptr, "bytes_out is null");
+  BS_CHECK(num_kv_heads > 0 && num_heads % num_kv_heads == 0, "heads must equal kv_heads * groups");
+  const int64_t groups = num_heads / num_kv_heads;
+  int grid = 0;
+  if (int rc = decode_grid(use_mma_path(dtype, block_size, head_dim, groups), dtype, head_dim,
+                           groups, &grid))
+    return rc;
+  const WsLayout w = ws_layout(num_seqs * num_kv_heads, 0, grid, record_stride(groups, head_dim));
+  *bytes_out = static_cast<uint64_t>(w.total);
+  return BS_OK;
+}
+
+int bs_paged_attention_batched(const void* query, int64_t query_seq_stride, const void* key_pool,
+                               const void* value_pool, const int32_t* block_tables,
+                               int64_t table_stride, int64_t table_rows, const int32_t* seq_rows,
+                               const int32_t* context_lens, int64_t num_seqs, int64_t num_heads,
+                               int64_t num_kv_heads, int64_t head_dim, int64_t block_size,
+                               int64_t num_blocks, int64_t max_blocks_per_seq, int32_t dtype,
+                               double scaling, int64_t units_hint, void* output,
+                               int64_t output_seq_stride, void* workspace,
+                               uint64_t workspace_bytes, void* stream) {
+  BS_CHECK(dtype == BS_BF16 || dtype == BS_F32, "dtype must be bfloat16 or float32");
+  BS_CHECK(num_seqs >= 0, "num_seqs must be non-negative");
+  BS_CHECK(num_kv_heads > 0 && num_heads > 0 && num_heads % num_kv_heads == 0,
+           "heads must equal kv_heads * groups");
+  BS_CHECK(head_dim > 0 && block_size > 0 && num_blocks > 0, "sizes must be positive");
+  BS_CHECK(max_blocks_per_seq > 0 && max_blocks_per_seq <= table_stride,
+           "max_blocks_per_seq must be in [1, table_stride]");
+  BS_CHECK(table_rows > 0 && table_rows <= kInt32Max, "table_rows out of range");
+  BS_CHECK(query_seq_stride >= num_heads * head_dim && output_seq_stride >= num_heads * head_dim,
+           "sequence strides must cover heads * head_dim");
+  const int64_t groups = num_heads / num_kv_heads;
+  if (head_dim > kMaxHeadDim || groups > kMaxGroups) {
+    return fail(BS_ERR_UNSUPPORTED, "head_dim <= %lld and groups <= %lld are supported",
+                static_cast<long long>(kMaxHeadDim), static_cast<long long>(kMaxGroups));
+  }
+  if (num_kv_heads * num_blocks * block_size > kInt32Max ||
+      max_blocks_per_seq * block_size > kInt32Max || num_seqs > kInt32Max) {
+    return fail(BS_ERR_UNSUPPORTED, "pool or table larger than 2^31 rows");
+  }
+  if (num_seqs == 0) return BS_OK;
+  BS_CHECK(query && key_pool && value_pool && block_tables && context_lens && output,
+           "null pointer argument");
+  const bool mma = use_mma_path(dtype, block_size, head_dim, groups);
+  if (mma) {
+    BS_CHECK(aligned16(query) && aligned16(key_pool) && aligned16(value_pool) &&
+                 (query_seq_stride * 2) % 16 == 0,
+             "query, pools and query rows must be 16-byte aligned");
+  }
+  int grid_max = 0;
+  if (int rc = decode_grid(mma, dtype, head_dim, groups, &grid_max)) return rc;
+  const WsLayout w =
+      ws_layout(num_seqs * num_kv_heads, 0, grid_max, record_stride(groups, head_dim));
+  if (workspace == nullptr || workspace_bytes < static_cast<uint64_t>(w.total)) {
+    return fail(BS_ERR_WORKSPACE, "workspace of %llu bytes is smaller than the %lld needed",
+                static_cast<unsigned long long>(workspace_bytes), static_cast<long long>(w.total));
+  }
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  bsb::DecodeArgs a{};
+  a.q = query;
+  a.q_stride_seq = query_seq_stride;
+  a.out = output;
+  a.o_stride_seq = output_seq_stride;
+  a.k_pool = key_pool;
+  a.v_pool = value_pool;
+  a.block_tables = block_tables;
+  a.bt_stride = table_stride;
+  a.bt_rows = static_cast<int32_t>(table_rows);
+  a.seq_rows = seq_rows;
+  a.context_lens = context_lens;
+  a.num_seqs = static_cast<int32_t>(num_seqs);
+  a.num_heads = static_cast<int32_t>(num_heads);
+  a.num_kv_heads = static_cast<int32_t>(num_kv_heads);
+  a.groups = static_cast<int32_t>(groups);
+  a.head_dim = static_cast<int32_t>(head_dim);
+  a.block_size = static_cast<int32_t>(block_size);
+  a.num_blocks = static_cast<int32_t>(num_blocks);
+  a.max_blocks = static_cast<int32_t>(max_blocks_per_seq);
+  a.scale = static_cast<float>(scaling);
+  a.partials = reinterpret_cast<float*>(ws + w.partials);
+  a.rec_stride = record_stride(groups, head_dim);
+  a.seg_counters = reinterpret_cast<int32_t*>(ws + w.counters);
+  a.status = reinterpret_cast<uint32_t*>(ws);
+  int64_t grid = grid_max;
+  if (units_hint > 0) {
+    const int64_t want = (units_hint + 3) / 4;
+    if (want < grid) grid = want;
+  }
+  return launch_decode(a, dtype, static_cast<int>(grid), static_cast<cudaStream_t>(stream));
+}
+
+int bs_reshape_and_cache(const void* key, const void* value, int64_t key_token_stride,
+                         int64_t value_token_stride, int32_t input_dtype,
+                         const int32_t* slot_mapping, int64_t num_tokens, void* key_pool,
+                         void* value_pool, int32_t pool_dtype, int64_t num_kv_heads,
+                         int64_t num_blocks, int64_t block_size, int64_t head_dim,
+                         uint32_t* status, void* stream) {
+  BS_CHECK(input_dtype == BS_BF16 || input_dtype == BS_F32, "input dtype must be bf16 or fp32");
+  BS_CHECK(pool_dtype == BS_BF16 || pool_dtype == BS_F32, "pool dtype must be bf16 or fp32");
+  BS_CHECK(num_tokens >= 0 && num_tokens <= kInt32Max, "num_tokens out of range");
+  BS_CHECK(num_kv_heads > 0 && num_blocks > 0 && block_size > 0 && head_dim > 0,
+           "sizes must be positive");
+  BS_CHECK(key_token_stride >= num_kv_heads * head_dim &&
+               value_token_stride >= num_kv_heads * head_dim,
+           "token strides must cover kv_heads * head_dim");
+  const int64_t pool_slots = num_blocks * block_size;
+  if (num_kv_heads * pool_slots > kInt32Max * 64ll) {
+    return fail(BS_ERR_UNSUPPORTED, "pool too large");
+  }
+  if (num_tokens == 0) return BS_OK;
+  BS_CHECK(key && value && slot_mapping && key_pool && value_pool, "null pointer argument");
+  const int in_sz = dtype_size(input_dtype), pool_sz = dtype_size(pool_dtype);
+  const bool vec = head_dim % 8 == 0 && aligned16(key) && aligned16(value) &&
+                   aligned16(key_pool) && aligned16(value_pool) &&
+                   (key_token_stride * in_sz) % 16 == 0 && (value_token_stride * in_sz) % 16 == 0 &&
+                   (head_dim * pool_sz) % 16 == 0;
+  DeviceInfo* d = nullptr;
+  if (int rc = current_device_info(&d)) return rc;
+  const int rc = bsb::launch_slot_write(
+      key, value, key_token_stride, value_token_stride, input_dtype == BS_BF16, slot_mapping,
+      static_cast<int32_t>(num_tokens), static_cast<int32_t>(num_kv_heads),
+      static_cast<int32_t>(head_dim), key_pool, value_pool, pool_dtype == BS_BF16, pool_slots, vec,
+      d->sms, status, static_cast<cudaStream_t>(stream));
+  if (rc != 0) return cuda_fail(static_cast<cudaError_t>(rc), "slot write launch");
+  return BS_OK;
+}
+
+int bs_step_metadata(const int32_t* seq_rows, const int32_t* start_pos, const int32_t* n_new,
+                     int64_t num_rows, const int32_t* block_tables, int64_t table_stride,
+                     int64_t table_rows, int64_t max_blocks_per_seq, int64_t block_size,
+                     int64_t num_blocks, int64_t num_tokens, int32_t* cu_q, int32_t* positions,
+                     int32_t* slot_mapping, int32_t* context_lens, uint32_t* status,
+                     void* stream) {
+  BS_CHECK(num_rows >= 0 && num_rows <= bsb::max_metadata_rows(), "num_rows must be in [0, %d]",
+           bsb::max_metadata_rows());
+  BS_CHECK(num_tokens >= 0 && num_tokens <= kInt32Max, "num_tokens out of range");
+  BS_CHECK(block_size > 0 && num_blocks > 0 && num_blocks * block_size <= kInt32Max,
+           "pool slots must fit in int32");
+  BS_CHECK(max_blocks_per_seq > 0 && max_blocks_per_seq <= table_stride,
+           "max_blocks_per_seq must be in [1, table_stride]");
+  BS_CHECK(table_rows > 0 && table_rows <= kInt32Max, "table_rows out of range");
+  if (num_rows == 0) return BS_OK;
+  BS_CHECK(start_pos && n_new && block_tables && cu_q && context_lens, "null pointer argument");
+  BS_CHECK(num_tokens == 0 || (positions && slot_mapping), "null pointer argument");
+  const int rc = bsb::launch_step_metadata(
+      seq_rows, start_pos, n_new, static_cast<int32_t>(num_rows), block_tables, table_stride,
+      static_cast<int32_t>(table_rows), static_cast<int32_t>(max_blocks_per_seq),
+      static_cast<int32_t>(block_size), static_cast<int32_t>(num_blocks),
+      static_cast<int32_t>(num_tokens), cu_q, positions, slot_mapping, context_lens, status,
+      static_cast<cudaStream_t>(stream));
+  if (rc != 0) return cuda_fail(static_cast<cudaError_t>(rc), "metadata kernel launch");
+  return BS_OK;
+}
+
+int bs_take_status(void* workspace, void* stream, uint32_t* status_out) {
+  BS_CHECK(workspace != nullptr, "workspace is null");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  uint32_t bits = 0;
+  cudaError_t e = cudaMemcpyAsync(&bits, workspace, sizeof(bits), cudaMemcpyDeviceToHost, st);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+  if (e == cudaSuccess && bits != 0) e = cudaMemsetAsync(workspace, 0, sizeof(bits), st);
+  if (e != cudaSuccess) return cuda_fail(e, "reading the status word");
+  if (status_out != nullptr) *status_out = bits;
+  if (bits == 0) return BS_OK;
+  std::string msg = "device reported:";
+  if (bits & BS_STATUS_BAD_BLOCK) msg += " block table entry out of range;";
+  if (bits & BS_STATUS_BAD_LENGTH) msg += " context length out of range;";
+  if (bits & BS_STATUS_WAIT_TIMEOUT) msg += " pipeline wait timed out;";
+  if (bits & BS_STATUS_BAD_SLOT) msg += " slot outside the pool;";
+  if (bits & BS_STATUS_BAD_ROW) msg += " sequence row outside the block tables;";
+  g_error = msg;
+  return BS_ERR_DEVICE;
+}
+
+}  // extern "C"

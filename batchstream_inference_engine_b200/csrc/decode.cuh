@@ -1,0 +1,282 @@
+// Split-K ragged decode attention: the parts shared by the tensor-core and the
+// SIMT kernels.
+//
+// Work layout ("stream-K" over KV blocks).  A *segment* is one (sequence, kv
+// head) pair; it holds nb = ceil(len / block_size) *units* (KV blocks).  Segments
+// are laid out sequence-major, kv-head minor, so unit u of the whole batch lives
+// in segment s with U(s) <= u < U(s) + nb.  The W units are cut into C equal
+// contiguous spans, one per CTA (the first W % C CTAs take one unit more), so
+// every CTA streams the same number of KV bytes whatever the length mix.  A CTA
+// that sees a whole segment writes the final output rows directly.  A segment cut
+// by span boundaries gets one partial record (unnormalised O, row max, row sum)
+// per CTA that touched it; the last of those CTAs to finish (atomic counter, no
+// waiting) merges the records and writes the output, then resets the counter to 0
+// so the workspace is ready for the next launch.
+//
+// Arithmetic follows the reference op (csrc/paged_attention.cpp:47-74 of the
+// BatchStream sources): scores are fp32 dot products, rounded to bf16, scaled,
+// rounded to bf16 again; softmax runs in fp32; the probabilities are rounded to
+// bf16 before they weight V; the weighted sum accumulates in fp32 and is cast to
+// the output dtype at the end.  The online softmax keeps everything in base 2
+// (scores multiplied by log2(e)).
+#pragma once
+
+#include "common.cuh"
+
+namespace bsb {
+
+constexpr float kLog2e = 1.4426950408889634f;
+
+struct DecodeArgs {
+  const void* q;         // [B, H, D]; heads of one sequence contiguous (stride D)
+  int64_t q_stride_seq;  // elements between sequences
+  void* out;             // [B, H, D] with the same head/dim layout
+  int64_t o_stride_seq;
+  const void* k_pool;  // [Hkv, NB, bs, D] contiguous
+  const void* v_pool;
+  const int32_t* block_tables;  // [rows, bt_stride]
+  int64_t bt_stride;
+  int32_t bt_rows;
+  const int32_t* seq_rows;  // optional [B] row of each sequence in block_tables
+  const int32_t* context_lens;  // [B]
+  int32_t num_seqs, num_heads, num_kv_heads, groups, head_dim, block_size, num_blocks,
+      max_blocks;  // max_blocks = usable entries per table row
+  float scale;
+  float* partials;  // [2 * C, rec_stride]
+  int32_t rec_stride;
+  int32_t* seg_counters;  // [B * Hkv], zero between launches
+  uint32_t* status;
+};
+
+// Units of sequence i after validation; also returns the clamped length.
+__device__ __forceinline__ int32_t seq_units(const DecodeArgs& a, int32_t i, int32_t& len,
+                                             int32_t& row, bool report) {
+  len = __ldg(a.context_lens + i);
+  row = a.seq_rows != nullptr ? __ldg(a.seq_rows + i) : i;
+  if (row < 0 || row >= a.bt_rows) {
+    if (report) set_status(a.status, kStatusBadRow);
+    len = 0;
+    return 0;
+  }
+  const int64_t cap = static_cast<int64_t>(a.max_blocks) * a.block_size;
+  if (len <= 0 || len > cap) {
+    if (report) set_status(a.status, kStatusBadLength);
+    len = 0;
+    return 0;
+  }
+  return (len + a.block_size - 1) / a.block_size;
+}
+
+struct Span {
+  int64_t W, q, rem;  // total units, units per CTA, CTAs with one extra unit
+  int64_t r0, r1;     // this CTA's unit range
+  int32_t seq;        // sequence holding unit r0
+  int64_t prefix;     // units of sequences before `seq`, for one kv head
+};
+
+__device__ __forceinline__ int64_t span_begin(int64_t c, int64_t q, int64_t rem) {
+  return c * q + (c < rem ? c : rem);
+}
+
+// CTA whose span holds unit u.
+__device__ __forceinline__ int64_t span_owner(int64_t u, int64_t q, int64_t rem) {
+  const int64_t head = (q + 1) * rem;
+  return u < head ? u / (q + 1) : rem + (u - head) / q;
+}
+
+// Record slot of CTA c for the segment starting at unit U: slot 0 is the
+// segment the span starts in, slot 1 the one it ends in.
+__device__ __forceinline__ int64_t record_index(int64_t c, int64_t U, int64_t q, int64_t rem) {
+  return c * 2 + (U <= span_begin(c, q, rem) ? 0 : 1);
+}
+
+// Block-wide exclusive scan helper storage.
+struct ScanSmem {
+  int64_t warp_tot[32];
+  int64_t total;
+  int32_t found_seq;
+  int64_t found_prefix;
+};
+
+__device__ __forceinline__ int64_t warp_inclusive_scan(int64_t v) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int64_t n = __shfl_up_sync(0xffffffffu, v, o);
+    if (lane >= o) v += n;
+  }
+  return v;
+}
+
+// All threads of the CTA call this.  Computes W and this CTA's span, and finds
+// the sequence holding the span's first unit.
+__device__ __forceinline__ Span compute_span(const DecodeArgs& a, ScanSmem& sm) {
+  const int tid = threadIdx.x, nthr = blockDim.x, lane = tid & 31, warp = tid >> 5;
+  const int nwarps = (nthr + 31) >> 5;
+  const int64_t C = gridDim.x, c = blockIdx.x;
+  const int32_t B = a.num_seqs;
+  Span sp;
+
+  // Pass 1: total units.  Only CTA 0 reports bad lengths, once.
+  int64_t local = 0;
+  for (int32_t i = tid; i < B; i += nthr) {
+    int32_t len, row;
+    local += seq_units(a, i, len, row, c == 0);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) local += __shfl_xor_sync(0xffffffffu, local, o);
+  if (lane == 0) sm.warp_tot[warp] = local;
+  if (tid == 0) sm.found_seq = -1;
+  __syncthreads();
+  if (tid == 0) {
+    int64_t t = 0;
+    for (int w = 0; w < nwarps; ++w) t += sm.warp_tot[w];
+    sm.total = t;
+  }
+  __syncthreads();
+  const int64_t Hkv = a.num_kv_heads;
+  sp.W = sm.total * Hkv;
+  sp.q = sp.W / C;
+  sp.rem = sp.W % C;
+  sp.r0 = span_begin(c, sp.q, sp.rem);
+  sp.r1 = sp.r0 + sp.q + (c < sp.rem ? 1 : 0);
+  sp.seq = -1;
+  sp.prefix = 0;
+  if (sp.r0 >= sp.r1) return sp;
+
+  // Pass 2: chunked exclusive scan until the sequence holding r0 is found.
+  int64_t carry = 0;
+  for (int32_t base = 0; base < B; base += nthr) {
+    const int32_t i = base + tid;
+    int64_t nb = 0;
+    if (i < B) {
+      int32_t len, row;
+      nb = seq_units(a, i, len, row, false);
+    }
+    int64_t incl = warp_inclusive_scan(nb);
+    __syncthreads();  // warp_tot reuse
+    if (lane == 31) sm.warp_tot[warp] = incl;
+    __syncthreads();
+    int64_t before = carry;
+    for (int w = 0; w < warp; ++w) before += sm.warp_tot[w];
+    const int64_t excl = before + incl - nb;
+    if (nb > 0 && excl * Hkv <= sp.r0 && sp.r0 < (excl + nb) * Hkv) {
+      sm.found_seq = i;
+      sm.found_prefix = excl;
+    }
+    int64_t chunk_total = 0;
+    for (int w = 0; w < nwarps; ++w) chunk_total += sm.warp_tot[w];
+    __syncthreads();
+    if (sm.found_seq >= 0) break;
+    carry += chunk_total;
+  }
+  sp.seq = sm.found_seq;
+  sp.prefix = sm.found_prefix;
+  if (sp.seq < 0) sp.r1 = sp.r0;  // cannot happen when r0 < W; never walk from nowhere
+  return sp;
+}
+
+// Describes the part of one segment that a CTA processes.
+struct Portion {
+  int32_t seq, kvh;
+  int32_t whole;          // the CTA sees every unit of the segment
+  int64_t seg_unit;       // U(s)
+  int32_t nb;             // units of the segment
+};
+
+template <typename OutT>
+__device__ __forceinline__ void store_out(OutT* p, float v);
+template <>
+__device__ __forceinline__ void store_out<__nv_bfloat16>(__nv_bfloat16* p, float v) {
+  *p = __float2bfloat16_rn(v);
+}
+template <>
+__device__ __forceinline__ void store_out<float>(float* p, float v) {
+  *p = v;
+}
+
+// Combines the NW per-warp states deposited in shared memory (sO [NW][G][D],
+// sM / sL [NW][G], maxima in base 2) and writes either the output rows or this
+// CTA's partial record; the last CTA of a cut segment merges all records.
+// Called by the NW*32 consumer threads (ctid = 0 .. NW*32-1) with barrier `bar`.
+template <int NW, typename OutT>
+__device__ void emit_portion(const DecodeArgs& a, const Span& sp, const Portion& po,
+                             const float* sO, const float* sM, const float* sL, int ctid,
+                             int32_t* s_flag, uint32_t bar) {
+  constexpr int NT = NW * 32;
+  const int G = a.groups, D = a.head_dim;
+  const int head0 = po.kvh * G;
+  OutT* out = static_cast<OutT*>(a.out) + static_cast<int64_t>(po.seq) * a.o_stride_seq +
+              static_cast<int64_t>(head0) * D;
+  float* rec = nullptr;
+  if (!po.whole) {
+    rec = a.partials + record_index(blockIdx.x, po.seg_unit, sp.q, sp.rem) * a.rec_stride;
+  }
+  for (int e = ctid; e < G * D; e += NT) {
+    const int r = e / D;
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < NW; ++w) M = fmaxf(M, sM[w * G + r]);
+    float L = 0.f, O = 0.f;
+#pragma unroll
+    for (int w = 0; w < NW; ++w) {
+      const float f = fast_exp2(sM[w * G + r] - M);
+      L += sL[w * G + r] * f;
+      O += sO[(w * G + r) * D + (e - r * D)] * f;
+    }
+    if (po.whole) {
+      store_out<OutT>(out + e, O / L);
+    } else {
+      rec[e] = O;
+      if (e - r * D == 0) {
+        rec[G * D + r] = M;
+        rec[G * D + G + r] = L;
+      }
+    }
+  }
+  if (po.whole) {
+    named_barrier_sync(bar, NT);  // shared state may be reused after this
+    return;
+  }
+  __threadfence();
+  named_barrier_sync(bar, NT);
+  const int64_t seg = static_cast<int64_t>(po.seq) * a.num_kv_heads + po.kvh;
+  const int64_t c_first = span_owner(po.seg_unit, sp.q, sp.rem);
+  const int64_t c_last = span_owner(po.seg_unit + po.nb - 1, sp.q, sp.rem);
+  if (ctid == 0) {
+    const int prev = atomicAdd(a.seg_counters + seg, 1);
+    const bool last = prev == static_cast<int>(c_last - c_first);
+    *s_flag = last ? 1 : 0;
+    if (last) atomicExch(a.seg_counters + seg, 0);
+  }
+  named_barrier_sync(bar, NT);
+  if (*s_flag) {
+    __threadfence();
+    for (int e = ctid; e < G * D; e += NT) {
+      const int r = e / D;
+      float M = -INFINITY;
+      for (int64_t cc = c_first; cc <= c_last; ++cc) {
+        const float* rr = a.partials + record_index(cc, po.seg_unit, sp.q, sp.rem) * a.rec_stride;
+        M = fmaxf(M, __ldcg(rr + G * D + r));
+      }
+      float L = 0.f, O = 0.f;
+      for (int64_t cc = c_first; cc <= c_last; ++cc) {
+        const float* rr = a.partials + record_index(cc, po.seg_unit, sp.q, sp.rem) * a.rec_stride;
+        const float f = fast_exp2(__ldcg(rr + G * D + r) - M);
+        L += __ldcg(rr + G * D + G + r) * f;
+        O += __ldcg(rr + e) * f;
+      }
+      store_out<OutT>(out + e, O / L);
+    }
+  }
+  named_barrier_sync(bar, NT);
+}
+
+// Host-side launchers (defined in decode_mma.cu / decode_simt.cu).
+int launch_decode_mma(const DecodeArgs& a, const CUtensorMap& kmap, const CUtensorMap& vmap,
+                      int grid, cudaStream_t stream);
+int decode_mma_ctas_per_sm(int head_dim, int groups);
+int launch_decode_simt(const DecodeArgs& a, int dtype_is_bf16, int grid, cudaStream_t stream);
+int decode_simt_ctas_per_sm(int head_dim, int groups, int dtype_is_bf16);
+
+}  // namespace bsb

@@ -1,0 +1,276 @@
+"""Torch-facing wrappers of the C ABI: the paged-attention path on CUDA tensors.
+
+PyTorch provides device memory, the current stream and the tensors; every
+computation runs in the sm_100a kernels of ``libbatchstream_b200.so``.  Errors
+surface as ``RuntimeError``, as the reference op raises them through
+``TORCH_CHECK`` (csrc/paged_attention.cpp:22-44).
+"""
+
+from __future__ import annotations
+
+import ctypes
+import threading
+
+import torch
+
+from . import _lib
+from ._lib import BS_BF16, BS_F32, check, i64_array, lib
+
+_DTYPES = {torch.bfloat16: BS_BF16, torch.float32: BS_F32}
+
+
+def dtype_code(dtype: torch.dtype) -> int:
+    """C-ABI dtype code; any other dtype maps to an invalid code the C side rejects."""
+    return _DTYPES.get(dtype, -1)
+
+
+def _stream_of(t: torch.Tensor) -> int:
+    if t.is_cuda:
+        return torch.cuda.current_stream(t.device).cuda_stream
+    return 0
+
+
+def _require_cuda(name: str, *tensors: torch.Tensor) -> torch.device:
+    device = None
+    for t in tensors:
+        if t is None:
+            continue
+        if not t.is_cuda:
+            raise RuntimeError(f"{name}: every tensor must be a CUDA tensor")
+        if device is None:
+            device = t.device
+        elif t.device != device:
+            raise RuntimeError(f"{name}: tensors are on different devices")
+    return device
+
+
+class _Workspaces:
+    """Zero-filled scratch buffers, one per (device, stream), grown on demand.
+
+    The kernels leave the counter region zero after every call, so a buffer is
+    zero-filled only when it is (re)allocated.
+    """
+
+    def __init__(self):
+        self._lock = threading.Lock()
+        self._buffers: dict[tuple[int, int], torch.Tensor] = {}
+
+    def get(self, device: torch.device, stream: int, nbytes: int) -> torch.Tensor:
+        key = (device.index if device.index is not None else torch.cuda.current_device(), stream)
+        with self._lock:
+            buf = self._buffers.get(key)
+            if buf is None or buf.numel() < nbytes:
+                size = max(nbytes, 1 << 20)
+                if buf is not None:
+                    size = max(size, 2 * buf.numel())
+                buf = torch.zeros(size, dtype=torch.uint8, device=device)
+                self._buffers[key] = buf
+            return buf
+
+
+_workspaces = _Workspaces()
+
+
+def workspace_for(device: torch.device, nbytes: int) -> torch.Tensor:
+    """The scratch buffer used for calls on the current stream of `device`."""
+    return _workspaces.get(device, torch.cuda.current_stream(device).cuda_stream, nbytes)
+
+
+def take_status(device: torch.device | None = None) -> int:
+    """Synchronise the current stream and raise if a kernel set a status bit.
+
+    Returns 0 when no bit was set (kernels never fault on bad tables, lengths or
+    slots; they record the problem here instead).
+    """
+    device = device or torch.device("cuda", torch.cuda.current_device())
+    stream = torch.cuda.current_stream(device).cuda_stream
+    ws = _workspaces.get(device, stream, 0)
+    bits = ctypes.c_uint32(0)
+    check(lib().bs_take_status(ws.data_ptr(), stream, ctypes.byref(bits)))
+    return bits.value
+
+
+def _shape_args(t: torch.Tensor):
+    return t.dim(), i64_array(t.shape), i64_array(t.stride())
+
+
+def paged_attention(query: torch.Tensor, keys: torch.Tensor, values: torch.Tensor,
+                    block_table: list[int], length: int, block_size: int, groups: int,
+                    scaling: float) -> torch.Tensor:
+    """Drop-in for the reference op ``paged_attention`` (csrc/paged_attention.cpp:76-105).
+
+    Same positional signature and the same malformed-input errors; runs on CUDA
+    tensors and accepts float32 when query, keys and values are all float32.
+    Returns [heads, head_dim] in the query dtype on the query's device.
+    """
+    if query.dim() == 2:
+        query = query.contiguous()  # the reference copies it too (paged_attention.cpp:81)
+    table = [int(b) for b in block_table]
+    qn, qs, qst = _shape_args(query)
+    kn, ks, kst = _shape_args(keys)
+    vn, vs, vst = _shape_args(values)
+    device = query.device
+    stream = _stream_of(query)
+    if query.dim() == 2 and query.is_cuda:
+        out = torch.empty(query.shape, dtype=query.dtype, device=device)
+    else:
+        out = torch.empty(0)
+    ws_ptr, ws_bytes = 0, 0
+    if query.is_cuda and keys.dim() == 4 and query.dim() == 2 and keys.size(0) > 0:
+        with torch.cuda.device(device):
+            need = ctypes.c_uint64(0)
+            check(lib().bs_paged_attention_workspace_bytes(
+                query.size(0), keys.size(0), query.size(1), len(table), dtype_code(query.dtype),
+                block_size, ctypes.byref(need)))
+            ws = workspace_for(device, need.value)
+            ws_ptr, ws_bytes = ws.data_ptr(), ws.numel()
+    ctx = torch.cuda.device(device) if query.is_cuda else _NullContext()
+    with ctx:
+        check(lib().bs_paged_attention(
+            query.data_ptr(), dtype_code(query.dtype), qn, qs, qst,
+            keys.data_ptr(), dtype_code(keys.dtype), kn, ks, kst,
+            values.data_ptr(), dtype_code(values.dtype), vn, vs, vst,
+            i64_array(table), len(table), int(length), int(block_size), int(groups),
+            float(scaling), out.data_ptr(), ws_ptr, ws_bytes, stream))
+    return out
+
+
+class _NullContext:
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        return False
+
+
+def paged_attention_batched(query: torch.Tensor, key_pool: torch.Tensor, value_pool: torch.Tensor,
+                            block_tables: torch.Tensor, context_lens: torch.Tensor, scaling: float,
+                            seq_rows: torch.Tensor | None = None, out: torch.Tensor | None = None,
+                            max_blocks_per_seq: int | None = None,
+                            units_hint: int = 0) -> torch.Tensor:
+    """Decode attention for a whole ragged batch in one launch.
+
+    query [B, H, D]; key_pool/value_pool [Hkv, NB, bs, D] (one layer of the
+    pool, contiguous); block_tables int32 [rows, max_blocks]; context_lens int32
+    [B]; seq_rows int32 [B] (row of each sequence in block_tables, default b).
+    Returns [B, H, D] in the query dtype.  Bad tables or lengths never fault: they
+    set a status bit that ``take_status`` raises.
+    """
+    device = _require_cuda("paged_attention_batched", query, key_pool, value_pool, block_tables,
+                           context_lens, seq_rows, out)
+    if query.dim() != 3 or key_pool.dim() != 4 or value_pool.shape != key_pool.shape:
+        raise RuntimeError("query must be [B, H, D] and the pools [Hkv, NB, bs, D]")
+    if query.dtype != key_pool.dtype or value_pool.dtype != key_pool.dtype:
+        raise RuntimeError("query and pools must share a dtype")
+    if not (key_pool.is_contiguous() and value_pool.is_contiguous()):
+        raise RuntimeError("pools must be contiguous")
+    if block_tables.dtype != torch.int32 or context_lens.dtype != torch.int32:
+        raise RuntimeError("block_tables and context_lens must be int32")
+    if seq_rows is not None and seq_rows.dtype != torch.int32:
+        raise RuntimeError("seq_rows must be int32")
+    B, H, D = query.shape
+    Hkv, NB, bs, Dk = key_pool.shape
+    if Dk != D:
+        raise RuntimeError("query and pools disagree on head_dim")
+    if context_lens.numel() < B or (seq_rows is not None and seq_rows.numel() < B):
+        raise RuntimeError("context_lens / seq_rows must hold one entry per sequence")
+    if query.stride(2) != 1 or query.stride(1) != D:
+        query = query.contiguous()
+    if block_tables.stride(1) != 1:
+        block_tables = block_tables.contiguous()
+    if out is None:
+        out = torch.empty((B, H, D), dtype=query.dtype, device=device)
+    elif out.shape != (B, H, D) or out.stride(2) != 1 or out.stride(1) != D:
+        raise RuntimeError("out must be [B, H, D] with contiguous heads")
+    mb = block_tables.size(1) if max_blocks_per_seq is None else int(max_blocks_per_seq)
+    code = dtype_code(query.dtype)
+    with torch.cuda.device(device):
+        stream = torch.cuda.current_stream(device).cuda_stream
+        need = ctypes.c_uint64(0)
+        check(lib().bs_paged_attention_batched_workspace_bytes(B, H, Hkv, D, bs, code,
+                                                               ctypes.byref(need)))
+        ws = workspace_for(device, need.value)
+        check(lib().bs_paged_attention_batched(
+            query.data_ptr(), query.stride(0), key_pool.data_ptr(), value_pool.data_ptr(),
+            block_tables.data_ptr(), block_tables.stride(0), block_tables.size(0),
+            seq_rows.data_ptr() if seq_rows is not None else None, context_lens.data_ptr(),
+            B, H, Hkv, D, bs, NB, mb, code, float(scaling), int(units_hint), out.data_ptr(),
+            out.stride(0), ws.data_ptr(), ws.numel(), stream))
+    return out
+
+
+def reshape_and_cache(key: torch.Tensor, value: torch.Tensor, key_pool: torch.Tensor,
+                      value_pool: torch.Tensor, slot_mapping: torch.Tensor) -> None:
+    """Write rows [T, Hkv, D] (or [T, Hkv*D]) into pool[h, slot // bs, slot % bs].
+
+    The batched form of PagedKVCache.append (src/server/torch_model.py:149-153);
+    an fp32 input into a bf16 pool is rounded to nearest-even.
+    """
+    device = _require_cuda("reshape_and_cache", key, value, key_pool, value_pool, slot_mapping)
+    Hkv, NB, bs, D = key_pool.shape
+    T = slot_mapping.numel()
+    if slot_mapping.dtype != torch.int32:
+        raise RuntimeError("slot_mapping must be int32")
+    if key.dtype != value.dtype or key_pool.dtype != value_pool.dtype or value_pool.shape != key_pool.shape:
+        raise RuntimeError("key/value dtypes or pool shapes disagree")
+    if not (key_pool.is_contiguous() and value_pool.is_contiguous()):
+        raise RuntimeError("pools must be contiguous")
+    k2 = key.reshape(key.size(0), -1) if key.dim() != 2 else key
+    v2 = value.reshape(value.size(0), -1) if value.dim() != 2 else value
+    if k2.size(0) < T or v2.size(0) < T or k2.size(1) != Hkv * D or v2.size(1) != Hkv * D:
+        raise RuntimeError("key/value must be [T, kv_heads, head_dim]")
+    if k2.stride(1) != 1:
+        k2 = k2.contiguous()
+    if v2.stride(1) != 1:
+        v2 = v2.contiguous()
+    ws = workspace_for(device, 0)
+    with torch.cuda.device(device):
+        stream = torch.cuda.current_stream(device).cuda_stream
+        check(lib().bs_reshape_and_cache(
+            k2.data_ptr(), v2.data_ptr(), k2.stride(0), v2.stride(0), dtype_code(key.dtype),
+            slot_mapping.data_ptr(), T, key_pool.data_ptr(), value_pool.data_ptr(),
+            dtype_code(key_pool.dtype), Hkv, NB, bs, D, ws.data_ptr(), stream))
+
+
+def step_metadata(block_tables: torch.Tensor, start_pos: torch.Tensor, n_new: torch.Tensor,
+                  num_tokens: int, block_size: int, num_blocks: int,
+                  seq_rows: torch.Tensor | None = None, max_blocks_per_seq: int | None = None):
+    """Device metadata of one step: (cu_q, positions, slot_mapping, context_lens), all int32.
+
+    Rows r hold n_new[r] new tokens after start_pos[r] cached ones; the slot of a
+    token is the reference's BlockAllocator.locate flattened to
+    block * block_size + offset (src/server/block_allocator.py:28-30).
+    """
+    device = _require_cuda("step_metadata", block_tables, start_pos, n_new, seq_rows)
+    R = start_pos.numel()
+    for name, t in (("block_tables", block_tables), ("start_pos", start_pos), ("n_new", n_new)):
+        if t.dtype != torch.int32:
+            raise RuntimeError(f"{name} must be int32")
+    if block_tables.stride(1) != 1:
+        block_tables = block_tables.contiguous()
+    cu_q = torch.empty(R + 1, dtype=torch.int32, device=device)
+    positions = torch.empty(max(num_tokens, 1), dtype=torch.int32, device=device)
+    slots = torch.empty(max(num_tokens, 1), dtype=torch.int32, device=device)
+    context = torch.empty(max(R, 1), dtype=torch.int32, device=device)
+    mb = block_tables.size(1) if max_blocks_per_seq is None else int(max_blocks_per_seq)
+    ws = workspace_for(device, 0)
+    with torch.cuda.device(device):
+        stream = torch.cuda.current_stream(device).cuda_stream
+        check(lib().bs_step_metadata(
+            seq_rows.data_ptr() if seq_rows is not None else None, start_pos.data_ptr(),
+            n_new.data_ptr(), R, block_tables.data_ptr(), block_tables.stride(0),
+            block_tables.size(0), mb, block_size, num_blocks, num_tokens, cu_q.data_ptr(),
+            positions.data_ptr(), slots.data_ptr(), context.data_ptr(), ws.data_ptr(), stream))
+    return cu_q, positions[:num_tokens], slots[:num_tokens], context[:R]
+
+
+__all__ = [
+    "paged_attention",
+    "paged_attention_batched",
+    "reshape_and_cache",
+    "step_metadata",
+    "take_status",
+    "workspace_for",
+    "dtype_code",
+    "_lib",
+]

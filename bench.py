@@ -1,0 +1,504 @@
+"""Benchmark of the paged-attention decode path (one JSON line on rank 0).
+
+Workload (default ``decode_d64``): the large ragged decode sweep — per GPU a batch
+of 256 sequences with context lengths log-normal (median 1024, sigma 1.0)
+clipped to [16, 32768], bf16 KV, block size 16, one attention layer, 14 query /
+2 kv heads, head_dim 64 (``decode_d128``: 28 / 4 heads, head_dim 128).  Block
+tables are random over a pool sized to 60% of the GPU's memory.  With N GPUs,
+256 * N sequences are drawn and split across ranks by a greedy
+longest-first partition into shards with equal KV tokens (weak scaling: per-GPU
+work is fixed).
+
+One step = one decode step of one layer for the whole batch: device metadata
+(positions, slots, context lengths) -> slot write of the step's new K/V token
+-> split-K batched decode attention.  `value` is decode algorithmic bytes
+(K/V of every context token + q + out + tables + lengths) per second over the
+whole step, max over ranks.  Four batches with disjoint random tables rotate so
+consecutive steps read different KV blocks (888 MB footprint > 126 MB L2).
+
+``--impl reference`` times the reference's own C++ op (built from its sources
+into oracle/_ref) on the host cores on a bounded sample of the same workload.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import threading
+import time
+from concurrent.futures import ThreadPoolExecutor
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+WORKLOADS = {
+    "decode_d64": dict(heads=14, kv_heads=2, head_dim=64),
+    "decode_d128": dict(heads=28, kv_heads=4, head_dim=128),
+}
+SEQS_PER_GPU = 256
+BLOCK = 16
+ROTATIONS = 4
+POOL_FRACTION = 0.6
+
+
+def parse_args():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=50)
+    p.add_argument("--warmup", type=int, default=5)
+    p.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    p.add_argument("--workload", choices=sorted(WORKLOADS), default="decode_d64")
+    p.add_argument("--cpu-seconds", type=float, default=10.0,
+                   help="CPU work per CPU-baseline measurement")
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--pool-gb", type=float, default=0.0,
+                   help="pool size per GPU in GB (default: 60%% of device memory)")
+    return p.parse_args()
+
+
+# ------------------------------------------------------------------ workload
+
+
+def lengths_all(n_gpus: int) -> np.ndarray:
+    rng = np.random.default_rng(0)
+    lens = rng.lognormal(math.log(1024.0), 1.0, SEQS_PER_GPU * n_gpus)
+    return np.clip(np.rint(lens), 16, 32768).astype(np.int64)
+
+
+def shard(lens: np.ndarray, n: int, rank: int) -> np.ndarray:
+    """Longest-first greedy partition into n shards with equal KV tokens."""
+    order = np.argsort(-lens, kind="stable")
+    loads = np.zeros(n, dtype=np.int64)
+    counts = np.zeros(n, dtype=np.int64)
+    owner = np.empty(len(lens), dtype=np.int64)
+    cap = math.ceil(len(lens) / n)
+    for i in order:
+        cand = [r for r in range(n) if counts[r] < cap]
+        r = min(cand, key=lambda x: (loads[x], x))
+        owner[i] = r
+        loads[r] += lens[i]
+        counts[r] += 1
+    return lens[owner == rank]
+
+
+def algorithmic_bytes(lens, heads, kv_heads, head_dim) -> int:
+    """K/V of every context token + q + out (bf16) + table entries + lengths."""
+    blocks = sum(-(-int(n) // BLOCK) for n in lens)
+    kv = 2 * kv_heads * int(np.sum(lens)) * head_dim * 2
+    return kv + len(lens) * heads * head_dim * (2 + 2) + blocks * 4 + len(lens) * 4
+
+
+# ------------------------------------------------------------------ clocks
+
+
+class ClockSampler:
+    """nvidia-smi clock/throttle samples every 200 ms while the timed loop runs."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = Path(tempfile.mkstemp(prefix="clocks_", suffix=".csv")[1])
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=self.path.open("w"), stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+        return False
+
+    def summary(self) -> dict:
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        try:
+            lines = self.path.read_text().strip().splitlines()
+        except OSError:
+            lines = []
+        for line in lines:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx.append(float(parts[2]))
+            except ValueError:
+                continue
+            for name, flag in zip(names, parts[5:9]):
+                if flag.lower() == "active":
+                    reasons.add(name)
+        self.path.unlink(missing_ok=True)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx),
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ------------------------------------------------------------------ CPU baseline
+
+
+def cpu_sample_inputs(lens, heads, kv_heads, head_dim, count, seed=7):
+    """Host copies of a few sequences of the workload (compact pools, own tables)."""
+    import torch
+
+    rng = np.random.default_rng(seed)
+    pick = rng.choice(len(lens), size=min(count, len(lens)), replace=False)
+    cases = []
+    g = torch.Generator().manual_seed(seed)
+    for i in pick:
+        n = int(lens[i])
+        nb = -(-n // BLOCK)
+        perm = torch.randperm(nb, generator=g).tolist()
+        k = torch.randn(kv_heads, nb, BLOCK, head_dim, generator=g).bfloat16()
+        v = torch.randn(kv_heads, nb, BLOCK, head_dim, generator=g).bfloat16()
+        q = torch.randn(heads, head_dim, generator=g).bfloat16()
+        cases.append((q, k, v, perm, n))
+    return cases
+
+
+def time_cpu(lens, heads, kv_heads, head_dim, seconds):
+    """Times the reference C++ op (oracle/_ref) or, if absent, the oracle port,
+    called per sequence as the reference calls it, on all host cores (the op
+    releases the GIL, so a thread per core runs calls in parallel)."""
+    import torch
+
+    import oracle
+
+    op = oracle.load_reference_op()
+    kind = "reference" if op is not None else "port"
+    cores = os.cpu_count() or 1
+    torch.set_num_threads(1)  # the parallelism is across calls, one per core
+    cases = cpu_sample_inputs(lens, heads, kv_heads, head_dim, count=64)
+    groups = heads // kv_heads
+
+    if op is not None:
+        def run(case):
+            q, k, v, table, n = case
+            op(q, k, v, table, n, BLOCK, groups, head_dim ** -0.5)
+    else:
+        prepared = [(q.view(torch.int16).numpy().view(np.uint16),
+                     k.view(torch.int16).numpy().view(np.uint16),
+                     v.view(torch.int16).numpy().view(np.uint16), t, n)
+                    for q, k, v, t, n in cases]
+
+        def run(case_index):
+            q, k, v, t, n = prepared[case_index]
+            oracle.decode(q, k, v, t, n, BLOCK, groups, head_dim ** -0.5)
+
+    items = cases if op is not None else list(range(len(cases)))
+    nbytes = [algorithmic_bytes([c[4]], heads, kv_heads, head_dim) for c in cases]
+    with ThreadPoolExecutor(max_workers=cores) as pool:
+        list(pool.map(run, items[: min(len(items), cores)]))  # warm-up
+        done_bytes, calls = 0, 0
+        start = time.perf_counter()
+        while time.perf_counter() - start < seconds:
+            list(pool.map(run, items))
+            done_bytes += sum(nbytes)
+            calls += len(items)
+        elapsed = time.perf_counter() - start
+    gbs = done_bytes / elapsed / 1e9
+    sample = (f"{len(cases)} sequences of the workload (lengths {min(c[4] for c in cases)}-"
+              f"{max(c[4] for c in cases)}), {calls} per-sequence op calls over "
+              f"{elapsed:.1f} s, {cores} threads")
+    return {"value": round(gbs, 3), "unit": "GB/s", "cores": cores, "kind": kind,
+            "sample": sample}
+
+
+# ------------------------------------------------------------------ GPU arm
+
+
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+
+    from batchstream_inference_engine_b200 import ops
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120),
+                                device_id=dev)
+    w = WORKLOADS[args.workload]
+    H, Hkv, D = w["heads"], w["kv_heads"], w["head_dim"]
+    all_lens = lengths_all(world)
+    lens = shard(all_lens, world, rank)
+    B = len(lens)
+    blocks = [-(-int(n) // BLOCK) for n in lens]
+    width = max(blocks)
+
+    free, total = torch.cuda.mem_get_info(dev)
+    block_bytes = 2 * Hkv * BLOCK * D * 2
+    nb = int(POOL_FRACTION * total // block_bytes)
+    if args.pool_gb > 0:
+        nb = int(args.pool_gb * 1e9 // block_bytes)
+    nb = min(nb, int(0.9 * free // block_bytes), (2**31 - 1) // (Hkv * BLOCK))
+    k_pool = torch.empty((Hkv, nb, BLOCK, D), dtype=torch.bfloat16, device=dev)
+    v_pool = torch.empty_like(k_pool)
+    gen = torch.Generator(device=dev).manual_seed(1234 + rank)
+    k_pool.normal_(generator=gen)
+    v_pool.normal_(generator=gen)
+
+    # ROTATIONS batches with disjoint random tables over the pool.
+    need = sum(blocks)
+    perm = torch.randperm(nb, device=dev, generator=gen)[: need * ROTATIONS].to(torch.int32)
+    tables = []
+    for r in range(ROTATIONS):
+        bt = torch.full((B, width), -1, dtype=torch.int32, device=dev)
+        cur = r * need
+        for i, m in enumerate(blocks):
+            bt[i, :m] = perm[cur: cur + m]
+            cur += m
+        tables.append(bt)
+    q = torch.randn((ROTATIONS, B, H, D), generator=gen, device=dev).bfloat16()
+    k_new = torch.randn((ROTATIONS, B, Hkv, D), generator=gen, device=dev).bfloat16()
+    v_new = torch.randn((ROTATIONS, B, Hkv, D), generator=gen, device=dev).bfloat16()
+    start_pos = torch.tensor(lens - 1, dtype=torch.int32, device=dev)
+    n_new = torch.ones(B, dtype=torch.int32, device=dev)
+    out = torch.empty((B, H, D), dtype=torch.bfloat16, device=dev)
+    units = Hkv * sum(blocks)
+    scale = D ** -0.5
+
+    def step(r):
+        _, _, slots, ctx = ops.step_metadata(tables[r], start_pos, n_new, B, BLOCK, nb)
+        ops.reshape_and_cache(k_new[r], v_new[r], k_pool, v_pool, slots)
+        return ctx, slots
+
+    stream = torch.cuda.current_stream(dev)
+    for i in range(args.warmup):
+        ctx, _ = step(i % ROTATIONS)
+        ops.paged_attention_batched(q[i % ROTATIONS], k_pool, v_pool, tables[i % ROTATIONS], ctx,
+                                    scale, out=out, units_hint=units)
+    ops.take_status(dev)
+
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    mids = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    with ClockSampler(local) as clocks:
+        t0 = torch.cuda.Event(enable_timing=True)
+        t1 = torch.cuda.Event(enable_timing=True)
+        t0.record(stream)
+        for i in range(args.steps):
+            r = i % ROTATIONS
+            starts[i].record(stream)
+            ctx, _ = step(r)
+            mids[i].record(stream)
+            ops.paged_attention_batched(q[r], k_pool, v_pool, tables[r], ctx, scale, out=out,
+                                        units_hint=units)
+            ends[i].record(stream)
+        t1.record(stream)
+        torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+    ops.take_status(dev)
+    total_ms = t0.elapsed_time(t1)
+    decode_ms = [m.elapsed_time(e) for m, e in zip(mids, ends)]
+    step_bytes = algorithmic_bytes(lens, H, Hkv, D)
+
+    # End to end through the public API from pinned host buffers: every step
+    # ships q, the new K/V rows, the lengths and one table entry per sequence
+    # to the device and reads the attention output back.
+    hq = q[0].cpu().pin_memory()
+    hk = k_new[0].cpu().pin_memory()
+    hv = v_new[0].cpu().pin_memory()
+    hstart = start_pos.cpu().pin_memory()
+    hdelta = torch.stack([torch.arange(B, dtype=torch.int64) * width,
+                          torch.tensor([b - 1 for b in blocks], dtype=torch.int64)]).pin_memory()
+    hout = torch.empty((B, H, D), dtype=torch.bfloat16).pin_memory()
+    dq, dk, dv = torch.empty_like(q[0]), torch.empty_like(k_new[0]), torch.empty_like(v_new[0])
+    dstart = torch.empty_like(start_pos)
+    ddelta = torch.empty((2, B), dtype=torch.int64, device=dev)
+    e2e_table = tables[0].clone()
+    last_col = torch.tensor([b - 1 for b in blocks], device=dev)
+    last_entry = e2e_table[torch.arange(B, device=dev), last_col].to(torch.int64)
+    h2d = sum(t.numel() * t.element_size() for t in (hq, hk, hv, hstart, hdelta))
+    d2h = hout.numel() * hout.element_size()
+
+    def e2e_step():
+        dq.copy_(hq, non_blocking=True)
+        dk.copy_(hk, non_blocking=True)
+        dv.copy_(hv, non_blocking=True)
+        dstart.copy_(hstart, non_blocking=True)
+        ddelta.copy_(hdelta, non_blocking=True)
+        flat = e2e_table.view(-1)
+        flat.index_copy_(0, ddelta[0] + ddelta[1], last_entry.to(torch.int32))
+        _, _, slots, ctx = ops.step_metadata(e2e_table, dstart, n_new, B, BLOCK, nb)
+        ops.reshape_and_cache(dk, dv, k_pool, v_pool, slots)
+        ops.paged_attention_batched(dq, k_pool, v_pool, e2e_table, ctx, scale, out=out,
+                                    units_hint=units)
+        hout.copy_(out, non_blocking=True)
+
+    for _ in range(args.warmup):
+        e2e_step()
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+    a0 = torch.cuda.Event(enable_timing=True)
+    a1 = torch.cuda.Event(enable_timing=True)
+    a0.record(stream)
+    for _ in range(args.steps):
+        e2e_step()
+    a1.record(stream)
+    torch.cuda.synchronize(dev)
+    e2e_ms = a0.elapsed_time(a1)
+    ops.take_status(dev)
+
+    times = torch.tensor([total_ms, e2e_ms, statistics.mean(decode_ms), float(step_bytes)],
+                         dtype=torch.float64, device=dev)
+    if world > 1:
+        mx = times.clone()
+        dist.all_reduce(mx, op=dist.ReduceOp.MAX)
+        bytes_all = times[3:4].clone()
+        dist.all_reduce(bytes_all, op=dist.ReduceOp.SUM)
+        total_ms, e2e_ms, decode_avg_ms = mx[0].item(), mx[1].item(), mx[2].item()
+        job_bytes = bytes_all.item()
+    else:
+        decode_avg_ms = times[2].item()
+        job_bytes = float(step_bytes)
+
+    result = None
+    if rank == 0:
+        peaks = {}
+        try:
+            peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text())
+        except (OSError, ValueError):
+            pass
+        peak = peaks.get("hbm_gbs")
+        peak_note = "measured" if peak else "fallback"
+        peak = peak or 6650.0
+        value = job_bytes * args.steps / (total_ms / 1e3) / 1e9
+        achieved = step_bytes / (decode_avg_ms / 1e3) / 1e9
+        e2e_value = job_bytes * args.steps / (e2e_ms / 1e3) / 1e9
+        clock = clocks.summary()
+        result = {
+            "metric": "decode paged-attn HBM GB/s",
+            "value": round(value, 1),
+            "unit": "GB/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": round(total_ms / args.steps, 4),
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "bf16",
+            "data": "synthetic (seeded lognormal lengths, N(0,1) K/V/q, random block tables)",
+            "config": {
+                "workload": f"{args.workload}: ragged decode, {SEQS_PER_GPU} seqs/GPU, lognormal "
+                            f"(median 1024, sigma 1) lengths clipped to [16, 32768], "
+                            f"{H}q/{Hkv}kv d{D}, block 16, one layer",
+                "num_seqs_per_gpu": B,
+                "kv_tokens_rank0": int(np.sum(lens)),
+                "pool_blocks": nb,
+                "l2": f"inputs larger than L2: {ROTATIONS} rotating batches with disjoint tables, "
+                      f"{ROTATIONS * step_bytes / 1e6:.0f} MB per GPU",
+                "step": "step metadata + K/V slot write + split-K decode",
+                "parallelism": f"dp{world} replicas, no collective on the path",
+            },
+            "roofline": {
+                "bound": "hbm",
+                "kernel": "decode_mma_kernel (split-K decode)",
+                "achieved": round(achieved, 1),
+                "peak": peak,
+                "peak_source": f"{peak_note} (MEASURED_PEAKS.json hbm_gbs)" if peak_note == "measured"
+                else "fallback 6650 GB/s",
+                "unit": "GB/s",
+                "frac": round(achieved / peak, 4),
+                "traffic": None,
+                "decode_ms": round(decode_avg_ms, 4),
+                "algorithmic_bytes_per_launch": step_bytes,
+            },
+            "e2e": {"value": round(e2e_value, 1), "unit": "GB/s", "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms / args.steps, 4),
+                    "path": "pinned host -> device, metadata + slot write + decode, "
+                            "device -> pinned host"},
+            "gpu_launches": 3 * args.steps,
+            "clocks": clock,
+        }
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0 and not args.no_cpu_baseline and world == 1:
+        result["cpu_baseline"] = time_cpu(all_lens, H, Hkv, D, args.cpu_seconds)
+    if rank == 0:
+        print(json.dumps(result), flush=True)
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    w = WORKLOADS[args.workload]
+    H, Hkv, D = w["heads"], w["kv_heads"], w["head_dim"]
+    lens = lengths_all(1)
+    # Each step is a bounded sample of the workload (64 of its sequences, about
+    # a quarter of its KV bytes), so the whole run stays within minutes.
+    per_step = max(1.0, min(args.cpu_seconds, 6.0) / 2)
+    vals = []
+    base = None
+    for i in range(args.warmup + args.steps):
+        res = time_cpu(lens, H, Hkv, D, per_step if i >= args.warmup else 0.2)
+        if i >= args.warmup:
+            vals.append(res["value"])
+            base = res
+    value = statistics.median(vals)
+    base["value"] = value
+    print(json.dumps({
+        "metric": "decode paged-attn HBM GB/s",
+        "impl": "reference",
+        "value": value,
+        "unit": "GB/s",
+        "n_gpus": args.gpus,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic (seeded lognormal lengths, N(0,1) K/V/q)",
+        "config": {"workload": f"{args.workload}: reference C++ op per sequence on host cores"},
+        "cpu_baseline": base,
+        "e2e": {"value": value, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
+def main():
+    args = parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,153 @@
+/*
+ * batchstream_b200 — C ABI of the B200 paged-attention path of the BatchStream
+ * inference engine.
+ *
+ * Every entry point takes plain device pointers, sizes and a cudaStream_t passed
+ * as `void*`, returns BS_OK (0) or an error code, and never throws.  On error,
+ * bs_last_error() returns a message for the calling thread; a binding raises it
+ * as the reference's RuntimeError.  Nothing here allocates device memory: a call
+ * that needs scratch space takes a caller-provided `workspace` whose size comes
+ * from the matching *_workspace_bytes() query, zero-filled once when it is
+ * first allocated (the kernels leave it zero-filled again after every call).
+ * One workspace serves one call at a time.
+ *
+ * Layouts (row-major, elements):
+ *   query     [num_seqs, num_heads, head_dim], heads of a sequence contiguous
+ *   key/value pool of one layer [num_kv_heads, num_blocks, block_size, head_dim],
+ *             contiguous — the reference's PagedKVPool layer view
+ *             (src/server/torch_model.py:120-122)
+ *   block tables  int32 [rows, table_stride]; context lengths int32 [num_seqs]
+ *
+ * Device-side problems (a table entry out of range, a bad length or slot) never
+ * fault: the kernels skip the access and set a bit in the status word at byte 0 of
+ * the workspace; bs_take_status() reads and clears it.
+ */
+#ifndef BATCHSTREAM_B200_H_
+#define BATCHSTREAM_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum bs_dtype { BS_BF16 = 0, BS_F32 = 1 };
+
+enum bs_error {
+  BS_OK = 0,
+  BS_ERR_INVALID = 1,     /* malformed input: the reference's TORCH_CHECK cases */
+  BS_ERR_UNSUPPORTED = 2, /* valid but outside this library's limits */
+  BS_ERR_CUDA = 3,        /* a CUDA runtime call failed */
+  BS_ERR_WORKSPACE = 4,   /* workspace missing or too small */
+  BS_ERR_DEVICE = 5       /* a kernel reported a status bit (bs_take_status) */
+};
+
+/* Status bits reported by kernels (see bs_take_status). */
+#define BS_STATUS_BAD_BLOCK 0x1u
+#define BS_STATUS_BAD_LENGTH 0x2u
+#define BS_STATUS_WAIT_TIMEOUT 0x4u
+#define BS_STATUS_BAD_SLOT 0x8u
+#define BS_STATUS_BAD_ROW 0x10u
+
+/* Message of the last failing call on this thread ("" if none). */
+const char* bs_last_error(void);
+
+/* Library version string. */
+const char* bs_version(void);
+
+/*
+ * Single-sequence decode attention, the drop-in for the reference op
+ *   paged_attention(query, keys, values, block_table, length, block_size,
+ *                   groups, scaling) -> Tensor[heads, head_dim]
+ * (csrc/paged_attention.cpp:76-105, bound at :109-111; Python twin
+ * src/server/torch_model.py:67-80).  Shapes and strides are passed so that the
+ * same sixteen input checks run here (paged_attention.cpp:22-44); the query must
+ * already be contiguous (the reference copies it, paged_attention.cpp:81).
+ * Unlike the reference, float32 is accepted when query, keys and values are all
+ * float32.  `block_table` is host memory (the reference's list[int]); the table
+ * is validated on the host and staged through the workspace.  `output` is
+ * [heads, head_dim] contiguous in the query dtype.
+ */
+int bs_paged_attention(const void* query, int32_t query_dtype, int32_t query_ndim,
+                       const int64_t* query_shape, const int64_t* query_strides,
+                       const void* keys, int32_t keys_dtype, int32_t keys_ndim,
+                       const int64_t* keys_shape, const int64_t* keys_strides,
+                       const void* values, int32_t values_dtype, int32_t values_ndim,
+                       const int64_t* values_shape, const int64_t* values_strides,
+                       const int64_t* block_table, int64_t block_table_len, int64_t length,
+                       int64_t block_size, int64_t groups, double scaling, void* output,
+                       void* workspace, uint64_t workspace_bytes, void* stream);
+
+/* Workspace bytes bs_paged_attention needs for this shape (current device). */
+int bs_paged_attention_workspace_bytes(int64_t num_heads, int64_t num_kv_heads, int64_t head_dim,
+                                       int64_t block_table_len, int32_t dtype,
+                                       int64_t block_size, uint64_t* bytes_out);
+
+/*
+ * Batched ragged decode attention: one new token per sequence, all sequences of
+ * a step in one launch.  Replaces the per-sequence loop of op calls in
+ * TorchModel._attention (src/server/torch_model.py:268-270 -> PagedKVCache.attend
+ * :155-164).  Sequence b attends over context_lens[b] tokens whose blocks are
+ * block_tables[seq_rows ? seq_rows[b] : b][0 .. ceil(len / block_size)).
+ * `units_hint` is the total number of (kv head, block) pairs of the batch if the
+ * caller knows it, else 0; it only sizes the grid.
+ */
+int bs_paged_attention_batched(const void* query, int64_t query_seq_stride, const void* key_pool,
+                               const void* value_pool, const int32_t* block_tables,
+                               int64_t table_stride, int64_t table_rows, const int32_t* seq_rows,
+                               const int32_t* context_lens, int64_t num_seqs, int64_t num_heads,
+                               int64_t num_kv_heads, int64_t head_dim, int64_t block_size,
+                               int64_t num_blocks, int64_t max_blocks_per_seq, int32_t dtype,
+                               double scaling, int64_t units_hint, void* output,
+                               int64_t output_seq_stride, void* workspace,
+                               uint64_t workspace_bytes, void* stream);
+
+int bs_paged_attention_batched_workspace_bytes(int64_t num_seqs, int64_t num_heads,
+                                               int64_t num_kv_heads, int64_t head_dim,
+                                               int64_t block_size, int32_t dtype,
+                                               uint64_t* bytes_out);
+
+/*
+ * K/V slot write: key/value rows [num_tokens, num_kv_heads, head_dim] (token
+ * stride in elements, heads contiguous) go to pool[h, slot / bs, slot % bs, :].
+ * Replaces PagedKVCache.append's per-token indexed stores
+ * (src/server/torch_model.py:149-153 with BlockAllocator.locate,
+ * src/server/block_allocator.py:28-30).  A negative slot is skipped.  `status`
+ * is a device uint32 word (may be NULL) that gets BS_STATUS_BAD_SLOT for a slot
+ * beyond the pool.
+ */
+int bs_reshape_and_cache(const void* key, const void* value, int64_t key_token_stride,
+                         int64_t value_token_stride, int32_t input_dtype,
+                         const int32_t* slot_mapping, int64_t num_tokens, void* key_pool,
+                         void* value_pool, int32_t pool_dtype, int64_t num_kv_heads,
+                         int64_t num_blocks, int64_t block_size, int64_t head_dim,
+                         uint32_t* status, void* stream);
+
+/*
+ * Step metadata on the device for a ragged batch of `num_rows` rows with
+ * n_new[r] new tokens after start_pos[r] cached ones (the reference builds these
+ * on the host in TorchModel._hidden_states, src/server/torch_model.py:231-241,
+ * and per token through BlockAllocator.locate).  Writes cu_q[num_rows + 1],
+ * positions[num_tokens], slot_mapping[num_tokens] and
+ * context_lens[num_rows] = start_pos + n_new.  num_tokens = sum(n_new).
+ */
+int bs_step_metadata(const int32_t* seq_rows, const int32_t* start_pos, const int32_t* n_new,
+                     int64_t num_rows, const int32_t* block_tables, int64_t table_stride,
+                     int64_t table_rows, int64_t max_blocks_per_seq, int64_t block_size,
+                     int64_t num_blocks, int64_t num_tokens, int32_t* cu_q, int32_t* positions,
+                     int32_t* slot_mapping, int32_t* context_lens, uint32_t* status,
+                     void* stream);
+
+/*
+ * Waits for `stream`, then reads and clears the status word at the start of a
+ * workspace.  Returns BS_ERR_DEVICE (with a message naming the bits) when any
+ * bit was set, BS_OK otherwise; *status_out gets the bits.
+ */
+int bs_take_status(void* workspace, void* stream, uint32_t* status_out);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* BATCHSTREAM_B200_H_ */
