@@ -121,15 +121,22 @@ int32_t record_stride(int64_t groups, int64_t head_dim) {
   return static_cast<int32_t>(round_up(groups * head_dim + 2 * groups, 4));
 }
 
-// Workspace layout: [status 256 B][counters][staging ints][partial records].
+// Workspace layout: [status 256 B][segment counters, fixed capacity][staging
+// ints][partial records].  The counter region has the same offset and size for
+// every call, whatever its batch, so no call's staging or records ever land on
+// another call's counters: the kernels leave every counter at zero, and a
+// workspace that was zero-filled once stays valid for any sequence of calls.
+constexpr int64_t kMaxSegments = 1 << 16;
+
 struct WsLayout {
   int64_t counters, staging, partials, total;
 };
 
 WsLayout ws_layout(int64_t segments, int64_t staging_ints, int64_t grid, int64_t rec_stride) {
+  (void)segments;  // bounded by kMaxSegments, checked by the callers
   WsLayout w;
   w.counters = 256;
-  w.staging = w.counters + round_up(segments * 4, 256);
+  w.staging = w.counters + kMaxSegments * 4;
   w.partials = w.staging + round_up(staging_ints * 4, 256);
   w.total = w.partials + round_up(2 * grid * rec_stride * 4, 256);
   return w;
@@ -288,7 +295,7 @@ int bs_paged_attention(const void* query, int32_t query_dtype, int32_t query_ndi
   const int64_t heads = query_shape[0], head_dim = query_shape[1], kv_heads = keys_shape[0];
   BS_CHECK(is_contiguous(2, query_shape, query_strides),
            "query must be contiguous (the binding copies it first)");
-  if (head_dim > kMaxHeadDim || groups > kMaxGroups) {
+  if (head_dim > kMaxHeadDim || groups > kMaxGroups || kv_heads > kMaxSegments) {
     return fail(BS_ERR_UNSUPPORTED, "head_dim <= %lld and groups <= %lld are supported",
                 static_cast<long long>(kMaxHeadDim), static_cast<long long>(kMaxGroups));
   }
@@ -402,6 +409,10 @@ int bs_paged_attention_batched(const void* query, int64_t query_seq_stride, cons
   if (num_kv_heads * num_blocks * block_size > kInt32Max ||
       max_blocks_per_seq * block_size > kInt32Max || num_seqs > kInt32Max) {
     return fail(BS_ERR_UNSUPPORTED, "pool or table larger than 2^31 rows");
+  }
+  if (num_seqs * num_kv_heads > kMaxSegments) {
+    return fail(BS_ERR_UNSUPPORTED, "num_seqs * num_kv_heads must be at most %lld",
+                static_cast<long long>(kMaxSegments));
   }
   if (num_seqs == 0) return BS_OK;
   BS_CHECK(query && key_pool && value_pool && block_tables && context_lens && output,

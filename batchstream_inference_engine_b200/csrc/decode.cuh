@@ -48,6 +48,20 @@ struct DecodeArgs {
   uint32_t* status;
 };
 
+// Units of a sequence from its raw length and table row (already loaded);
+// invalid ones count as 0 units with len = 0.
+__device__ __forceinline__ int32_t units_of(const DecodeArgs& a, int32_t raw_len, int32_t raw_row,
+                                            int32_t& len, int32_t& row) {
+  len = raw_len;
+  row = raw_row;
+  const int64_t cap = static_cast<int64_t>(a.max_blocks) * a.block_size;
+  if (row < 0 || row >= a.bt_rows || len <= 0 || len > cap) {
+    len = 0;
+    return 0;
+  }
+  return (len + a.block_size - 1) / a.block_size;
+}
+
 // Units of sequence i after validation; also returns the clamped length.
 __device__ __forceinline__ int32_t seq_units(const DecodeArgs& a, int32_t i, int32_t& len,
                                              int32_t& row, bool report) {
@@ -270,6 +284,173 @@ __device__ void emit_portion(const DecodeArgs& a, const Span& sp, const Portion&
     }
   }
   named_barrier_sync(bar, NT);
+}
+
+// ------------------------------------------------------------------ warp spans
+
+// Sequence (and units before it, per kv head) holding each of NW target units.
+struct WarpStarts {
+  int32_t seq[8];
+  int64_t prefix[8];
+};
+
+// Like compute_span, then splits the CTA span into NW contiguous warp spans and
+// locates the sequence holding each warp's first unit.  All threads call it.
+template <int NW>
+__device__ __forceinline__ Span compute_warp_spans(const DecodeArgs& a, ScanSmem& sm,
+                                                   WarpStarts& ws) {
+  static_assert(NW <= 8, "at most 8 warp spans");
+  Span sp = compute_span(a, sm);
+  const int tid = threadIdx.x, nthr = blockDim.x, lane = tid & 31, warp = tid >> 5;
+  const int nwarps = (nthr + 31) >> 5;
+  const int32_t B = a.num_seqs;
+  const int64_t Hkv = a.num_kv_heads;
+  if (tid < NW) ws.seq[tid] = -1;
+  __syncthreads();
+  if (sp.r0 >= sp.r1) return sp;
+  int64_t carry = 0;
+  for (int32_t base = 0; base < B; base += nthr) {
+    const int32_t i = base + tid;
+    int64_t nb = 0;
+    if (i < B) {
+      int32_t len, row;
+      nb = seq_units(a, i, len, row, false);
+    }
+    int64_t incl = warp_inclusive_scan(nb);
+    __syncthreads();
+    if (lane == 31) sm.warp_tot[warp] = incl;
+    __syncthreads();
+    int64_t before = carry;
+    for (int w = 0; w < warp; ++w) before += sm.warp_tot[w];
+    const int64_t excl = before + incl - nb;
+    if (nb > 0) {
+#pragma unroll
+      for (int k = 0; k < NW; ++k) {
+        const int64_t target = sp.r0 + (sp.r1 - sp.r0) * k / NW;
+        if (excl * Hkv <= target && target < (excl + nb) * Hkv) {
+          ws.seq[k] = i;
+          ws.prefix[k] = excl;
+        }
+      }
+    }
+    int64_t chunk_total = 0;
+    for (int w = 0; w < nwarps; ++w) chunk_total += sm.warp_tot[w];
+    carry += chunk_total;
+    __syncthreads();
+    // The last target is the largest; once it is found every target is.
+    const int64_t last_target = sp.r0 + (sp.r1 - sp.r0) * (NW - 1) / NW;
+    if (carry * Hkv > last_target) break;
+  }
+  return sp;
+}
+
+// First half of the cross-CTA merge of a cut segment, done by one warp: writes
+// this CTA's record (O unnormalised, M, L for the G rows; o/m/l in shared memory,
+// O row-major [G][D]) and counts the CTA in.  Returns true (on every lane) when
+// this CTA was the last contributor, which then owes the segment's final merge.
+__device__ __forceinline__ bool warp_write_record(const DecodeArgs& a, const Span& sp,
+                                                  int32_t seq, int32_t kvh, int64_t seg_unit,
+                                                  int32_t nb, const float* o, const float* m,
+                                                  const float* l, int lane) {
+  const int G = a.groups, D = a.head_dim;
+  float* rec = a.partials + record_index(blockIdx.x, seg_unit, sp.q, sp.rem) * a.rec_stride;
+  for (int e = lane; e < G * D; e += 32) rec[e] = o[e];
+  for (int r = lane; r < G; r += 32) {
+    rec[G * D + r] = m[r];
+    rec[G * D + G + r] = l[r];
+  }
+  __threadfence();
+  __syncwarp();
+  const int64_t segi = static_cast<int64_t>(seq) * a.num_kv_heads + kvh;
+  const int64_t c_first = span_owner(seg_unit, sp.q, sp.rem);
+  const int64_t c_last = span_owner(seg_unit + nb - 1, sp.q, sp.rem);
+  int last = 0;
+  if (lane == 0) {
+    const int prev = atomicAdd(a.seg_counters + segi, 1);
+    last = prev == static_cast<int>(c_last - c_first);
+    if (last) atomicExch(a.seg_counters + segi, 0);
+  }
+  return __shfl_sync(0xffffffffu, last, 0) != 0;
+}
+
+// Second half: every thread of the CTA merges the n = c_last - c_first + 1
+// records of a segment and writes its output rows.  `scratch` is shared memory
+// for 2 * n * G + 2 * G floats.  Row weights are computed once per record, then
+// the O rows stream in as float4 loads that do not depend on one another.
+// Must be called by all threads of the CTA (it synchronises them).
+template <typename OutT>
+__device__ void cta_merge_records(const DecodeArgs& a, const Span& sp, int32_t seq, int32_t kvh,
+                                  int64_t seg_unit, int32_t nb, float* scratch) {
+  const int G = a.groups, D = a.head_dim;
+  const int tid = threadIdx.x, nthr = blockDim.x;
+  const int64_t c_first = span_owner(seg_unit, sp.q, sp.rem);
+  const int n = static_cast<int>(span_owner(seg_unit + nb - 1, sp.q, sp.rem) - c_first + 1);
+  float* wm = scratch;          // [n][G]: record maxima, then weights
+  float* wl = scratch + n * G;  // [n][G]: record sums
+  float* rowM = wl + n * G;     // [G]
+  float* rowInvL = rowM + G;    // [G]
+  for (int idx = tid; idx < n * G; idx += nthr) {
+    const int c = idx / G, r = idx - c * G;
+    const float* rr =
+        a.partials + record_index(c_first + c, seg_unit, sp.q, sp.rem) * a.rec_stride;
+    wm[idx] = __ldcg(rr + G * D + r);
+    wl[idx] = __ldcg(rr + G * D + G + r);
+  }
+  __syncthreads();
+  if (tid < G) {
+    float M = -INFINITY;
+    for (int c = 0; c < n; ++c) M = fmaxf(M, wm[c * G + tid]);
+    rowM[tid] = M;
+  }
+  __syncthreads();
+  for (int idx = tid; idx < n * G; idx += nthr) wm[idx] = fast_exp2(wm[idx] - rowM[idx % G]);
+  __syncthreads();
+  if (tid < G) {
+    float L = 0.f;
+    for (int c = 0; c < n; ++c) L += wl[c * G + tid] * wm[c * G + tid];
+    rowInvL[tid] = 1.f / L;
+  }
+  __syncthreads();
+  OutT* out = static_cast<OutT*>(a.out) + static_cast<int64_t>(seq) * a.o_stride_seq +
+              static_cast<int64_t>(kvh) * G * D;
+  for (int e4 = tid; e4 < G * D / 4; e4 += nthr) {
+    const int r = (e4 * 4) / D;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    int c = 0;
+    for (; c + 4 <= n; c += 4) {
+      float4 v[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const float* rr =
+            a.partials + record_index(c_first + c + u, seg_unit, sp.q, sp.rem) * a.rec_stride;
+        v[u] = __ldcg(reinterpret_cast<const float4*>(rr) + e4);
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const float w = wm[(c + u) * G + r];
+        acc.x += w * v[u].x;
+        acc.y += w * v[u].y;
+        acc.z += w * v[u].z;
+        acc.w += w * v[u].w;
+      }
+    }
+    for (; c < n; ++c) {
+      const float* rr =
+          a.partials + record_index(c_first + c, seg_unit, sp.q, sp.rem) * a.rec_stride;
+      const float4 v = __ldcg(reinterpret_cast<const float4*>(rr) + e4);
+      const float w = wm[c * G + r];
+      acc.x += w * v.x;
+      acc.y += w * v.y;
+      acc.z += w * v.z;
+      acc.w += w * v.w;
+    }
+    const float inv = rowInvL[r];
+    store_out<OutT>(out + 4 * e4 + 0, acc.x * inv);
+    store_out<OutT>(out + 4 * e4 + 1, acc.y * inv);
+    store_out<OutT>(out + 4 * e4 + 2, acc.z * inv);
+    store_out<OutT>(out + 4 * e4 + 3, acc.w * inv);
+  }
+  __syncthreads();  // scratch may be reused
 }
 
 // Host-side launchers (defined in decode_mma.cu / decode_simt.cu).

@@ -1,232 +1,240 @@
 // Tensor-core split-K decode attention for bf16 KV pools, block_size 16,
 // head_dim 64 or 128, up to 16 query heads per kv head.
 //
-// One persistent CTA per (SM x occupancy) slot.  Warp 4 is the producer: it
-// walks the CTA's span of KV blocks (see decode.cuh), looks each block up in the
-// block table and issues one TMA box per block half (16 tokens x 64 dims,
-// 128-byte swizzle) for K and for V into a ring of NSTAGE stages, plus a bulk copy
-// of the query rows of the GQA group at the start of every segment.  Warps 0-3 are
-// consumers: warp w owns block w of each 4-block tile and runs
-//     S = Q K^T   (m16n8k16, rows = the group's query heads padded to 16)
-//     online softmax on the fragments (quad shuffles, base-2)
-//     O += P V    (P re-used from the S accumulators as the A operand)
-// so each KV byte is read from HBM once for all query heads of its group (the
-// reference op re-reads it once per query head, csrc/paged_attention.cpp:92-103).
+// Every warp is an independent stream-K worker.  The CTA's span of KV blocks
+// (decode.cuh) is cut into W contiguous warp spans; a warp walks its span one
+// block at a time through its own ring of S shared-memory stages.  Its lane 0
+// looks the block up in the block table (32 entries per coalesced load) and
+// issues one TMA box per 64-dim half of the block for K and for V (16 tokens x
+// 128 bytes, 128-byte swizzle), plus a bulk copy of the GQA group's query rows at
+// the start of each segment; each stage completes on the warp's own mbarrier.
+// Many short independent pipelines per SM keep far more DRAM requests moving than
+// a few deep ones, because a pipeline drains in order.
+//
+// Per block the warp runs
+//     S = Q K^T   (mma.sync m16n8k16; rows = the group's query heads padded to 16)
+//     online softmax on the fragments (quad shuffles, base 2)
+//     O += P V    (P reused from the S accumulators as the A operand)
+// so each KV byte leaves HBM once for all query heads of its group; the
+// reference op reads it once per query head (csrc/paged_attention.cpp:92-103).
+// A segment whose blocks all lie in the warp's span is written straight from
+// registers.  Cut segments go to per-warp slots in shared memory; after one CTA
+// barrier the warp holding the end of each chain merges it and writes the output
+// or, for a segment that crosses CTAs, the CTA's partial record (decode.cuh).
 #include "decode.cuh"
 
 namespace bsb {
 namespace {
 
-constexpr int kNCW = 4;     // consumer warps == KV blocks per tile
-constexpr int kBS = 16;     // tokens per block (fast path only)
-constexpr int kThreads = (kNCW + 1) * 32;
+constexpr int kBS = 16;  // tokens per block (fast path only)
 
-enum : int32_t { kFirst = 1, kLast = 2, kWhole = 4 };
+enum : int32_t { kFirst = 1, kLast = 2, kWhole = 4, kSlot1 = 8 };
 
 struct TileMeta {
-  int32_t seq;   // -1: no more work
+  int32_t seq;
   int32_t kvh;
-  int32_t blk0;  // index of the tile's first block within the sequence
-  int32_t nblk;  // blocks in this tile
-  int32_t len;   // context length of the sequence
+  int32_t blk;  // block index within the sequence
+  int32_t len;  // context length of the sequence
   int32_t flags;
-  int32_t nb;    // units of the segment
-  int32_t pad;
+  int32_t nb;   // units of the segment
   int64_t seg_unit;
 };
 
 template <int D, bool G16>
 struct Cfg {
+  static constexpr int W = 4;                  // warps per CTA
+  static constexpr int S = (D == 64) ? 3 : 2;  // stages per warp
+  static constexpr int MIN_CTAS = (D == 64) ? 3 : 2;  // resident CTAs per SM (register cap)
   static constexpr int HALVES = D / 64;
-  static constexpr int BLOCK_BYTES = kBS * D * 2;        // one block of one kv head
-  static constexpr int TILE_BYTES = kNCW * BLOCK_BYTES;  // K (or V) part of a stage
-  static constexpr int Q_BYTES = 16 * D * 2;
-  static constexpr int STAGE_BYTES = 2 * TILE_BYTES + Q_BYTES;  // multiple of 1024
-  static constexpr int NSTAGE = (D == 64) ? 5 : 3;
   static constexpr int GROWS = G16 ? 16 : 8;
-  static constexpr int MERGE_FLOATS = kNCW * GROWS * D + 2 * kNCW * GROWS;
-  static constexpr int SMEM_BYTES = 1024 /*align slack*/ + NSTAGE * STAGE_BYTES + MERGE_FLOATS * 4;
+  static constexpr int BLOCK_BYTES = kBS * D * 2;  // one block of one kv head
+  static constexpr int Q_BYTES = GROWS * D * 2;
+  static constexpr int STAGE_BYTES = 2 * BLOCK_BYTES + Q_BYTES;  // K | V | Q
+  static constexpr int SLOT_FLOATS = GROWS * D + 2 * GROWS;
+  // Slot 0 (a warp's first, cut portion) has its own storage; slot 1 (its last
+  // portion) is written after the warp's final block and reuses its stages.
+  static constexpr int SLOT0_BYTES = ((SLOT_FLOATS * 4 + 1023) / 1024) * 1024;
+  static constexpr int SMEM_BYTES = 1024 + W * S * STAGE_BYTES + W * SLOT0_BYTES;
   static_assert(STAGE_BYTES % 1024 == 0, "stages must stay 1024-byte aligned");
+  static_assert(SLOT_FLOATS * 4 <= S * STAGE_BYTES, "slot 1 must fit in the stages");
 };
 
 template <int D, bool G16>
-__global__ void __launch_bounds__(kThreads)
+__global__ void __launch_bounds__(Cfg<D, G16>::W * 32, Cfg<D, G16>::MIN_CTAS)
     decode_mma_kernel(const __grid_constant__ CUtensorMap kmap,
                       const __grid_constant__ CUtensorMap vmap, const DecodeArgs a) {
   using C = Cfg<D, G16>;
-  constexpr int NSTAGE = C::NSTAGE;
+  constexpr int W = C::W, S = C::S;
   extern __shared__ uint8_t smem_raw[];
-  __shared__ uint64_t full_bar[NSTAGE];
-  __shared__ uint64_t empty_bar[NSTAGE];
-  __shared__ TileMeta meta[NSTAGE];
+  __shared__ uint64_t full_bar[W][S];
+  __shared__ TileMeta meta[W][S];
   __shared__ ScanSmem scan;
-  __shared__ int32_t s_flag;
+  __shared__ WarpStarts starts;
+  __shared__ int32_t slot_seq[W][2], slot_kvh[W][2], slot_nb[W][2];
+  __shared__ int64_t slot_unit[W][2];
+  // Segments whose last record this CTA wrote: merged by the whole CTA.
+  __shared__ int32_t fin_count;
+  __shared__ int32_t fin_seq[2 * W], fin_kvh[2 * W], fin_nb[2 * W];
+  __shared__ int64_t fin_unit[2 * W];
 
   const uint32_t raw = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + (((raw + 1023u) & ~1023u) - raw);
-  float* sO = reinterpret_cast<float*>(smem + NSTAGE * C::STAGE_BYTES);
-  float* sM = sO + kNCW * C::GROWS * D;
-  float* sL = sM + kNCW * C::GROWS;
-
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  auto stages_of = [&](int w) { return smem + w * S * C::STAGE_BYTES; };
+  auto slot_of = [&](int w, int k) {
+    return reinterpret_cast<float*>(k == 0 ? smem + W * S * C::STAGE_BYTES + w * C::SLOT0_BYTES
+                                           : stages_of(w));
+  };
+  uint8_t* wst = stages_of(warp);
+
   if (tid == 0) {
-    for (int s = 0; s < NSTAGE; ++s) {
-      mbar_init(&full_bar[s], 1);
-      mbar_init(&empty_bar[s], kNCW);
-    }
+    for (int w = 0; w < W; ++w)
+      for (int s = 0; s < S; ++s) mbar_init(&full_bar[w][s], 1);
     fence_barrier_init();
-  }
-  if (warp == kNCW && lane == 0) {
     prefetch_tensormap(&kmap);
     prefetch_tensormap(&vmap);
   }
-  const Span sp = compute_span(a, scan);  // contains __syncthreads (orders the inits)
+  if (tid < W * 2) slot_seq[tid / 2][tid % 2] = -1;
+  if (tid == 0) fin_count = 0;
+  const Span sp = compute_warp_spans<W>(a, scan, starts);  // syncs the inits
   if (sp.r0 >= sp.r1) return;
 
   const int G = a.groups;
   const int64_t Hkv = a.num_kv_heads;
+  const int64_t spanw = sp.r1 - sp.r0;
+  const int64_t wr0 = sp.r0 + spanw * warp / W;
+  const int64_t wr1 = sp.r0 + spanw * (warp + 1) / W;
+  const int32_t ntiles = static_cast<int32_t>(wr1 - wr0);
 
-  if (warp == kNCW) {
-    // ------------------------------------------------------------ producer
-    const uint64_t policy = l2_policy_evict_first();
-    int stage = 0;
-    uint32_t phase = 0;
-    int32_t i = sp.seq;
-    int64_t prefix = sp.prefix;
-    int32_t len, row;
-    int32_t nb = seq_units(a, i, len, row, false);
-    int64_t rel = sp.r0 - prefix * Hkv;
-    int32_t h = static_cast<int32_t>(rel / nb);
-    int32_t off = static_cast<int32_t>(rel % nb);
-    int64_t u = sp.r0;
-    bool ok = true;
-    while (u < sp.r1 && ok) {
-      const int64_t left = sp.r1 - u;
-      const int32_t take = (nb - off < left) ? (nb - off) : static_cast<int32_t>(left);
-      const bool whole = (off == 0 && take == nb);
-      const int64_t seg_unit = prefix * Hkv + static_cast<int64_t>(h) * nb;
-      const int32_t* table = a.block_tables + static_cast<int64_t>(row) * a.bt_stride;
-      for (int32_t t0 = off; t0 < off + take && ok; t0 += kNCW) {
-        const int32_t nblk = min(kNCW, off + take - t0);
-        int32_t blk = 0;
-        bool valid = false;
-        if (lane < nblk) {
-          blk = __ldg(table + t0 + lane);
-          valid = blk >= 0 && blk < a.num_blocks;
-          if (!valid) set_status(a.status, kStatusBadBlock);
-        }
-        const uint32_t vmask = __ballot_sync(0xffffffffu, valid);
-        const bool first = (t0 == off);
-        if (lane == 0) {
-          ok = mbar_wait(&empty_bar[stage], phase ^ 1u);
-          if (ok) {
-            TileMeta& m = meta[stage];
-            m.seq = i;
-            m.kvh = h;
-            m.blk0 = t0;
-            m.nblk = nblk;
-            m.len = len;
-            m.flags = (first ? kFirst : 0) | ((t0 + kNCW >= off + take) ? kLast : 0) |
-                      (whole ? kWhole : 0);
-            m.nb = nb;
-            m.seg_unit = seg_unit;
-            const uint32_t bytes =
-                __popc(vmask) * 2u * C::BLOCK_BYTES + (first ? G * D * 2u : 0u);
-            mbar_arrive_expect_tx(&full_bar[stage], bytes);
-          } else {
-            set_status(a.status, kStatusWaitTimeout);
-          }
-        }
-        ok = __shfl_sync(0xffffffffu, ok, 0);
-        if (!ok) break;
-        uint8_t* st = smem + stage * C::STAGE_BYTES;
-        if (valid) {
-          // Row of the block in the [Hkv * NB * bs, D] view; the host checks that
-          // Hkv * NB * bs fits in int32.
-          const int32_t y = (h * a.num_blocks + blk) * kBS;
-#pragma unroll
-          for (int hf = 0; hf < C::HALVES; ++hf) {
-            tma_load_2d_hint(st + (lane * C::HALVES + hf) * 2048, &kmap, &full_bar[stage], hf * 64,
-                             y, policy);
-            tma_load_2d_hint(st + C::TILE_BYTES + (lane * C::HALVES + hf) * 2048, &vmap,
-                             &full_bar[stage], hf * 64, y, policy);
-          }
-        }
-        if (first && lane == 0) {
-          const __nv_bfloat16* qsrc = static_cast<const __nv_bfloat16*>(a.q) +
-                                      static_cast<int64_t>(i) * a.q_stride_seq +
-                                      static_cast<int64_t>(h) * G * D;
-          bulk_load(st + 2 * C::TILE_BYTES, qsrc, G * D * 2u, &full_bar[stage]);
-        }
-        if (++stage == NSTAGE) {
-          stage = 0;
-          phase ^= 1u;
-        }
-      }
-      u += take;
-      off = 0;
-      if (++h == Hkv) {
-        h = 0;
-        prefix += nb;
-        do {
-          ++i;
-          nb = (i < a.num_seqs) ? seq_units(a, i, len, row, false) : 1;
-        } while (nb == 0);
-      }
+  // ---------------------------------------------------------------- issue cursor
+  // All lanes keep identical copies; lane 0 writes the stage metadata and
+  // issues the copies.
+  const uint64_t policy = l2_policy_evict_first();
+  int32_t ci = starts.seq[warp];
+  int64_t cprefix = starts.prefix[warp];
+  int32_t clen = 0, crow = 0, cnb = 0, ch = 0, cb = 0;
+  int32_t nxt_len = 0, nxt_row = 0;
+  int32_t win_row = -1, win0 = 0, win_val = 0;
+  int64_t cu = wr0;
+  if (ntiles > 0) {
+    cnb = seq_units(a, ci, clen, crow, false);
+    const int64_t rel = wr0 - cprefix * Hkv;
+    ch = static_cast<int32_t>(rel / cnb);
+    cb = static_cast<int32_t>(rel % cnb);
+    if (ci + 1 < a.num_seqs) {
+      nxt_len = __ldg(a.context_lens + ci + 1);
+      nxt_row = a.seq_rows != nullptr ? __ldg(a.seq_rows + ci + 1) : ci + 1;
     }
-    // End-of-work marker (also sent after a timeout so consumers stop).
-    if (lane == 0) {
-      if (mbar_wait(&empty_bar[stage], phase ^ 1u)) {
-        meta[stage].seq = -1;
-        mbar_arrive(&full_bar[stage]);
-      } else {
-        set_status(a.status, kStatusWaitTimeout);
-      }
-    }
-    return;
   }
 
-  // -------------------------------------------------------------- consumers
+  auto issue = [&](int stage) {
+    const int32_t* table = a.block_tables + static_cast<int64_t>(crow) * a.bt_stride;
+    if (win_row != crow || cb < win0 || cb >= win0 + 32) {
+      win_row = crow;
+      win0 = cb;
+      win_val = (cb + lane < cnb) ? __ldg(table + cb + lane) : 0;
+    }
+    const int32_t blk = __shfl_sync(0xffffffffu, win_val, cb - win0);
+    const bool valid = blk >= 0 && blk < a.num_blocks;
+    const int64_t seg_unit = cprefix * Hkv + static_cast<int64_t>(ch) * cnb;
+    const bool first = (cu == wr0) || (cb == 0);
+    const bool last = (cu == wr1 - 1) || (cb == cnb - 1);
+    const bool whole = seg_unit >= wr0 && seg_unit + cnb <= wr1;
+    if (lane == 0) {
+      if (!valid) set_status(a.status, kStatusBadBlock);
+      TileMeta& m = meta[warp][stage];
+      m.seq = ci;
+      m.kvh = ch;
+      m.blk = cb;
+      m.len = clen;
+      m.flags = (first ? kFirst : 0) | (last ? kLast : 0) | (whole ? kWhole : 0) |
+                (seg_unit > wr0 ? kSlot1 : 0);
+      m.nb = cnb;
+      m.seg_unit = seg_unit;
+      uint8_t* st = wst + stage * C::STAGE_BYTES;
+      const uint32_t bytes = (valid ? 2u * C::BLOCK_BYTES : 0u) + (first ? G * D * 2u : 0u);
+      mbar_arrive_expect_tx(&full_bar[warp][stage], bytes);
+      if (valid) {
+        // Row of the block in the [Hkv * NB * bs, D] view; the host checks that
+        // Hkv * NB * bs fits in int32.
+        const int32_t y = (ch * a.num_blocks + blk) * kBS;
+#pragma unroll
+        for (int hf = 0; hf < C::HALVES; ++hf) {
+          tma_load_2d_hint(st + hf * 2048, &kmap, &full_bar[warp][stage], hf * 64, y, policy);
+          tma_load_2d_hint(st + C::BLOCK_BYTES + hf * 2048, &vmap, &full_bar[warp][stage],
+                           hf * 64, y, policy);
+        }
+      }
+      if (first) {
+        const __nv_bfloat16* qsrc = static_cast<const __nv_bfloat16*>(a.q) +
+                                    static_cast<int64_t>(ci) * a.q_stride_seq +
+                                    static_cast<int64_t>(ch) * G * D;
+        bulk_load(st + 2 * C::BLOCK_BYTES, qsrc, G * D * 2u, &full_bar[warp][stage]);
+      }
+    }
+    // Advance to the next unit.
+    ++cu;
+    if (++cb == cnb) {
+      cb = 0;
+      if (++ch == Hkv) {
+        ch = 0;
+        cprefix += cnb;
+        ++ci;
+        cnb = (ci < a.num_seqs) ? units_of(a, nxt_len, nxt_row, clen, crow) : 1;
+        while (cnb == 0) {  // empty or invalid sequences own no units
+          ++ci;
+          cnb = (ci < a.num_seqs) ? seq_units(a, ci, clen, crow, false) : 1;
+        }
+        if (ci + 1 < a.num_seqs) {
+          nxt_len = __ldg(a.context_lens + ci + 1);
+          nxt_row = a.seq_rows != nullptr ? __ldg(a.seq_rows + ci + 1) : ci + 1;
+        }
+      }
+    }
+  };
+
+  for (int s = 0; s < S && s < ntiles; ++s) issue(s);
+
+  // ---------------------------------------------------------------- compute
   const int g = lane >> 2, t = lane & 3;
   constexpr int KSTEPS = D / 16;
   constexpr int NTILES = D / 8;
   uint32_t qa[KSTEPS][4];
   float o[NTILES][4];
-  float m2[2], lsum[2];
-  int stage = 0;
-  uint32_t phase = 0;
+  float m2[2] = {-INFINITY, -INFINITY}, lsum[2] = {0.f, 0.f};
   const float scale = a.scale;
 
-  while (true) {
-    if (!mbar_wait(&full_bar[stage], phase)) {
-      set_status(a.status, kStatusWaitTimeout);
+  for (int32_t it = 0; it < ntiles; ++it) {
+    const int stage = it % S;
+    const uint32_t phase = (it / S) & 1;
+    if (!mbar_wait(&full_bar[warp][stage], phase)) {
+      if (lane == 0) set_status(a.status, kStatusWaitTimeout);
       break;
     }
-    const TileMeta mt = meta[stage];
-    if (mt.seq < 0) break;
-    const uint8_t* st = smem + stage * C::STAGE_BYTES;
+    const TileMeta mt = meta[warp][stage];
+    const uint8_t* st = wst + stage * C::STAGE_BYTES;
     if (mt.flags & kFirst) {
       m2[0] = m2[1] = -INFINITY;
       lsum[0] = lsum[1] = 0.f;
 #pragma unroll
       for (int n = 0; n < NTILES; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
-      const uint32_t* sq = reinterpret_cast<const uint32_t*>(st + 2 * C::TILE_BYTES);
+      const uint32_t* sq = reinterpret_cast<const uint32_t*>(st + 2 * C::BLOCK_BYTES);
 #pragma unroll
       for (int kk = 0; kk < KSTEPS; ++kk) {
         // Row r, dims (16kk + 2t, +1) -> 32-bit word (r*D + 16kk + 2t) / 2.
         const int w0 = (g * D + 16 * kk + 2 * t) >> 1;
         const int w1 = ((g + 8) * D + 16 * kk + 2 * t) >> 1;
         qa[kk][0] = (g < G) ? sq[w0] : 0u;
-        qa[kk][1] = (g + 8 < G) ? sq[w1] : 0u;
+        qa[kk][1] = (G16 && g + 8 < G) ? sq[w1] : 0u;
         qa[kk][2] = (g < G) ? sq[w0 + 4] : 0u;
-        qa[kk][3] = (g + 8 < G) ? sq[w1 + 4] : 0u;
+        qa[kk][3] = (G16 && g + 8 < G) ? sq[w1 + 4] : 0u;
       }
     }
-    if (warp < mt.nblk) {
-      const int tok0 = (mt.blk0 + warp) * kBS;
+    {
+      const int tok0 = mt.blk * kBS;
       const int valid = min(kBS, mt.len - tok0);
-      const uint32_t kbase = smem_u32(st) + warp * C::HALVES * 2048;
-      const uint32_t vbase = kbase + C::TILE_BYTES;
+      const uint32_t kbase = smem_u32(st);
+      const uint32_t vbase = kbase + C::BLOCK_BYTES;
       float s[2][4];
 #pragma unroll
       for (int j = 0; j < 2; ++j) s[j][0] = s[j][1] = s[j][2] = s[j][3] = 0.f;
@@ -256,8 +264,7 @@ __global__ void __launch_bounds__(kThreads)
           mx[e >> 1] = fmaxf(mx[e >> 1], v);
         }
       }
-      float corr[2];
-      uint32_t pa[4];
+      float corr[2] = {1.f, 1.f};
 #pragma unroll
       for (int hr = 0; hr < (G16 ? 2 : 1); ++hr) {
         float m = mx[hr];
@@ -277,7 +284,7 @@ __global__ void __launch_bounds__(kThreads)
         }
         lsum[hr] = lsum[hr] * corr[hr] + ps;
       }
-      if (!G16) corr[1] = 1.f;
+      uint32_t pa[4];
       pa[0] = pack_bf16x2(s[0][0], s[0][1]);
       pa[1] = G16 ? pack_bf16x2(s[0][2], s[0][3]) : 0u;
       pa[2] = pack_bf16x2(s[1][0], s[1][1]);
@@ -314,43 +321,142 @@ __global__ void __launch_bounds__(kThreads)
         }
       }
     }
+    // The stage has been read: refill it with the block S positions ahead.
     __syncwarp();
-    if (lane == 0) mbar_arrive(&empty_bar[stage]);
-    if (++stage == NSTAGE) {
-      stage = 0;
-      phase ^= 1u;
+    if (it + S < ntiles) {
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      issue(stage);
     }
 
     if (mt.flags & kLast) {
-      // Deposit this warp's state and merge the four warps.
+      float lrow[2];
 #pragma unroll
-      for (int hr = 0; hr < (G16 ? 2 : 1); ++hr) {
+      for (int hr = 0; hr < 2; ++hr) {
         float l = lsum[hr];
         l += __shfl_xor_sync(0xffffffffu, l, 1);
         l += __shfl_xor_sync(0xffffffffu, l, 2);
-        const int r = g + 8 * hr;
-        if (r < G) {
-          if (t == 0) {
-            sM[warp * G + r] = m2[hr];
-            sL[warp * G + r] = l;
-          }
+        lrow[hr] = l;
+      }
+      if (mt.flags & kWhole) {
+        // The whole segment is in this warp: normalised output from registers.
+        __nv_bfloat16* out = static_cast<__nv_bfloat16*>(a.out) +
+                             static_cast<int64_t>(mt.seq) * a.o_stride_seq +
+                             static_cast<int64_t>(mt.kvh) * G * D;
 #pragma unroll
-          for (int n = 0; n < NTILES; ++n) {
-            float* dst = sO + (warp * G + r) * D + 8 * n + 2 * t;
-            dst[0] = o[n][2 * hr];
-            dst[1] = o[n][2 * hr + 1];
+        for (int hr = 0; hr < (G16 ? 2 : 1); ++hr) {
+          const int r = g + 8 * hr;
+          if (r < G) {
+            const float inv = 1.f / lrow[hr];
+#pragma unroll
+            for (int n = 0; n < NTILES; ++n) {
+              *reinterpret_cast<uint32_t*>(out + r * D + 8 * n + 2 * t) =
+                  pack_bf16x2(o[n][2 * hr] * inv, o[n][2 * hr + 1] * inv);
+            }
           }
         }
+      } else {
+        // A cut portion: park it in slot 0 (first portion) or slot 1 (last).
+        const int k = (mt.flags & kSlot1) ? 1 : 0;
+        float* slot = slot_of(warp, k);
+#pragma unroll
+        for (int hr = 0; hr < (G16 ? 2 : 1); ++hr) {
+          const int r = g + 8 * hr;
+          if (r < G) {
+#pragma unroll
+            for (int n = 0; n < NTILES; ++n) {
+              slot[r * D + 8 * n + 2 * t] = o[n][2 * hr];
+              slot[r * D + 8 * n + 2 * t + 1] = o[n][2 * hr + 1];
+            }
+            if (t == 0) {
+              slot[G * D + r] = m2[hr];
+              slot[G * D + G + r] = lrow[hr];
+            }
+          }
+        }
+        if (lane == 0) {
+          slot_seq[warp][k] = mt.seq;
+          slot_kvh[warp][k] = mt.kvh;
+          slot_nb[warp][k] = mt.nb;
+          slot_unit[warp][k] = mt.seg_unit;
+        }
       }
-      named_barrier_sync(1, kNCW * 32);
-      Portion po;
-      po.seq = mt.seq;
-      po.kvh = mt.kvh;
-      po.whole = (mt.flags & kWhole) ? 1 : 0;
-      po.seg_unit = mt.seg_unit;
-      po.nb = mt.nb;
-      emit_portion<kNCW, __nv_bfloat16>(a, sp, po, sO, sM, sL, tid, &s_flag, 1);
     }
+  }
+
+  // ---------------------------------------------------------------- CTA merge
+  // A segment cut between warps is a chain: the last portion of the warp where
+  // it starts, the only portion of warps inside it, the first portion of the
+  // warp where it ends.  The chain's tail (no later non-empty warp continues the
+  // segment) folds the earlier slots into its own and finishes the segment.
+  __syncthreads();
+  auto warp_empty = [&](int w) {
+    return sp.r0 + spanw * (w + 1) / W == sp.r0 + spanw * w / W;
+  };
+  auto holds = [&](int w, int k, int32_t seq, int32_t kvh) {
+    return slot_seq[w][k] == seq && slot_kvh[w][k] == kvh;
+  };
+  for (int k = 0; k < 2; ++k) {
+    const int32_t seq = slot_seq[warp][k];
+    if (seq < 0) continue;
+    const int32_t kvh = slot_kvh[warp][k];
+    bool tail = true;
+    if (k == 1 || slot_seq[warp][1] < 0) {
+      for (int w2 = warp + 1; w2 < W; ++w2) {
+        if (warp_empty(w2)) continue;
+        tail = !holds(w2, 0, seq, kvh);
+        break;
+      }
+    }
+    if (!tail) continue;
+    float* mine = slot_of(warp, k);
+    for (int w2 = warp - 1; w2 >= 0; --w2) {
+      if (warp_empty(w2)) continue;
+      const int k2 = holds(w2, 1, seq, kvh) ? 1 : (holds(w2, 0, seq, kvh) ? 0 : -1);
+      if (k2 < 0) break;
+      const float* other = slot_of(w2, k2);
+      for (int e = lane; e < G * D; e += 32) {
+        const int r = e / D;
+        const float M = fmaxf(mine[G * D + r], other[G * D + r]);
+        mine[e] = mine[e] * fast_exp2(mine[G * D + r] - M) +
+                  other[e] * fast_exp2(other[G * D + r] - M);
+      }
+      __syncwarp();
+      if (lane < G) {
+        const float M = fmaxf(mine[G * D + lane], other[G * D + lane]);
+        mine[G * D + G + lane] = mine[G * D + G + lane] * fast_exp2(mine[G * D + lane] - M) +
+                                 other[G * D + G + lane] * fast_exp2(other[G * D + lane] - M);
+        mine[G * D + lane] = M;
+      }
+      __syncwarp();
+      if (k2 == 1) break;  // the chain starts in that warp
+    }
+    const int64_t seg_unit = slot_unit[warp][k];
+    const int32_t nb = slot_nb[warp][k];
+    if (seg_unit >= sp.r0 && seg_unit + nb <= sp.r1) {
+      __nv_bfloat16* out = static_cast<__nv_bfloat16*>(a.out) +
+                           static_cast<int64_t>(seq) * a.o_stride_seq +
+                           static_cast<int64_t>(kvh) * G * D;
+      for (int e = lane; e < G * D; e += 32) {
+        out[e] = __float2bfloat16_rn(mine[e] / mine[G * D + G + e / D]);
+      }
+    } else if (warp_write_record(a, sp, seq, kvh, seg_unit, nb, mine, mine + G * D,
+                                 mine + G * D + G, lane)) {
+      if (lane == 0) {
+        const int idx = atomicAdd(&fin_count, 1);
+        fin_seq[idx] = seq;
+        fin_kvh[idx] = kvh;
+        fin_nb[idx] = nb;
+        fin_unit[idx] = seg_unit;
+      }
+    }
+  }
+  // Segments crossing CTAs for which this CTA came last: merge with all threads.
+  // The stages and slots are free now and serve as scratch.
+  __syncthreads();
+  const int nfin = fin_count;
+  for (int f = 0; f < nfin; ++f) {
+    cta_merge_records<__nv_bfloat16>(a, sp, fin_seq[f], fin_kvh[f], fin_unit[f], fin_nb[f],
+                                     reinterpret_cast<float*>(smem));
   }
 }
 
@@ -366,7 +472,7 @@ int launch_one(const DecodeArgs& a, const CUtensorMap& kmap, const CUtensorMap& 
     if (e != cudaSuccess) return static_cast<int>(e);
     configured = true;
   }
-  decode_mma_kernel<D, G16><<<grid, kThreads, C::SMEM_BYTES, stream>>>(kmap, vmap, a);
+  decode_mma_kernel<D, G16><<<grid, C::W * 32, C::SMEM_BYTES, stream>>>(kmap, vmap, a);
   return static_cast<int>(cudaGetLastError());
 }
 
@@ -377,7 +483,7 @@ int occupancy_one() {
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
   if (e != cudaSuccess) return -static_cast<int>(e);
   int n = 0;
-  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, decode_mma_kernel<D, G16>, kThreads,
+  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, decode_mma_kernel<D, G16>, C::W * 32,
                                                     C::SMEM_BYTES);
   if (e != cudaSuccess) return -static_cast<int>(e);
   return n;

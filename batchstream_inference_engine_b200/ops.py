@@ -63,7 +63,10 @@ class _Workspaces:
                 size = max(nbytes, 1 << 20)
                 if buf is not None:
                     size = max(size, 2 * buf.numel())
-                buf = torch.zeros(size, dtype=torch.uint8, device=device)
+                fresh = torch.zeros(size, dtype=torch.uint8, device=device)
+                if buf is not None:  # keep status bits not yet taken
+                    fresh[:4].copy_(buf[:4])
+                buf = fresh
                 self._buffers[key] = buf
             return buf
 

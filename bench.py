@@ -27,9 +27,7 @@ import json
 import math
 import os
 import statistics
-import subprocess
 import sys
-import tempfile
 import threading
 import time
 from concurrent.futures import ThreadPoolExecutor
@@ -53,8 +51,8 @@ POOL_FRACTION = 0.6
 def parse_args():
     p = argparse.ArgumentParser()
     p.add_argument("--gpus", type=int, default=1)
-    p.add_argument("--steps", type=int, default=50)
-    p.add_argument("--warmup", type=int, default=5)
+    p.add_argument("--steps", type=int, default=1000)
+    p.add_argument("--warmup", type=int, default=20)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
     p.add_argument("--workload", choices=sorted(WORKLOADS), default="decode_d64")
     p.add_argument("--cpu-seconds", type=float, default=10.0,
@@ -101,60 +99,75 @@ def algorithmic_bytes(lens, heads, kv_heads, head_dim) -> int:
 
 
 class ClockSampler:
-    """nvidia-smi clock/throttle samples every 200 ms while the timed loop runs."""
+    """Samples SM clock and clock-event reasons through NVML every 2 ms while the
+    timed loop runs (reading only; no GPU setting is touched)."""
 
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = {
+        "hw_slowdown": "nvmlClocksEventReasonHwSlowdown",
+        "hw_thermal_slowdown": "nvmlClocksEventReasonHwThermalSlowdown",
+        "sw_thermal_slowdown": "nvmlClocksEventReasonSwThermalSlowdown",
+        "sw_power_cap": "nvmlClocksEventReasonSwPowerCap",
+    }
 
-    def __init__(self, gpu_index: int):
-        self.gpu = gpu_index
-        self.proc = None
-        self.path = Path(tempfile.mkstemp(prefix="clocks_", suffix=".csv")[1])
+    def __init__(self, device):
+        self.device = device
+        self.samples: list[tuple[int, int]] = []
+        self.max_mhz = None
+        self._stop = threading.Event()
+        self._thread = None
+        self._nvml = None
+        self._handle = None
+
+    def _open(self):
+        import pynvml
+        import torch
+
+        pynvml.nvmlInit()
+        props = torch.cuda.get_device_properties(self.device)
+        bus = f"{props.pci_domain_id:08x}:{props.pci_bus_id:02x}:{props.pci_device_id:02x}.0"
+        try:
+            self._handle = pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+        except pynvml.NVMLError:
+            self._handle = pynvml.nvmlDeviceGetHandleByIndex(self.device.index or 0)
+        self._nvml = pynvml
+        self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._handle, pynvml.NVML_CLOCK_SM)
+
+    def _run(self):
+        nv, h = self._nvml, self._handle
+        while not self._stop.is_set():
+            try:
+                self.samples.append((nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM),
+                                     nv.nvmlDeviceGetCurrentClocksEventReasons(h)))
+            except Exception:
+                pass
+            self._stop.wait(0.002)
 
     def __enter__(self):
         try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
-                 "--format=csv,noheader,nounits", "-lms", "200"],
-                stdout=self.path.open("w"), stderr=subprocess.DEVNULL)
-        except OSError:
-            self.proc = None
+            self._open()
+            self._thread = threading.Thread(target=self._run, daemon=True)
+            self._thread.start()
+        except Exception:
+            self._thread = None
         return self
 
     def __exit__(self, *exc):
-        if self.proc is not None:
-            self.proc.terminate()
-            try:
-                self.proc.wait(timeout=5)
-            except subprocess.TimeoutExpired:
-                self.proc.kill()
+        self._stop.set()
+        if self._thread is not None:
+            self._thread.join(timeout=5)
         return False
 
     def summary(self) -> dict:
-        sm, mx, reasons = [], [], set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        try:
-            lines = self.path.read_text().strip().splitlines()
-        except OSError:
-            lines = []
-        for line in lines:
-            parts = [p.strip() for p in line.split(",")]
-            if len(parts) < 9:
-                continue
-            try:
-                sm.append(float(parts[1]))
-                mx.append(float(parts[2]))
-            except ValueError:
-                continue
-            for name, flag in zip(names, parts[5:9]):
-                if flag.lower() == "active":
-                    reasons.add(name)
-        self.path.unlink(missing_ok=True)
-        if not sm:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
-        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx),
-                "reasons": sorted(reasons), "samples": len(sm)}
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": [], "samples": 0}
+        active = set()
+        for _, bits in self.samples:
+            for name, const in self.REASONS.items():
+                if bits & getattr(self._nvml, const):
+                    active.add(name)
+        return {"sm_mhz": statistics.median(mhz for mhz, _ in self.samples),
+                "sm_max_mhz": self.max_mhz, "reasons": sorted(active),
+                "samples": len(self.samples)}
 
 
 # ------------------------------------------------------------------ CPU baseline
@@ -304,10 +317,11 @@ def run_ours(args):
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize(dev)
-    with ClockSampler(local) as clocks:
+    with ClockSampler(dev) as clocks:
         t0 = torch.cuda.Event(enable_timing=True)
         t1 = torch.cuda.Event(enable_timing=True)
         t0.record(stream)
+        torch.cuda.nvtx.range_push("timed")
         for i in range(args.steps):
             r = i % ROTATIONS
             starts[i].record(stream)
@@ -316,6 +330,7 @@ def run_ours(args):
             ops.paged_attention_batched(q[r], k_pool, v_pool, tables[r], ctx, scale, out=out,
                                         units_hint=units)
             ends[i].record(stream)
+        torch.cuda.nvtx.range_pop()
         t1.record(stream)
         torch.cuda.synchronize(dev)
     if world > 1:

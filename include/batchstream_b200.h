@@ -7,9 +7,11 @@
  * bs_last_error() returns a message for the calling thread; a binding raises it
  * as the reference's RuntimeError.  Nothing here allocates device memory: a call
  * that needs scratch space takes a caller-provided `workspace` whose size comes
- * from the matching *_workspace_bytes() query, zero-filled once when it is
- * first allocated (the kernels leave it zero-filled again after every call).
- * One workspace serves one call at a time.
+ * from the matching *_workspace_bytes() query.  A workspace must be zero-filled
+ * once, when it is first allocated: its first 256 KiB + 256 bytes hold the
+ * status word and per-segment counters, which every call leaves at zero again;
+ * the rest is scratch.  Any sequence of calls (any batch size, single-sequence
+ * and batched) may share one workspace, one call at a time.
  *
  * Layouts (row-major, elements):
  *   query     [num_seqs, num_heads, head_dim], heads of a sequence contiguous
