@@ -45,7 +45,7 @@ _SIGNATURES = {
     ),
     "bs_paged_attention_batched": (
         [_p, _i64, _p, _p, _p, _i64, _i64, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64, _i64,
-         _i32, _dbl, _i64, _p, _i64, _p, _u64, _p],
+         _i32, _dbl, _i64, _i32, _p, _i64, _p, _u64, _p],
         ctypes.c_int,
     ),
     "bs_paged_attention_batched_workspace_bytes": (

@@ -22,6 +22,23 @@
 namespace bsb {
 namespace {
 
+cudaLaunchConfig_t pdl_config(int grid, int threads, cudaStream_t stream) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(threads);
+  cfg.stream = stream;
+  return cfg;
+}
+
+// Programmatic stream serialization: the kernel may launch before the previous
+// one on the stream finishes; it calls pdl_wait() before reading any input.
+void pdl_attr(cudaLaunchConfig_t& cfg, cudaLaunchAttribute* attr) {
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+}
+
 constexpr int kMetaThreads = 256;
 constexpr int kMaxMetaRows = 8192;
 
@@ -36,6 +53,8 @@ __global__ void __launch_bounds__(kMetaThreads)
   __shared__ int32_t cu[kMaxMetaRows + 1];
   __shared__ int32_t warp_tot[kMetaThreads / 32];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  pdl_trigger();
+  pdl_wait();
 
   // Block-wide exclusive scan of n_new in chunks of kMetaThreads.
   int32_t carry = 0;
@@ -135,6 +154,8 @@ __global__ void __launch_bounds__(256)
                           int64_t v_stride, const int32_t* __restrict__ slots, int32_t T,
                           int32_t Hkv, int32_t D, Tpool* __restrict__ k_pool,
                           Tpool* __restrict__ v_pool, int64_t pool_slots, uint32_t* status) {
+  pdl_trigger();
+  pdl_wait();
   const int32_t vecs = D >> 3;
   const int64_t per_tensor = static_cast<int64_t>(T) * Hkv * vecs;
   const int64_t total = 2 * per_tensor;
@@ -184,6 +205,8 @@ __global__ void __launch_bounds__(256)
                              int64_t v_stride, const int32_t* __restrict__ slots, int32_t T,
                              int32_t Hkv, int32_t D, Tpool* __restrict__ k_pool,
                              Tpool* __restrict__ v_pool, int64_t pool_slots, uint32_t* status) {
+  pdl_trigger();
+  pdl_wait();
   const int64_t per_tensor = static_cast<int64_t>(T) * Hkv * D;
   for (int64_t idx = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
        idx < 2 * per_tensor; idx += static_cast<int64_t>(gridDim.x) * blockDim.x) {
@@ -214,16 +237,13 @@ int launch_slot_write_t(const void* k, const void* v, int64_t ks, int64_t vs, co
   int64_t blocks = (work + 255) / 256;
   const int64_t cap = static_cast<int64_t>(sms) * 8;
   if (blocks > cap) blocks = cap;
-  if (vec) {
-    slot_write_vec_kernel<Tin, Tpool><<<static_cast<int>(blocks), 256, 0, stream>>>(
-        static_cast<const Tin*>(k), static_cast<const Tin*>(v), ks, vs, slots, T, Hkv, D,
-        static_cast<Tpool*>(kp), static_cast<Tpool*>(vp), pool_slots, status);
-  } else {
-    slot_write_scalar_kernel<Tin, Tpool><<<static_cast<int>(blocks), 256, 0, stream>>>(
-        static_cast<const Tin*>(k), static_cast<const Tin*>(v), ks, vs, slots, T, Hkv, D,
-        static_cast<Tpool*>(kp), static_cast<Tpool*>(vp), pool_slots, status);
-  }
-  return static_cast<int>(cudaGetLastError());
+  cudaLaunchConfig_t cfg = pdl_config(static_cast<int>(blocks), 256, stream);
+  cudaLaunchAttribute attr[1];
+  pdl_attr(cfg, attr);
+  auto kernel = vec ? slot_write_vec_kernel<Tin, Tpool> : slot_write_scalar_kernel<Tin, Tpool>;
+  return static_cast<int>(cudaLaunchKernelEx(
+      &cfg, kernel, static_cast<const Tin*>(k), static_cast<const Tin*>(v), ks, vs, slots, T, Hkv,
+      D, static_cast<Tpool*>(kp), static_cast<Tpool*>(vp), pool_slots, status));
 }
 
 }  // namespace
@@ -237,10 +257,12 @@ int launch_step_metadata(const int32_t* seq_rows, const int32_t* start_pos, cons
                          int32_t* slots, int32_t* context_lens, uint32_t* status,
                          cudaStream_t stream) {
   const int grid = T > 0 ? (T + kMetaThreads - 1) / kMetaThreads : 1;
-  step_metadata_kernel<<<grid, kMetaThreads, 0, stream>>>(
-      seq_rows, start_pos, n_new, R, block_tables, bt_stride, bt_rows, max_blocks, block_size,
-      num_blocks, T, cu_q, positions, slots, context_lens, status);
-  return static_cast<int>(cudaGetLastError());
+  cudaLaunchConfig_t cfg = pdl_config(grid, kMetaThreads, stream);
+  cudaLaunchAttribute attr[1];
+  pdl_attr(cfg, attr);
+  return static_cast<int>(cudaLaunchKernelEx(
+      &cfg, step_metadata_kernel, seq_rows, start_pos, n_new, R, block_tables, bt_stride, bt_rows,
+      max_blocks, block_size, num_blocks, T, cu_q, positions, slots, context_lens, status));
 }
 
 // in_bf16 / pool_bf16: element types of the k/v rows and of the pool.

@@ -216,14 +216,46 @@ bool is_contiguous(int32_t ndim, const int64_t* shape, const int64_t* strides) {
 }
 
 // Shared launch of the decode kernels once everything is validated.
+// Encoded pool maps of the last few pools seen by this thread (a model's layers
+// reuse the same views every step, so encoding once per view is enough).
+struct MapCacheEntry {
+  const void* base = nullptr;
+  int64_t rows = 0, head_dim = 0;
+  CUtensorMap map;
+};
+
+int cached_pool_map(CUtensorMap* out, const void* base, int64_t rows, int64_t head_dim) {
+  constexpr int kEntries = 128;
+  thread_local MapCacheEntry cache[kEntries];
+  thread_local int next = 0;
+  for (int i = 0; i < kEntries; ++i) {
+    const MapCacheEntry& e = cache[i];
+    if (e.base == base && e.rows == rows && e.head_dim == head_dim) {
+      *out = e.map;
+      return BS_OK;
+    }
+  }
+  MapCacheEntry& e = cache[next];
+  if (int rc = encode_pool_map(&e.map, base, rows, head_dim)) {
+    e.base = nullptr;
+    return rc;
+  }
+  e.base = base;
+  e.rows = rows;
+  e.head_dim = head_dim;
+  next = (next + 1) % kEntries;
+  *out = e.map;
+  return BS_OK;
+}
+
 int launch_decode(bsb::DecodeArgs& a, int32_t dtype, int grid, cudaStream_t stream) {
   const bool mma = use_mma_path(dtype, a.block_size, a.head_dim, a.groups);
   int rc;
   if (mma) {
     CUtensorMap kmap, vmap;
     const int64_t rows = static_cast<int64_t>(a.num_kv_heads) * a.num_blocks * a.block_size;
-    if ((rc = encode_pool_map(&kmap, a.k_pool, rows, a.head_dim))) return rc;
-    if ((rc = encode_pool_map(&vmap, a.v_pool, rows, a.head_dim))) return rc;
+    if ((rc = cached_pool_map(&kmap, a.k_pool, rows, a.head_dim))) return rc;
+    if ((rc = cached_pool_map(&vmap, a.v_pool, rows, a.head_dim))) return rc;
     rc = bsb::launch_decode_mma(a, kmap, vmap, grid, stream);
   } else {
     rc = bsb::launch_decode_simt(a, dtype == BS_BF16, grid, stream);
@@ -388,10 +420,11 @@ int bs_paged_attention_batched(const void* query, int64_t query_seq_stride, cons
                                const int32_t* context_lens, int64_t num_seqs, int64_t num_heads,
                                int64_t num_kv_heads, int64_t head_dim, int64_t block_size,
                                int64_t num_blocks, int64_t max_blocks_per_seq, int32_t dtype,
-                               double scaling, int64_t units_hint, void* output,
+                               double scaling, int64_t units_hint, int32_t flags, void* output,
                                int64_t output_seq_stride, void* workspace,
                                uint64_t workspace_bytes, void* stream) {
   BS_CHECK(dtype == BS_BF16 || dtype == BS_F32, "dtype must be bfloat16 or float32");
+  BS_CHECK((flags & ~BS_LENS_READY) == 0, "unknown flags");
   BS_CHECK(num_seqs >= 0, "num_seqs must be non-negative");
   BS_CHECK(num_kv_heads > 0 && num_heads > 0 && num_heads % num_kv_heads == 0,
            "heads must equal kv_heads * groups");
@@ -457,6 +490,7 @@ int bs_paged_attention_batched(const void* query, int64_t query_seq_stride, cons
   a.rec_stride = record_stride(groups, head_dim);
   a.seg_counters = reinterpret_cast<int32_t*>(ws + w.counters);
   a.status = reinterpret_cast<uint32_t*>(ws);
+  a.lens_ready = (flags & BS_LENS_READY) ? 1 : 0;
   int64_t grid = grid_max;
   if (units_hint > 0) {
     const int64_t want = (units_hint + 3) / 4;

@@ -179,6 +179,16 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   return *reinterpret_cast<uint32_t*>(&v);
 }
 
+// Programmatic dependent launch.  A kernel launched with the programmatic
+// stream-serialization attribute may start while the previous kernel on its
+// stream is still running; pdl_wait() blocks until that kernel has finished and
+// its writes are visible (a no-op without the attribute).  pdl_trigger() lets
+// the next such kernel start early.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // Consumer-only named barrier (id 1); the producer warp never joins it.
 __device__ __forceinline__ void named_barrier_sync(uint32_t id, uint32_t threads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");

@@ -46,6 +46,10 @@ struct DecodeArgs {
   int32_t rec_stride;
   int32_t* seg_counters;  // [B * Hkv], zero between launches
   uint32_t* status;
+  // Non-zero when context_lens, block_tables and seq_rows were final before the
+  // kernel launched just ahead of this one: the span search may then overlap it
+  // (programmatic dependent launch); query and pools are read only after it.
+  int32_t lens_ready;
 };
 
 // Units of a sequence from its raw length and table row (already loaded);

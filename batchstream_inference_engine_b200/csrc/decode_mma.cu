@@ -96,7 +96,9 @@ __global__ void __launch_bounds__(Cfg<D, G16>::W * 32, Cfg<D, G16>::MIN_CTAS)
   }
   if (tid < W * 2) slot_seq[tid / 2][tid % 2] = -1;
   if (tid == 0) fin_count = 0;
+  if (!a.lens_ready) pdl_wait();
   const Span sp = compute_warp_spans<W>(a, scan, starts);  // syncs the inits
+  if (a.lens_ready) pdl_wait();  // query, pools and tables' contents from here on
   if (sp.r0 >= sp.r1) return;
 
   const int G = a.groups;
@@ -472,8 +474,17 @@ int launch_one(const DecodeArgs& a, const CUtensorMap& kmap, const CUtensorMap& 
     if (e != cudaSuccess) return static_cast<int>(e);
     configured = true;
   }
-  decode_mma_kernel<D, G16><<<grid, C::W * 32, C::SMEM_BYTES, stream>>>(kmap, vmap, a);
-  return static_cast<int>(cudaGetLastError());
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(C::W * 32);
+  cfg.dynamicSmemBytes = C::SMEM_BYTES;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return static_cast<int>(cudaLaunchKernelEx(&cfg, decode_mma_kernel<D, G16>, kmap, vmap, a));
 }
 
 template <int D, bool G16>

@@ -58,6 +58,7 @@ __global__ void __launch_bounds__(kThreads) decode_simt_kernel(const DecodeArgs 
   __shared__ int32_t s_flag;
   extern __shared__ float dsm[];  // sQ [G*D] | sO [warps*G*D] | sM [warps*G] | sL [warps*G]
 
+  pdl_wait();
   const Span sp = compute_span(a, scan);
   if (sp.r0 >= sp.r1) return;
 
@@ -242,8 +243,17 @@ int launch_decode_simt(const DecodeArgs& a, int dtype_is_bf16, int grid, cudaStr
   KernelFn fn = pick(a.head_dim, a.groups, dtype_is_bf16);
   const size_t smem = smem_bytes(a.head_dim, a.groups);
   if (int e = prepare(fn, smem)) return e;
-  fn<<<grid, kThreads, smem, stream>>>(a);
-  return static_cast<int>(cudaGetLastError());
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return static_cast<int>(cudaLaunchKernelEx(&cfg, fn, a));
 }
 
 int decode_simt_ctas_per_sm(int head_dim, int groups, int dtype_is_bf16) {

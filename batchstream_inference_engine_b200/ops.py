@@ -146,11 +146,14 @@ class _NullContext:
         return False
 
 
+_batched_ws_bytes: dict[tuple, int] = {}
+
+
 def paged_attention_batched(query: torch.Tensor, key_pool: torch.Tensor, value_pool: torch.Tensor,
                             block_tables: torch.Tensor, context_lens: torch.Tensor, scaling: float,
                             seq_rows: torch.Tensor | None = None, out: torch.Tensor | None = None,
                             max_blocks_per_seq: int | None = None,
-                            units_hint: int = 0) -> torch.Tensor:
+                            units_hint: int = 0, lens_ready: bool = False) -> torch.Tensor:
     """Decode attention for a whole ragged batch in one launch.
 
     query [B, H, D]; key_pool/value_pool [Hkv, NB, bs, D] (one layer of the
@@ -189,15 +192,20 @@ def paged_attention_batched(query: torch.Tensor, key_pool: torch.Tensor, value_p
     code = dtype_code(query.dtype)
     with torch.cuda.device(device):
         stream = torch.cuda.current_stream(device).cuda_stream
-        need = ctypes.c_uint64(0)
-        check(lib().bs_paged_attention_batched_workspace_bytes(B, H, Hkv, D, bs, code,
-                                                               ctypes.byref(need)))
-        ws = workspace_for(device, need.value)
+        key = (device.index, B, H, Hkv, D, bs, code)
+        need = _batched_ws_bytes.get(key)
+        if need is None:
+            got = ctypes.c_uint64(0)
+            check(lib().bs_paged_attention_batched_workspace_bytes(B, H, Hkv, D, bs, code,
+                                                                   ctypes.byref(got)))
+            need = _batched_ws_bytes[key] = got.value
+        ws = workspace_for(device, need)
         check(lib().bs_paged_attention_batched(
             query.data_ptr(), query.stride(0), key_pool.data_ptr(), value_pool.data_ptr(),
             block_tables.data_ptr(), block_tables.stride(0), block_tables.size(0),
             seq_rows.data_ptr() if seq_rows is not None else None, context_lens.data_ptr(),
-            B, H, Hkv, D, bs, NB, mb, code, float(scaling), int(units_hint), out.data_ptr(),
+            B, H, Hkv, D, bs, NB, mb, code, float(scaling), int(units_hint),
+            1 if lens_ready else 0, out.data_ptr(),
             out.stride(0), ws.data_ptr(), ws.numel(), stream))
     return out
 

@@ -304,12 +304,34 @@ def run_ours(args):
         ops.reshape_and_cache(k_new[r], v_new[r], k_pool, v_pool, slots)
         return ctx, slots
 
+    def decode(r, ctx):
+        ops.paged_attention_batched(q[r], k_pool, v_pool, tables[r], ctx, scale, out=out,
+                                    units_hint=units)
+
+    # Each step is replayed from two CUDA graphs (metadata + slot write, then the
+    # decode) so the device timings carry no host launch overhead; the events
+    # between the two graphs time the decode kernel on the launching stream.
     stream = torch.cuda.current_stream(dev)
+    capture = torch.cuda.Stream(dev)
+    capture.wait_stream(stream)
+    with torch.cuda.stream(capture):
+        for i in range(args.warmup):
+            ctx, _ = step(i % ROTATIONS)
+            decode(i % ROTATIONS, ctx)
+        ops.take_status(dev)
+        graphs = []
+        for r in range(ROTATIONS):
+            ga, gb = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
+            with torch.cuda.graph(ga, stream=capture):
+                ctx, _ = step(r)
+            with torch.cuda.graph(gb, stream=capture):
+                decode(r, ctx)
+            graphs.append((ga, gb, ctx))
+    torch.cuda.synchronize(dev)
     for i in range(args.warmup):
-        ctx, _ = step(i % ROTATIONS)
-        ops.paged_attention_batched(q[i % ROTATIONS], k_pool, v_pool, tables[i % ROTATIONS], ctx,
-                                    scale, out=out, units_hint=units)
-    ops.take_status(dev)
+        ga, gb, _ = graphs[i % ROTATIONS]
+        ga.replay()
+        gb.replay()
 
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     mids = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
@@ -323,18 +345,19 @@ def run_ours(args):
         t0.record(stream)
         torch.cuda.nvtx.range_push("timed")
         for i in range(args.steps):
-            r = i % ROTATIONS
+            ga, gb, _ = graphs[i % ROTATIONS]
             starts[i].record(stream)
-            ctx, _ = step(r)
+            ga.replay()
             mids[i].record(stream)
-            ops.paged_attention_batched(q[r], k_pool, v_pool, tables[r], ctx, scale, out=out,
-                                        units_hint=units)
+            gb.replay()
             ends[i].record(stream)
         torch.cuda.nvtx.range_pop()
         t1.record(stream)
         torch.cuda.synchronize(dev)
     if world > 1:
         dist.barrier()
+    with torch.cuda.stream(capture):
+        ops.take_status(dev)
     ops.take_status(dev)
     total_ms = t0.elapsed_time(t1)
     decode_ms = [m.elapsed_time(e) for m, e in zip(mids, ends)]

@@ -93,15 +93,19 @@ int bs_paged_attention_workspace_bytes(int64_t num_heads, int64_t num_kv_heads, 
  * :155-164).  Sequence b attends over context_lens[b] tokens whose blocks are
  * block_tables[seq_rows ? seq_rows[b] : b][0 .. ceil(len / block_size)).
  * `units_hint` is the total number of (kv head, block) pairs of the batch if the
- * caller knows it, else 0; it only sizes the grid.
+ * caller knows it, else 0; it only sizes the grid.  `flags` may hold
+ * BS_LENS_READY: context_lens, block_tables and seq_rows were final before the
+ * kernel launched just ahead of this call on the stream, so the kernel's span
+ * search may overlap that kernel (query and pools are always read after it).
  */
+#define BS_LENS_READY 0x1
 int bs_paged_attention_batched(const void* query, int64_t query_seq_stride, const void* key_pool,
                                const void* value_pool, const int32_t* block_tables,
                                int64_t table_stride, int64_t table_rows, const int32_t* seq_rows,
                                const int32_t* context_lens, int64_t num_seqs, int64_t num_heads,
                                int64_t num_kv_heads, int64_t head_dim, int64_t block_size,
                                int64_t num_blocks, int64_t max_blocks_per_seq, int32_t dtype,
-                               double scaling, int64_t units_hint, void* output,
+                               double scaling, int64_t units_hint, int32_t flags, void* output,
                                int64_t output_seq_stride, void* workspace,
                                uint64_t workspace_bytes, void* stream);
 
