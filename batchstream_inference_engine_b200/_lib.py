@@ -22,6 +22,7 @@ EXPORTS = (
     "bs_paged_attention_workspace_bytes",
     "bs_paged_attention_batched",
     "bs_paged_attention_batched_workspace_bytes",
+    "bs_paged_attention_batched_noalloc",
     "bs_reshape_and_cache",
     "bs_step_metadata",
     "bs_take_status",
@@ -46,6 +47,11 @@ _SIGNATURES = {
     "bs_paged_attention_batched": (
         [_p, _i64, _p, _p, _p, _i64, _i64, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64, _i64,
          _i32, _dbl, _i64, _i32, _p, _i64, _p, _u64, _p],
+        ctypes.c_int,
+    ),
+    "bs_paged_attention_batched_noalloc": (
+        [_p, _i64, _p, _p, _p, _i64, _i64, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64, _i64,
+         _i32, _dbl, _p, _i64, _p, _p],
         ctypes.c_int,
     ),
     "bs_paged_attention_batched_workspace_bytes": (

@@ -583,3 +583,8 @@ int bs_take_status(void* workspace, void* stream, uint32_t* status_out) {
 }
 
 }  // extern "C"
+
+namespace bsb {
+// Lets other translation units of the library report through bs_last_error().
+void set_last_error(const char* message) { g_error = message; }
+}  // namespace bsb

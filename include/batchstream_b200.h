@@ -109,6 +109,34 @@ int bs_paged_attention_batched(const void* query, int64_t query_seq_stride, cons
                                int64_t output_seq_stride, void* workspace,
                                uint64_t workspace_bytes, void* stream);
 
+/*
+ * Allocation-free form of bs_paged_attention_batched.  It has no counterpart in
+ * the reference (whose op allocates its scratch on the host heap); it exists for
+ * callers that cannot allocate device memory where they run attention — a host
+ * whose device memory already belongs to a fixed pool, an FFI caller without an
+ * allocator of its own, a step that must not block on an allocation.  Its
+ * scratch is one static device array of 8 MiB per GPU, present from the moment
+ * the library's kernels load on that GPU until the process exits.  Limits: at
+ * most 16384 (sequence, kv head) pairs per call, and shapes whose partial
+ * records fit the array (on B200 the bf16 path at head_dim 64 and 128 always does);
+ * larger calls fail with BS_ERR_UNSUPPORTED and a message.  The first call on
+ * each GPU finds the array's device address and clears it (synchronising that
+ * GPU once), so make that first call before capturing a stream.  All calls share
+ * the array: calls that overlap on the GPU race, so serialise them.  Kernel-side
+ * problems (bad table entry, length or row) are OR-ed into *device_status (a
+ * device word the caller zeroes) when it is not NULL.
+ */
+int bs_paged_attention_batched_noalloc(const void* query, int64_t query_seq_stride,
+                                       const void* key_pool, const void* value_pool,
+                                       const int32_t* block_tables, int64_t table_stride,
+                                       int64_t table_rows, const int32_t* seq_rows,
+                                       const int32_t* context_lens, int64_t num_seqs,
+                                       int64_t num_heads, int64_t num_kv_heads, int64_t head_dim,
+                                       int64_t block_size, int64_t num_blocks,
+                                       int64_t max_blocks_per_seq, int32_t dtype, double scaling,
+                                       void* output, int64_t output_seq_stride,
+                                       uint32_t* device_status, void* stream);
+
 int bs_paged_attention_batched_workspace_bytes(int64_t num_seqs, int64_t num_heads,
                                                int64_t num_kv_heads, int64_t head_dim,
                                                int64_t block_size, int32_t dtype,
