@@ -126,9 +126,10 @@ __device__ __forceinline__ int64_t warp_inclusive_scan(int64_t v) {
   return v;
 }
 
-// All threads of the CTA call this.  Computes W and this CTA's span, and finds
-// the sequence holding the span's first unit.
-__device__ __forceinline__ Span compute_span(const DecodeArgs& a, ScanSmem& sm) {
+// All threads of the CTA call this.  Computes W and this CTA's span, and (when
+// find_start) finds the sequence holding the span's first unit.
+__device__ __forceinline__ Span compute_span(const DecodeArgs& a, ScanSmem& sm,
+                                             bool find_start = true) {
   const int tid = threadIdx.x, nthr = blockDim.x, lane = tid & 31, warp = tid >> 5;
   const int nwarps = (nthr + 31) >> 5;
   const int64_t C = gridDim.x, c = blockIdx.x;
@@ -160,7 +161,7 @@ __device__ __forceinline__ Span compute_span(const DecodeArgs& a, ScanSmem& sm) 
   sp.r1 = sp.r0 + sp.q + (c < sp.rem ? 1 : 0);
   sp.seq = -1;
   sp.prefix = 0;
-  if (sp.r0 >= sp.r1) return sp;
+  if (sp.r0 >= sp.r1 || !find_start) return sp;
 
   // Pass 2: chunked exclusive scan until the sequence holding r0 is found.
   int64_t carry = 0;
@@ -304,7 +305,7 @@ template <int NW>
 __device__ __forceinline__ Span compute_warp_spans(const DecodeArgs& a, ScanSmem& sm,
                                                    WarpStarts& ws) {
   static_assert(NW <= 8, "at most 8 warp spans");
-  Span sp = compute_span(a, sm);
+  Span sp = compute_span(a, sm, false);  // warp 0's start is the CTA's start
   const int tid = threadIdx.x, nthr = blockDim.x, lane = tid & 31, warp = tid >> 5;
   const int nwarps = (nthr + 31) >> 5;
   const int32_t B = a.num_seqs;
@@ -345,6 +346,9 @@ __device__ __forceinline__ Span compute_warp_spans(const DecodeArgs& a, ScanSmem
     const int64_t last_target = sp.r0 + (sp.r1 - sp.r0) * (NW - 1) / NW;
     if (carry * Hkv > last_target) break;
   }
+  sp.seq = ws.seq[0];
+  sp.prefix = ws.prefix[0];
+  if (sp.seq < 0) sp.r1 = sp.r0;  // cannot happen when r0 < W; never walk from nowhere
   return sp;
 }
 

@@ -416,18 +416,23 @@ __global__ void __launch_bounds__(Cfg<D, G16>::W * 32, Cfg<D, G16>::MIN_CTAS)
       const int k2 = holds(w2, 1, seq, kvh) ? 1 : (holds(w2, 0, seq, kvh) ? 0 : -1);
       if (k2 < 0) break;
       const float* other = slot_of(w2, k2);
-      for (int e = lane; e < G * D; e += 32) {
-        const int r = e / D;
-        const float M = fmaxf(mine[G * D + r], other[G * D + r]);
-        mine[e] = mine[e] * fast_exp2(mine[G * D + r] - M) +
-                  other[e] * fast_exp2(other[G * D + r] - M);
-      }
-      __syncwarp();
+      // Row factors once (lane r < G), then one FMA pair per element; a row
+      // spans D >= 64 elements, so elements e = lane + 32j share row (32j) / D.
+      float fa = 0.f, fb = 0.f;
       if (lane < G) {
-        const float M = fmaxf(mine[G * D + lane], other[G * D + lane]);
-        mine[G * D + G + lane] = mine[G * D + G + lane] * fast_exp2(mine[G * D + lane] - M) +
-                                 other[G * D + G + lane] * fast_exp2(other[G * D + lane] - M);
+        const float ma = mine[G * D + lane], mb = other[G * D + lane];
+        const float M = fmaxf(ma, mb);
+        fa = fast_exp2(ma - M);
+        fb = fast_exp2(mb - M);
+        mine[G * D + G + lane] = mine[G * D + G + lane] * fa + other[G * D + G + lane] * fb;
         mine[G * D + lane] = M;
+      }
+      for (int j = 0; j < G * D / 32; ++j) {
+        const int r = (32 * j) / D;
+        const float a0 = __shfl_sync(0xffffffffu, fa, r);
+        const float b0 = __shfl_sync(0xffffffffu, fb, r);
+        const int e = lane + 32 * j;
+        mine[e] = mine[e] * a0 + other[e] * b0;
       }
       __syncwarp();
       if (k2 == 1) break;  // the chain starts in that warp
