@@ -23,6 +23,8 @@ EXPORTS = (
     "bs_paged_attention_batched",
     "bs_paged_attention_batched_workspace_bytes",
     "bs_paged_attention_batched_noalloc",
+    "bs_prefill_attention",
+    "bs_prefill_attention_workspace_bytes",
     "bs_reshape_and_cache",
     "bs_step_metadata",
     "bs_take_status",
@@ -55,6 +57,14 @@ _SIGNATURES = {
         ctypes.c_int,
     ),
     "bs_paged_attention_batched_workspace_bytes": (
+        [_i64, _i64, _i64, _i64, _i64, _i32, ctypes.POINTER(_u64)], ctypes.c_int,
+    ),
+    "bs_prefill_attention": (
+        [_p, _i64, _p, _i64, _i64, _i64, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64,
+         _i64, _i64, _i32, _dbl, _i32, _p, _i64, _p, _u64, _p],
+        ctypes.c_int,
+    ),
+    "bs_prefill_attention_workspace_bytes": (
         [_i64, _i64, _i64, _i64, _i64, _i32, ctypes.POINTER(_u64)], ctypes.c_int,
     ),
     "bs_reshape_and_cache": (

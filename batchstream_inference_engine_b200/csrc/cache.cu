@@ -287,3 +287,46 @@ int launch_slot_write(const void* k, const void* v, int64_t k_stride, int64_t v_
 }
 
 }  // namespace bsb
+
+namespace bsb {
+namespace {
+
+__global__ void __launch_bounds__(256)
+    expand_rows_kernel(const int32_t* __restrict__ cu_q, const int32_t* __restrict__ context_lens,
+                       const int32_t* __restrict__ seq_rows, int32_t R, int32_t T,
+                       int32_t* __restrict__ token_lens, int32_t* __restrict__ token_rows) {
+  pdl_trigger();
+  pdl_wait();
+  const int32_t t = blockIdx.x * blockDim.x + threadIdx.x;
+  if (t >= T) return;
+  // Last row r with cu_q[r] <= t.
+  int32_t lo = 0, hi = R - 1;
+  while (lo < hi) {
+    const int32_t mid = (lo + hi + 1) >> 1;
+    if (__ldg(cu_q + mid) <= t) lo = mid; else hi = mid - 1;
+  }
+  const int32_t begin = __ldg(cu_q + lo), end = __ldg(cu_q + lo + 1);
+  if (t >= end) {  // past the last chunk: a query with no context (reported by decode)
+    token_lens[t] = 0;
+    token_rows[t] = 0;
+    return;
+  }
+  const int32_t prior = __ldg(context_lens + lo) - (end - begin);
+  token_lens[t] = prior + (t - begin) + 1;
+  token_rows[t] = seq_rows != nullptr ? __ldg(seq_rows + lo) : lo;
+}
+
+}  // namespace
+
+int launch_expand_rows(const int32_t* cu_q, const int32_t* context_lens, const int32_t* seq_rows,
+                       int32_t R, int32_t T, int32_t* token_lens, int32_t* token_rows,
+                       cudaStream_t stream) {
+  if (T <= 0) return 0;
+  cudaLaunchConfig_t cfg = pdl_config((T + 255) / 256, 256, stream);
+  cudaLaunchAttribute attr[1];
+  pdl_attr(cfg, attr);
+  return static_cast<int>(cudaLaunchKernelEx(&cfg, expand_rows_kernel, cu_q, context_lens,
+                                             seq_rows, R, T, token_lens, token_rows));
+}
+
+}  // namespace bsb

@@ -16,6 +16,7 @@
 
 #include "../../include/batchstream_b200.h"
 #include "decode.cuh"
+#include "prefill.cuh"
 
 namespace bsb {
 int max_metadata_rows();
@@ -179,6 +180,22 @@ int encode_pool_map(CUtensorMap* map, const void* base, int64_t rows, int64_t he
                   box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(BS_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", static_cast<int>(r));
+  return BS_OK;
+}
+
+// [T, H, 64] bf16 query view in boxes of (64 dims, 1 head, 128 tokens) with
+// 128-byte swizzle: one box is the query tile of one head for the prefill kernel.
+int encode_query_map(CUtensorMap* map, const void* base, int64_t tokens, int64_t heads) {
+  EncodeTiledFn fn = nullptr;
+  if (int rc = get_encode_fn(&fn)) return rc;
+  cuuint64_t dims[3] = {64, static_cast<cuuint64_t>(heads), static_cast<cuuint64_t>(tokens)};
+  cuuint64_t strides[2] = {64 * 2, static_cast<cuuint64_t>(heads * 64 * 2)};
+  cuuint32_t box[3] = {64, 1, 128};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides,
+                  box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(BS_ERR_CUDA, "cuTensorMapEncodeTiled (query) failed (%d)", static_cast<int>(r));
   return BS_OK;
 }
 
@@ -497,6 +514,149 @@ int bs_paged_attention_batched(const void* query, int64_t query_seq_stride, cons
     if (want < grid) grid = want;
   }
   return launch_decode(a, dtype, static_cast<int>(grid), static_cast<cudaStream_t>(stream));
+}
+
+int bs_prefill_attention_workspace_bytes(int64_t num_tokens, int64_t num_heads,
+                                         int64_t num_kv_heads, int64_t head_dim,
+                                         int64_t block_size, int32_t dtype, uint64_t* bytes_out) {
+  BS_CHECK(bytes_out != nullptr, "bytes_out is null");
+  BS_CHECK(num_tokens >= 0, "num_tokens must be non-negative");
+  BS_CHECK(num_kv_heads > 0 && num_heads % num_kv_heads == 0, "heads must equal kv_heads * groups");
+  const int64_t groups = num_heads / num_kv_heads;
+  int grid = 0;
+  if (int rc = decode_grid(use_mma_path(dtype, block_size, head_dim, groups), dtype, head_dim,
+                           groups, &grid))
+    return rc;
+  // The per-token path stages token lengths and rows, then runs the decode.
+  const WsLayout w = ws_layout(num_tokens * num_kv_heads, 2 * num_tokens, grid,
+                               record_stride(groups, head_dim));
+  *bytes_out = static_cast<uint64_t>(w.total);
+  return BS_OK;
+}
+
+int bs_prefill_attention(const void* query, int64_t query_token_stride, const int32_t* cu_q,
+                         int64_t num_rows, int64_t num_tokens, int64_t max_query_len,
+                         const int32_t* context_lens, const int32_t* seq_rows,
+                         const void* key_pool, const void* value_pool,
+                         const int32_t* block_tables, int64_t table_stride, int64_t table_rows,
+                         int64_t max_blocks_per_seq, int64_t num_heads, int64_t num_kv_heads,
+                         int64_t head_dim, int64_t block_size, int64_t num_blocks, int32_t dtype,
+                         double scaling, int32_t flags, void* output, int64_t output_token_stride,
+                         void* workspace, uint64_t workspace_bytes, void* stream) {
+  BS_CHECK(dtype == BS_BF16 || dtype == BS_F32, "dtype must be bfloat16 or float32");
+  BS_CHECK((flags & ~BS_PREFILL_PER_TOKEN) == 0, "unknown flags");
+  BS_CHECK(num_rows >= 0 && num_tokens >= 0 && num_tokens <= kInt32Max, "bad row or token count");
+  BS_CHECK(num_kv_heads > 0 && num_heads > 0 && num_heads % num_kv_heads == 0,
+           "heads must equal kv_heads * groups");
+  BS_CHECK(head_dim > 0 && block_size > 0 && num_blocks > 0, "sizes must be positive");
+  BS_CHECK(max_blocks_per_seq > 0 && max_blocks_per_seq <= table_stride,
+           "max_blocks_per_seq must be in [1, table_stride]");
+  BS_CHECK(table_rows > 0 && table_rows <= kInt32Max, "table_rows out of range");
+  BS_CHECK(query_token_stride >= num_heads * head_dim && output_token_stride >= num_heads * head_dim,
+           "token strides must cover heads * head_dim");
+  const int64_t groups = num_heads / num_kv_heads;
+  if (head_dim > kMaxHeadDim || groups > kMaxGroups) {
+    return fail(BS_ERR_UNSUPPORTED, "head_dim <= %lld and groups <= %lld are supported",
+                static_cast<long long>(kMaxHeadDim), static_cast<long long>(kMaxGroups));
+  }
+  if (num_kv_heads * num_blocks * block_size > kInt32Max ||
+      max_blocks_per_seq * block_size > kInt32Max) {
+    return fail(BS_ERR_UNSUPPORTED, "pool or table larger than 2^31 rows");
+  }
+  if (num_tokens * num_kv_heads > kMaxSegments) {
+    return fail(BS_ERR_UNSUPPORTED, "num_tokens * num_kv_heads must be at most %lld",
+                static_cast<long long>(kMaxSegments));
+  }
+  if (num_rows == 0 || num_tokens == 0) return BS_OK;
+  BS_CHECK(query && cu_q && context_lens && key_pool && value_pool && block_tables && output,
+           "null pointer argument");
+  BS_CHECK(max_query_len > 0, "max_query_len must be positive");
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  BS_CHECK(ws != nullptr, "workspace is null");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const bool fast = !(flags & BS_PREFILL_PER_TOKEN) && dtype == BS_BF16 && head_dim == 64 &&
+                    block_size == 16 && query_token_stride == num_heads * head_dim &&
+                    aligned16(query) && aligned16(key_pool) && aligned16(value_pool) &&
+                    (output_token_stride * 2) % 16 == 0 && aligned16(output);
+  if (fast) {
+    CUtensorMap qmap, kmap, vmap;
+    const int64_t rows = num_kv_heads * num_blocks * block_size;
+    int rc;
+    if ((rc = encode_query_map(&qmap, query, num_tokens, num_heads))) return rc;
+    if ((rc = cached_pool_map(&kmap, key_pool, rows, head_dim))) return rc;
+    if ((rc = cached_pool_map(&vmap, value_pool, rows, head_dim))) return rc;
+    bsb::PrefillArgs p{};
+    p.q = query;
+    p.out = output;
+    p.o_stride_tok = output_token_stride;
+    p.cu_q = cu_q;
+    p.context_lens = context_lens;
+    p.seq_rows = seq_rows;
+    p.block_tables = block_tables;
+    p.bt_stride = table_stride;
+    p.bt_rows = static_cast<int32_t>(table_rows);
+    p.max_blocks = static_cast<int32_t>(max_blocks_per_seq);
+    p.num_rows = static_cast<int32_t>(num_rows);
+    p.num_heads = static_cast<int32_t>(num_heads);
+    p.num_kv_heads = static_cast<int32_t>(num_kv_heads);
+    p.groups = static_cast<int32_t>(groups);
+    p.num_blocks = static_cast<int32_t>(num_blocks);
+    p.qtiles = static_cast<int32_t>((max_query_len + 127) / 128);
+    p.scale = static_cast<float>(scaling);
+    p.status = reinterpret_cast<uint32_t*>(ws);
+    const int64_t grid = num_rows * num_heads * p.qtiles;
+    if (grid > kInt32Max) return fail(BS_ERR_UNSUPPORTED, "too many query tiles");
+    rc = bsb::launch_prefill_tc(p, qmap, kmap, vmap, static_cast<int>(grid), st);
+    if (rc != 0) return cuda_fail(static_cast<cudaError_t>(rc), "prefill kernel launch");
+    return BS_OK;
+  }
+  // Per-token path: token i of a chunk is a decode query over its causal length.
+  int grid_max = 0;
+  const bool mma = use_mma_path(dtype, block_size, head_dim, groups);
+  if (int rc = decode_grid(mma, dtype, head_dim, groups, &grid_max)) return rc;
+  const WsLayout w = ws_layout(num_tokens * num_kv_heads, 2 * num_tokens, grid_max,
+                               record_stride(groups, head_dim));
+  if (workspace_bytes < static_cast<uint64_t>(w.total)) {
+    return fail(BS_ERR_WORKSPACE, "workspace of %llu bytes is smaller than the %lld needed",
+                static_cast<unsigned long long>(workspace_bytes), static_cast<long long>(w.total));
+  }
+  if (mma) {
+    BS_CHECK(aligned16(query) && aligned16(key_pool) && aligned16(value_pool) &&
+                 (query_token_stride * 2) % 16 == 0,
+             "query, pools and query rows must be 16-byte aligned");
+  }
+  int32_t* token_lens = reinterpret_cast<int32_t*>(ws + w.staging);
+  int32_t* token_rows = token_lens + num_tokens;
+  int rc = bsb::launch_expand_rows(cu_q, context_lens, seq_rows, static_cast<int32_t>(num_rows),
+                                   static_cast<int32_t>(num_tokens), token_lens, token_rows, st);
+  if (rc != 0) return cuda_fail(static_cast<cudaError_t>(rc), "prefill row expansion");
+  bsb::DecodeArgs a{};
+  a.q = query;
+  a.q_stride_seq = query_token_stride;
+  a.out = output;
+  a.o_stride_seq = output_token_stride;
+  a.k_pool = key_pool;
+  a.v_pool = value_pool;
+  a.block_tables = block_tables;
+  a.bt_stride = table_stride;
+  a.bt_rows = static_cast<int32_t>(table_rows);
+  a.seq_rows = token_rows;
+  a.context_lens = token_lens;
+  a.num_seqs = static_cast<int32_t>(num_tokens);
+  a.num_heads = static_cast<int32_t>(num_heads);
+  a.num_kv_heads = static_cast<int32_t>(num_kv_heads);
+  a.groups = static_cast<int32_t>(groups);
+  a.head_dim = static_cast<int32_t>(head_dim);
+  a.block_size = static_cast<int32_t>(block_size);
+  a.num_blocks = static_cast<int32_t>(num_blocks);
+  a.max_blocks = static_cast<int32_t>(max_blocks_per_seq);
+  a.scale = static_cast<float>(scaling);
+  a.partials = reinterpret_cast<float*>(ws + w.partials);
+  a.rec_stride = record_stride(groups, head_dim);
+  a.seg_counters = reinterpret_cast<int32_t*>(ws + w.counters);
+  a.status = reinterpret_cast<uint32_t*>(ws);
+  a.lens_ready = 0;
+  return launch_decode(a, dtype, grid_max, st);
 }
 
 int bs_reshape_and_cache(const void* key, const void* value, int64_t key_token_stride,

@@ -131,10 +131,13 @@ __global__ void __launch_bounds__(Cfg<D, G16>::W * 32, Cfg<D, G16>::MIN_CTAS)
 
   auto issue = [&](int stage) {
     const int32_t* table = a.block_tables + static_cast<int64_t>(crow) * a.bt_stride;
+    // The window caches up to 32 entries of one table row, filled to the row's
+    // width rather than this sequence's block count: sequences that share a row
+    // (the tokens of a prefill chunk) have different lengths and reuse it.
     if (win_row != crow || cb < win0 || cb >= win0 + 32) {
       win_row = crow;
       win0 = cb;
-      win_val = (cb + lane < cnb) ? __ldg(table + cb + lane) : 0;
+      win_val = (cb + lane < a.max_blocks) ? __ldg(table + cb + lane) : 0;
     }
     const int32_t blk = __shfl_sync(0xffffffffu, win_val, cb - win0);
     const bool valid = blk >= 0 && blk < a.num_blocks;
@@ -209,7 +212,9 @@ __global__ void __launch_bounds__(Cfg<D, G16>::W * 32, Cfg<D, G16>::MIN_CTAS)
   for (int32_t it = 0; it < ntiles; ++it) {
     const int stage = it % S;
     const uint32_t phase = (it / S) & 1;
-    if (!mbar_wait(&full_bar[warp][stage], phase)) {
+    // Warp-uniform outcome: a lone lane leaving here would strand the others
+    // at the warp-collective ldmatrix / mma.sync below.
+    if (!__all_sync(0xffffffffu, mbar_wait(&full_bar[warp][stage], phase))) {
       if (lane == 0) set_status(a.status, kStatusWaitTimeout);
       break;
     }

@@ -1,0 +1,34 @@
+// Chunked-prefill attention: arguments shared by the tensor-core kernel
+// (prefill.cu) and the C ABI (capi.cu).
+#pragma once
+
+#include "common.cuh"
+
+namespace bsb {
+
+struct PrefillArgs {
+  const void* q;  // [T, H, D] bf16, heads of a token contiguous
+  void* out;      // [T, H, D] bf16 (token stride o_stride_tok elements)
+  int64_t o_stride_tok;
+  const int32_t* cu_q;          // [R + 1] token offsets of the chunks
+  const int32_t* context_lens;  // [R] cached tokens after the chunk (prior + n)
+  const int32_t* seq_rows;      // [R] block-table row (may be null: row r)
+  const int32_t* block_tables;
+  int64_t bt_stride;
+  int32_t bt_rows, max_blocks;
+  int32_t num_rows, num_heads, num_kv_heads, groups, num_blocks, qtiles;
+  float scale;
+  uint32_t* status;
+};
+
+int prefill_smem_bytes();
+int launch_prefill_tc(const PrefillArgs& a, const CUtensorMap& qmap, const CUtensorMap& kmap,
+                      const CUtensorMap& vmap, int grid, cudaStream_t stream);
+
+// Per-token decode view of prefill chunks: token t of chunk r becomes a query
+// with context length (ctx[r] - n[r]) + i + 1 over block-table row rows[r].
+int launch_expand_rows(const int32_t* cu_q, const int32_t* context_lens, const int32_t* seq_rows,
+                       int32_t R, int32_t T, int32_t* token_lens, int32_t* token_rows,
+                       cudaStream_t stream);
+
+}  // namespace bsb

@@ -285,3 +285,72 @@ __all__ = [
     "dtype_code",
     "_lib",
 ]
+
+
+BS_PREFILL_PER_TOKEN = 0x2
+_prefill_ws_bytes: dict[tuple, int] = {}
+
+
+def prefill_attention(query: torch.Tensor, key_pool: torch.Tensor, value_pool: torch.Tensor,
+                      block_tables: torch.Tensor, cu_q: torch.Tensor, context_lens: torch.Tensor,
+                      scaling: float, max_query_len: int, seq_rows: torch.Tensor | None = None,
+                      out: torch.Tensor | None = None, per_token: bool = False,
+                      max_blocks_per_seq: int | None = None) -> torch.Tensor:
+    """Causal attention of prompt chunks over their paged context, in one launch.
+
+    query [T, H, D] holds the chunks back to back (chunk r is rows cu_q[r] ..
+    cu_q[r+1]); context_lens[r] counts the sequence's cached tokens including the
+    chunk (its K/V must already be in the pool).  Query token i of chunk r sees
+    keys 0 .. context_lens[r] - n_r + i — the reference's attend() with
+    _causal_mask (src/server/torch_model.py:39-55, 295-297).  bf16 at head_dim 64
+    runs on the tcgen05 tensor cores; other shapes (or per_token=True) run each
+    token as a decode query over its causal length.  Returns [T, H, D].
+    """
+    device = _require_cuda("prefill_attention", query, key_pool, value_pool, block_tables, cu_q,
+                           context_lens, seq_rows, out)
+    if query.dim() != 3 or key_pool.dim() != 4 or value_pool.shape != key_pool.shape:
+        raise RuntimeError("query must be [T, H, D] and the pools [Hkv, NB, bs, D]")
+    if query.dtype != key_pool.dtype or value_pool.dtype != key_pool.dtype:
+        raise RuntimeError("query and pools must share a dtype")
+    if not (key_pool.is_contiguous() and value_pool.is_contiguous()):
+        raise RuntimeError("pools must be contiguous")
+    for name, t in (("block_tables", block_tables), ("cu_q", cu_q), ("context_lens", context_lens)):
+        if t.dtype != torch.int32:
+            raise RuntimeError(f"{name} must be int32")
+    if seq_rows is not None and seq_rows.dtype != torch.int32:
+        raise RuntimeError("seq_rows must be int32")
+    T, H, D = query.shape
+    Hkv, NB, bs, Dk = key_pool.shape
+    if Dk != D:
+        raise RuntimeError("query and pools disagree on head_dim")
+    R = context_lens.numel()
+    if cu_q.numel() < R + 1:
+        raise RuntimeError("cu_q must hold num_rows + 1 offsets")
+    if not query.is_contiguous():
+        query = query.contiguous()
+    if block_tables.stride(1) != 1:
+        block_tables = block_tables.contiguous()
+    if out is None:
+        out = torch.empty((T, H, D), dtype=query.dtype, device=device)
+    elif out.shape != (T, H, D) or out.stride(2) != 1 or out.stride(1) != D:
+        raise RuntimeError("out must be [T, H, D] with contiguous heads")
+    mb = block_tables.size(1) if max_blocks_per_seq is None else int(max_blocks_per_seq)
+    code = dtype_code(query.dtype)
+    with torch.cuda.device(device):
+        stream = torch.cuda.current_stream(device).cuda_stream
+        key = (device.index, T, H, Hkv, D, bs, code)
+        need = _prefill_ws_bytes.get(key)
+        if need is None:
+            got = ctypes.c_uint64(0)
+            check(lib().bs_prefill_attention_workspace_bytes(T, H, Hkv, D, bs, code,
+                                                             ctypes.byref(got)))
+            need = _prefill_ws_bytes[key] = got.value
+        ws = workspace_for(device, need)
+        check(lib().bs_prefill_attention(
+            query.data_ptr(), query.stride(0), cu_q.data_ptr(), R, T, int(max_query_len),
+            context_lens.data_ptr(), seq_rows.data_ptr() if seq_rows is not None else None,
+            key_pool.data_ptr(), value_pool.data_ptr(), block_tables.data_ptr(),
+            block_tables.stride(0), block_tables.size(0), mb, H, Hkv, D, bs, NB, code,
+            float(scaling), BS_PREFILL_PER_TOKEN if per_token else 0, out.data_ptr(),
+            out.stride(0), ws.data_ptr(), ws.numel(), stream))
+    return out

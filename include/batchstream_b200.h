@@ -143,6 +143,33 @@ int bs_paged_attention_batched_workspace_bytes(int64_t num_seqs, int64_t num_hea
                                                uint64_t* bytes_out);
 
 /*
+ * Chunked-prefill attention for a ragged batch of prompt chunks, the batched
+ * form of PagedKVCache.attend's multi-token branch (_read_blocks + attend with
+ * _causal_mask, src/server/torch_model.py:39-64, 165-167, 295-297).  Chunk r has
+ * query tokens cu_q[r] .. cu_q[r+1] (rows of `query` [num_tokens, num_heads,
+ * head_dim]); its sequence holds context_lens[r] tokens after the chunk was
+ * written to the pool (the chunk's own K/V included), so query token i attends
+ * to keys 0 .. context_lens[r] - n + i.  bf16 with head_dim 64 and block size 16
+ * runs on the tcgen05 tensor cores (one CTA per chunk, head and 128-token tile;
+ * `max_query_len` bounds n); every other case, or BS_PREFILL_PER_TOKEN, runs
+ * each query token as a decode query over its own causal length.
+ */
+#define BS_PREFILL_PER_TOKEN 0x2
+int bs_prefill_attention(const void* query, int64_t query_token_stride, const int32_t* cu_q,
+                         int64_t num_rows, int64_t num_tokens, int64_t max_query_len,
+                         const int32_t* context_lens, const int32_t* seq_rows,
+                         const void* key_pool, const void* value_pool,
+                         const int32_t* block_tables, int64_t table_stride, int64_t table_rows,
+                         int64_t max_blocks_per_seq, int64_t num_heads, int64_t num_kv_heads,
+                         int64_t head_dim, int64_t block_size, int64_t num_blocks, int32_t dtype,
+                         double scaling, int32_t flags, void* output, int64_t output_token_stride,
+                         void* workspace, uint64_t workspace_bytes, void* stream);
+
+int bs_prefill_attention_workspace_bytes(int64_t num_tokens, int64_t num_heads,
+                                         int64_t num_kv_heads, int64_t head_dim,
+                                         int64_t block_size, int32_t dtype, uint64_t* bytes_out);
+
+/*
  * K/V slot write: key/value rows [num_tokens, num_kv_heads, head_dim] (token
  * stride in elements, heads contiguous) go to pool[h, slot / bs, slot % bs, :].
  * Replaces PagedKVCache.append's per-token indexed stores
