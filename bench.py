@@ -16,8 +16,19 @@ One step = one decode step of one layer for the whole batch: device metadata
 whole step, max over ranks.  Four batches with disjoint random tables rotate so
 consecutive steps read different KV blocks (888 MB footprint > 126 MB L2).
 
+Workload ``prefill_d64``: the prefill part of the mixed chunked-prefill step —
+per GPU 8 prompt chunks of 512 tokens after prior paged context drawn uniform
+in [0, 4096] (``default_rng(0)``), 14 query / 2 kv heads, head_dim 64, bf16.
+One step = device metadata -> slot write of the chunks' K/V -> chunked-prefill
+attention (tcgen05).  `value` is causal attention FLOPs
+(sum over chunks of 4 * H * D * (512 * prior + 512 * 513 / 2)) per second over
+the whole step; the roofline is the tensor pipe.  Sixteen batches with disjoint
+tables rotate (inputs larger than L2).
+
 ``--impl reference`` times the reference's own C++ op (built from its sources
-into oracle/_ref) on the host cores on a bounded sample of the same workload.
+into oracle/_ref) on the host cores on a bounded sample of the same workload;
+for ``prefill_d64`` (whose reference is torch code, not a built op) it times
+the oracle's C restatement of the reference's attend().
 """
 
 from __future__ import annotations
@@ -39,13 +50,17 @@ ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
 WORKLOADS = {
-    "decode_d64": dict(heads=14, kv_heads=2, head_dim=64),
-    "decode_d128": dict(heads=28, kv_heads=4, head_dim=128),
+    "decode_d64": dict(kind="decode", heads=14, kv_heads=2, head_dim=64),
+    "decode_d128": dict(kind="decode", heads=28, kv_heads=4, head_dim=128),
+    "prefill_d64": dict(kind="prefill", heads=14, kv_heads=2, head_dim=64),
 }
 SEQS_PER_GPU = 256
 BLOCK = 16
 ROTATIONS = 4
 POOL_FRACTION = 0.6
+PREFILL_CHUNKS = 8
+PREFILL_CHUNK = 512
+PREFILL_ROTATIONS = 16
 
 
 def parse_args():
@@ -93,6 +108,139 @@ def algorithmic_bytes(lens, heads, kv_heads, head_dim) -> int:
     blocks = sum(-(-int(n) // BLOCK) for n in lens)
     kv = 2 * kv_heads * int(np.sum(lens)) * head_dim * 2
     return kv + len(lens) * heads * head_dim * (2 + 2) + blocks * 4 + len(lens) * 4
+
+
+def prefill_priors(n_gpus: int, rank: int) -> np.ndarray:
+    """Prior context of each rank's chunks (rank 0: default_rng(0)'s first 8)."""
+    pri = np.random.default_rng(0).integers(0, 4097, PREFILL_CHUNKS * n_gpus)
+    return pri[rank * PREFILL_CHUNKS:(rank + 1) * PREFILL_CHUNKS].astype(np.int64)
+
+
+def prefill_flops(priors, heads, head_dim, n=PREFILL_CHUNK) -> int:
+    """QK^T + PV over the keys each query sees: 4 H D (n P + n (n + 1) / 2)."""
+    return sum(4 * heads * head_dim * (n * int(p) + n * (n + 1) // 2) for p in priors)
+
+
+# ------------------------------------------------------------------ shared pieces
+
+
+def setup_process():
+    """(world, rank, device); NCCL process group for N > 1 (short timeout)."""
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+    return world, rank, dev
+
+
+def measured_peak(key: str, fallback: float):
+    """(peak, note) from MEASURED_PEAKS.json, else the stated fallback."""
+    try:
+        peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text())
+    except (OSError, ValueError):
+        peaks = {}
+    if peaks.get(key):
+        return float(peaks[key]), f"measured (MEASURED_PEAKS.json {key})"
+    return fallback, f"fallback {fallback:g}"
+
+
+def capture_graphs(prep, kernel, rotations, warmup, dev):
+    """Two CUDA graphs per rotation (prep: metadata + slot write; kernel: the
+    attention launch), captured on a side stream after eager warm-up.  Returns
+    (graphs, capture stream); each entry keeps the metadata tensors its graphs
+    write and read alive."""
+    import torch
+
+    from batchstream_inference_engine_b200 import ops
+
+    stream = torch.cuda.current_stream(dev)
+    capture = torch.cuda.Stream(dev)
+    capture.wait_stream(stream)
+    with torch.cuda.stream(capture):
+        for i in range(warmup):
+            kernel(i % rotations, prep(i % rotations))
+        ops.take_status(dev)
+        graphs = []
+        for r in range(rotations):
+            ga, gb = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
+            with torch.cuda.graph(ga, stream=capture):
+                meta = prep(r)
+            with torch.cuda.graph(gb, stream=capture):
+                kernel(r, meta)
+            graphs.append((ga, gb, meta))
+        ops.take_status(dev)
+    torch.cuda.synchronize(dev)
+    return graphs, capture
+
+
+def take_all_status(capture, dev):
+    """Raises if a replayed graph (workspace of the capture stream) or an eager
+    call (current stream) recorded a device-side problem."""
+    import torch
+
+    from batchstream_inference_engine_b200 import ops
+
+    with torch.cuda.stream(capture):
+        ops.take_status(dev)
+    ops.take_status(dev)
+
+
+def timed_replays(graphs, steps, warmup, dev, world):
+    """Replays the graphs; returns (total ms, mean attention-kernel ms, clocks).
+    Events around the attention graph time the kernel on the launching stream."""
+    import torch
+    import torch.distributed as dist
+
+    stream = torch.cuda.current_stream(dev)
+    for i in range(warmup):
+        ga, gb, _ = graphs[i % len(graphs)]
+        ga.replay()
+        gb.replay()
+    mids = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    with ClockSampler(dev) as clocks:
+        t0 = torch.cuda.Event(enable_timing=True)
+        t1 = torch.cuda.Event(enable_timing=True)
+        t0.record(stream)
+        torch.cuda.nvtx.range_push("timed")
+        for i in range(steps):
+            ga, gb, _ = graphs[i % len(graphs)]
+            ga.replay()
+            mids[i].record(stream)
+            gb.replay()
+            ends[i].record(stream)
+        torch.cuda.nvtx.range_pop()
+        t1.record(stream)
+        torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+    kernel_ms = statistics.mean(m.elapsed_time(e) for m, e in zip(mids, ends))
+    return t0.elapsed_time(t1), kernel_ms, clocks.summary()
+
+
+def max_over_ranks(values, sums, dev, world):
+    """Max over ranks of `values`, sum over ranks of `sums` (floats)."""
+    import torch
+    import torch.distributed as dist
+
+    if world == 1:
+        return list(values), list(sums)
+    mx = torch.tensor(values, dtype=torch.float64, device=dev)
+    sm = torch.tensor(sums, dtype=torch.float64, device=dev)
+    dist.all_reduce(mx, op=dist.ReduceOp.MAX)
+    dist.all_reduce(sm, op=dist.ReduceOp.SUM)
+    return mx.tolist(), sm.tolist()
 
 
 # ------------------------------------------------------------------ clocks
@@ -243,22 +391,13 @@ def time_cpu(lens, heads, kv_heads, head_dim, seconds):
 # ------------------------------------------------------------------ GPU arm
 
 
-def run_ours(args):
+def run_decode(args):
     import torch
     import torch.distributed as dist
 
     from batchstream_inference_engine_b200 import ops
 
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
-    if world > 1:
-        from datetime import timedelta
-
-        dist.init_process_group("nccl", timeout=timedelta(seconds=120),
-                                device_id=dev)
+    world, rank, dev = setup_process()
     w = WORKLOADS[args.workload]
     H, Hkv, D = w["heads"], w["kv_heads"], w["head_dim"]
     all_lens = lengths_all(world)
@@ -299,73 +438,26 @@ def run_ours(args):
     units = Hkv * sum(blocks)
     scale = D ** -0.5
 
-    def step(r):
+    def prep(r):
         _, _, slots, ctx = ops.step_metadata(tables[r], start_pos, n_new, B, BLOCK, nb)
         ops.reshape_and_cache(k_new[r], v_new[r], k_pool, v_pool, slots)
-        return ctx, slots
+        return ctx
 
     def decode(r, ctx):
         ops.paged_attention_batched(q[r], k_pool, v_pool, tables[r], ctx, scale, out=out,
                                     units_hint=units)
 
     # Each step is replayed from two CUDA graphs (metadata + slot write, then the
-    # decode) so the device timings carry no host launch overhead; the events
-    # between the two graphs time the decode kernel on the launching stream.
-    stream = torch.cuda.current_stream(dev)
-    capture = torch.cuda.Stream(dev)
-    capture.wait_stream(stream)
-    with torch.cuda.stream(capture):
-        for i in range(args.warmup):
-            ctx, _ = step(i % ROTATIONS)
-            decode(i % ROTATIONS, ctx)
-        ops.take_status(dev)
-        graphs = []
-        for r in range(ROTATIONS):
-            ga, gb = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
-            with torch.cuda.graph(ga, stream=capture):
-                ctx, _ = step(r)
-            with torch.cuda.graph(gb, stream=capture):
-                decode(r, ctx)
-            graphs.append((ga, gb, ctx))
-    torch.cuda.synchronize(dev)
-    for i in range(args.warmup):
-        ga, gb, _ = graphs[i % ROTATIONS]
-        ga.replay()
-        gb.replay()
-
-    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    mids = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize(dev)
-    with ClockSampler(dev) as clocks:
-        t0 = torch.cuda.Event(enable_timing=True)
-        t1 = torch.cuda.Event(enable_timing=True)
-        t0.record(stream)
-        torch.cuda.nvtx.range_push("timed")
-        for i in range(args.steps):
-            ga, gb, _ = graphs[i % ROTATIONS]
-            starts[i].record(stream)
-            ga.replay()
-            mids[i].record(stream)
-            gb.replay()
-            ends[i].record(stream)
-        torch.cuda.nvtx.range_pop()
-        t1.record(stream)
-        torch.cuda.synchronize(dev)
-    if world > 1:
-        dist.barrier()
-    with torch.cuda.stream(capture):
-        ops.take_status(dev)
-    ops.take_status(dev)
-    total_ms = t0.elapsed_time(t1)
-    decode_ms = [m.elapsed_time(e) for m, e in zip(mids, ends)]
+    # decode) so the device timings carry no host launch overhead.
+    graphs, capture = capture_graphs(prep, decode, ROTATIONS, args.warmup, dev)
+    total_ms, decode_ms, clock = timed_replays(graphs, args.steps, args.warmup, dev, world)
+    take_all_status(capture, dev)
     step_bytes = algorithmic_bytes(lens, H, Hkv, D)
 
     # End to end through the public API from pinned host buffers: every step
     # ships q, the new K/V rows, the lengths and one table entry per sequence
     # to the device and reads the attention output back.
+    stream = torch.cuda.current_stream(dev)
     hq = q[0].cpu().pin_memory()
     hk = k_new[0].cpu().pin_memory()
     hv = v_new[0].cpu().pin_memory()
@@ -396,51 +488,18 @@ def run_ours(args):
                                     units_hint=units)
         hout.copy_(out, non_blocking=True)
 
-    for _ in range(args.warmup):
-        e2e_step()
-    torch.cuda.synchronize(dev)
-    if world > 1:
-        dist.barrier()
-    a0 = torch.cuda.Event(enable_timing=True)
-    a1 = torch.cuda.Event(enable_timing=True)
-    a0.record(stream)
-    for _ in range(args.steps):
-        e2e_step()
-    a1.record(stream)
-    torch.cuda.synchronize(dev)
-    e2e_ms = a0.elapsed_time(a1)
+    e2e_ms = time_e2e(e2e_step, args, dev, world)
     ops.take_status(dev)
 
-    times = torch.tensor([total_ms, e2e_ms, statistics.mean(decode_ms), float(step_bytes)],
-                         dtype=torch.float64, device=dev)
-    if world > 1:
-        mx = times.clone()
-        dist.all_reduce(mx, op=dist.ReduceOp.MAX)
-        bytes_all = times[3:4].clone()
-        dist.all_reduce(bytes_all, op=dist.ReduceOp.SUM)
-        total_ms, e2e_ms, decode_avg_ms = mx[0].item(), mx[1].item(), mx[2].item()
-        job_bytes = bytes_all.item()
-    else:
-        decode_avg_ms = times[2].item()
-        job_bytes = float(step_bytes)
-
+    (total_ms, e2e_ms, decode_ms), (job_bytes,) = max_over_ranks(
+        [total_ms, e2e_ms, decode_ms], [float(step_bytes)], dev, world)
     result = None
     if rank == 0:
-        peaks = {}
-        try:
-            peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text())
-        except (OSError, ValueError):
-            pass
-        peak = peaks.get("hbm_gbs")
-        peak_note = "measured" if peak else "fallback"
-        peak = peak or 6650.0
-        value = job_bytes * args.steps / (total_ms / 1e3) / 1e9
-        achieved = step_bytes / (decode_avg_ms / 1e3) / 1e9
-        e2e_value = job_bytes * args.steps / (e2e_ms / 1e3) / 1e9
-        clock = clocks.summary()
+        peak, peak_note = measured_peak("hbm_gbs", 6650.0)
+        achieved = step_bytes / (decode_ms / 1e3) / 1e9
         result = {
             "metric": "decode paged-attn HBM GB/s",
-            "value": round(value, 1),
+            "value": round(job_bytes * args.steps / (total_ms / 1e3) / 1e9, 1),
             "unit": "GB/s",
             "n_gpus": world,
             "steps": args.steps,
@@ -468,16 +527,16 @@ def run_ours(args):
                 "kernel": "decode_mma_kernel (split-K decode)",
                 "achieved": round(achieved, 1),
                 "peak": peak,
-                "peak_source": f"{peak_note} (MEASURED_PEAKS.json hbm_gbs)" if peak_note == "measured"
-                else "fallback 6650 GB/s",
+                "peak_source": peak_note,
                 "unit": "GB/s",
                 "frac": round(achieved / peak, 4),
-                "traffic": None,
-                "decode_ms": round(decode_avg_ms, 4),
+                "traffic": profiled_traffic(args.workload),
+                "decode_ms": round(decode_ms, 4),
                 "algorithmic_bytes_per_launch": step_bytes,
             },
-            "e2e": {"value": round(e2e_value, 1), "unit": "GB/s", "h2d_bytes_per_step": h2d,
-                    "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms / args.steps, 4),
+            "e2e": {"value": round(job_bytes * args.steps / (e2e_ms / 1e3) / 1e9, 1),
+                    "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                    "ms_per_step": round(e2e_ms / args.steps, 4),
                     "path": "pinned host -> device, metadata + slot write + decode, "
                             "device -> pinned host"},
             "gpu_launches": 3 * args.steps,
@@ -492,30 +551,248 @@ def run_ours(args):
         print(json.dumps(result), flush=True)
 
 
+def time_e2e(step, args, dev, world):
+    """Device time of `steps` end-to-end steps after `warmup` untimed ones."""
+    import torch
+    import torch.distributed as dist
+
+    stream = torch.cuda.current_stream(dev)
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+    a0 = torch.cuda.Event(enable_timing=True)
+    a1 = torch.cuda.Event(enable_timing=True)
+    a0.record(stream)
+    for _ in range(args.steps):
+        step()
+    a1.record(stream)
+    torch.cuda.synchronize(dev)
+    return a0.elapsed_time(a1)
+
+
+def profiled_traffic(workload: str):
+    """DRAM bytes per launch of the attention kernel from the committed ncu
+    summary of this workload (profiles/<kernel>_<workload>.md, line
+    `traffic_bytes_per_launch: N`), or None when there is none."""
+    for path in sorted((ROOT / "profiles").glob(f"*_{workload}.md")):
+        for line in path.read_text().splitlines():
+            if line.startswith("traffic_bytes_per_launch:"):
+                try:
+                    return int(line.split(":", 1)[1].strip())
+                except ValueError:
+                    return None
+    return None
+
+
+def run_prefill(args):
+    import torch
+    import torch.distributed as dist
+
+    from batchstream_inference_engine_b200 import ops
+
+    world, rank, dev = setup_process()
+    w = WORKLOADS[args.workload]
+    H, Hkv, D = w["heads"], w["kv_heads"], w["head_dim"]
+    n = PREFILL_CHUNK
+    R = PREFILL_CHUNKS
+    priors = prefill_priors(world, rank)
+    totals = priors + n
+    blocks = [-(-int(t) // BLOCK) for t in totals]
+    width = max(blocks)
+    rot = PREFILL_ROTATIONS
+    need = sum(blocks)
+    nb = need * rot + 64
+    gen = torch.Generator(device=dev).manual_seed(4321 + rank)
+    k_pool = torch.randn((Hkv, nb, BLOCK, D), generator=gen, device=dev).bfloat16()
+    v_pool = torch.randn((Hkv, nb, BLOCK, D), generator=gen, device=dev).bfloat16()
+    perm = torch.randperm(nb, device=dev, generator=gen)[: need * rot].to(torch.int32)
+    tables = []
+    for r in range(rot):
+        bt = torch.full((R, width), -1, dtype=torch.int32, device=dev)
+        cur = r * need
+        for i, m in enumerate(blocks):
+            bt[i, :m] = perm[cur: cur + m]
+            cur += m
+        tables.append(bt)
+    T = R * n
+    q = torch.randn((rot, T, H, D), generator=gen, device=dev).bfloat16()
+    k_new = torch.randn((rot, T, Hkv, D), generator=gen, device=dev).bfloat16()
+    v_new = torch.randn((rot, T, Hkv, D), generator=gen, device=dev).bfloat16()
+    start_pos = torch.tensor(priors, dtype=torch.int32, device=dev)
+    n_new = torch.full((R,), n, dtype=torch.int32, device=dev)
+    out = torch.empty((T, H, D), dtype=torch.bfloat16, device=dev)
+    scale = D ** -0.5
+
+    def prep(r):
+        cu, _, slots, ctx = ops.step_metadata(tables[r], start_pos, n_new, T, BLOCK, nb)
+        ops.reshape_and_cache(k_new[r], v_new[r], k_pool, v_pool, slots)
+        return cu, ctx
+
+    def prefill(r, meta):
+        cu, ctx = meta
+        ops.prefill_attention(q[r], k_pool, v_pool, tables[r], cu, ctx, scale,
+                              max_query_len=n, out=out)
+
+    graphs, capture = capture_graphs(prep, prefill, rot, args.warmup, dev)
+    total_ms, kernel_ms, clock = timed_replays(graphs, args.steps, args.warmup, dev, world)
+    take_all_status(capture, dev)
+    step_flops = prefill_flops(priors, H, D)
+
+    hq = q[0].cpu().pin_memory()
+    hk = k_new[0].cpu().pin_memory()
+    hv = v_new[0].cpu().pin_memory()
+    hstart = start_pos.cpu().pin_memory()
+    hout = torch.empty((T, H, D), dtype=torch.bfloat16).pin_memory()
+    dq, dk, dv = torch.empty_like(q[0]), torch.empty_like(k_new[0]), torch.empty_like(v_new[0])
+    dstart = torch.empty_like(start_pos)
+    h2d = sum(t.numel() * t.element_size() for t in (hq, hk, hv, hstart))
+    d2h = hout.numel() * hout.element_size()
+
+    def e2e_step():
+        dq.copy_(hq, non_blocking=True)
+        dk.copy_(hk, non_blocking=True)
+        dv.copy_(hv, non_blocking=True)
+        dstart.copy_(hstart, non_blocking=True)
+        cu, _, slots, ctx = ops.step_metadata(tables[0], dstart, n_new, T, BLOCK, nb)
+        ops.reshape_and_cache(dk, dv, k_pool, v_pool, slots)
+        ops.prefill_attention(dq, k_pool, v_pool, tables[0], cu, ctx, scale, max_query_len=n,
+                              out=out)
+        hout.copy_(out, non_blocking=True)
+
+    e2e_ms = time_e2e(e2e_step, args, dev, world)
+    ops.take_status(dev)
+
+    (total_ms, e2e_ms, kernel_ms), (job_flops,) = max_over_ranks(
+        [total_ms, e2e_ms, kernel_ms], [float(step_flops)], dev, world)
+    result = None
+    if rank == 0:
+        peak, peak_note = measured_peak("bf16_tflops", 1590.0)
+        achieved = step_flops / (kernel_ms / 1e3) / 1e12
+        result = {
+            "metric": "prefill paged-attn TFLOP/s",
+            "value": round(job_flops * args.steps / (total_ms / 1e3) / 1e12, 2),
+            "unit": "TFLOP/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": round(total_ms / args.steps, 4),
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "bf16",
+            "data": "synthetic (seeded priors, N(0,1) K/V/q, random block tables)",
+            "config": {
+                "workload": f"{args.workload}: {R} prompt chunks x {n} tokens per GPU after prior "
+                            f"paged context U[0, 4096], {H}q/{Hkv}kv d{D}, block 16, one layer",
+                "priors_rank0": [int(p) for p in prefill_priors(world, 0)],
+                "l2": f"inputs larger than L2: {rot} rotating batches with disjoint tables",
+                "step": "step metadata + K/V slot write + chunked-prefill attention",
+                "parallelism": f"dp{world} replicas, no collective on the path",
+            },
+            "roofline": {
+                "bound": "tensor",
+                "kernel": "prefill_kernel (tcgen05 chunked prefill)",
+                "achieved": round(achieved, 2),
+                "peak": peak,
+                "peak_source": peak_note,
+                "unit": "TFLOP/s",
+                "frac": round(achieved / peak, 4),
+                "traffic": profiled_traffic(args.workload),
+                "kernel_ms": round(kernel_ms, 4),
+                "algorithmic_flops_per_launch": step_flops,
+            },
+            "e2e": {"value": round(job_flops * args.steps / (e2e_ms / 1e3) / 1e12, 2),
+                    "unit": "TFLOP/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                    "ms_per_step": round(e2e_ms / args.steps, 4),
+                    "path": "pinned host -> device, metadata + slot write + prefill, "
+                            "device -> pinned host"},
+            "gpu_launches": 3 * args.steps,
+            "clocks": clock,
+        }
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0 and not args.no_cpu_baseline and world == 1:
+        result["cpu_baseline"] = time_cpu_prefill(priors, H, Hkv, D, args.cpu_seconds)
+    if rank == 0:
+        print(json.dumps(result), flush=True)
+
+
+def time_cpu_prefill(priors, heads, kv_heads, head_dim, seconds):
+    """Times the oracle's C restatement of the reference's prefill attend()
+    (bf16 rounding points) on the host cores, one chunk per thread (ctypes
+    releases the GIL), over rounds of the workload's chunks until `seconds`."""
+    import torch
+
+    import oracle
+
+    n = PREFILL_CHUNK
+    cores = os.cpu_count() or 1
+    g = torch.Generator().manual_seed(11)
+    cases = []
+    for p in priors:
+        total = int(p) + n
+        nb = -(-total // BLOCK)
+        table = torch.randperm(nb, generator=g).tolist()
+        bits = lambda t: t.bfloat16().view(torch.int16).numpy().view(np.uint16)
+        cases.append((bits(torch.randn(n, heads, head_dim, generator=g)),
+                      bits(torch.randn(kv_heads, nb, BLOCK, head_dim, generator=g)),
+                      bits(torch.randn(kv_heads, nb, BLOCK, head_dim, generator=g)),
+                      table, int(p)))
+    groups = heads // kv_heads
+
+    def run(case):
+        q, k, v, table, past = case
+        oracle.prefill(q, k, v, table, past, BLOCK, groups, head_dim ** -0.5)
+
+    flops = prefill_flops(priors, heads, head_dim)
+    with ThreadPoolExecutor(max_workers=min(cores, len(cases))) as pool:
+        done, rounds = 0, 0
+        start = time.perf_counter()
+        while rounds == 0 or time.perf_counter() - start < seconds:
+            list(pool.map(run, cases))
+            done += flops
+            rounds += 1
+        elapsed = time.perf_counter() - start
+    sample = (f"{rounds} round(s) of the workload's {len(cases)} chunks ({n} tokens after priors "
+              f"{min(priors)}-{max(priors)}) through the oracle's C attend(), {elapsed:.1f} s, "
+              f"{min(cores, len(cases))} threads")
+    return {"value": round(done / elapsed / 1e12, 6), "unit": "TFLOP/s",
+            "cores": min(cores, len(cases)), "kind": "port", "sample": sample}
+
+
 def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
     w = WORKLOADS[args.workload]
     H, Hkv, D = w["heads"], w["kv_heads"], w["head_dim"]
-    lens = lengths_all(1)
-    # Each step is a bounded sample of the workload (64 of its sequences, about
-    # a quarter of its KV bytes), so the whole run stays within minutes.
+    prefill = w["kind"] == "prefill"
+    # Each step is a bounded sample of the workload (decode: 64 of its sequences,
+    # about a quarter of its KV bytes; prefill: the rank's 8 chunks), so the
+    # whole run stays within minutes.
     per_step = max(1.0, min(args.cpu_seconds, 6.0) / 2)
     vals = []
     base = None
     for i in range(args.warmup + args.steps):
-        res = time_cpu(lens, H, Hkv, D, per_step if i >= args.warmup else 0.2)
+        seconds = per_step if i >= args.warmup else 0.2
+        if prefill:
+            res = time_cpu_prefill(prefill_priors(1, 0), H, Hkv, D, seconds)
+        else:
+            res = time_cpu(lengths_all(1), H, Hkv, D, seconds)
         if i >= args.warmup:
             vals.append(res["value"])
             base = res
     value = statistics.median(vals)
     base["value"] = value
+    unit = base["unit"]
     print(json.dumps({
-        "metric": "decode paged-attn HBM GB/s",
+        "metric": "prefill paged-attn TFLOP/s" if prefill else "decode paged-attn HBM GB/s",
         "impl": "reference",
         "value": value,
-        "unit": "GB/s",
+        "unit": unit,
         "n_gpus": args.gpus,
         "steps": args.steps,
         "warmup": args.warmup,
@@ -523,19 +800,25 @@ def run_reference(args):
         "scaling": "weak",
         "vs_baseline": None,
         "dtype": "bf16",
-        "data": "synthetic (seeded lognormal lengths, N(0,1) K/V/q)",
-        "config": {"workload": f"{args.workload}: reference C++ op per sequence on host cores"},
+        "data": "synthetic (seeded priors, N(0,1) K/V/q)" if prefill
+        else "synthetic (seeded lognormal lengths, N(0,1) K/V/q)",
+        "config": {"workload": f"{args.workload}: " + (
+            "oracle C restatement of the reference attend() per chunk on host cores" if prefill
+            else "reference C++ op per sequence on host cores")},
         "cpu_baseline": base,
-        "e2e": {"value": value, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "e2e": {"value": value, "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }), flush=True)
 
 
 def main():
     args = parse_args()
+    kind = WORKLOADS[args.workload]["kind"]
     if args.impl == "reference":
         run_reference(args)
+    elif kind == "prefill":
+        run_prefill(args)
     else:
-        run_ours(args)
+        run_decode(args)
 
 
 if __name__ == "__main__":
