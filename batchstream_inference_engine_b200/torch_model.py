@@ -1,0 +1,359 @@
+"""The paged-backend model step on the GPU: the reference's TorchModel with its
+per-sequence attention loop replaced by one batched call per layer.
+
+Mirrors src/server/torch_model.py: ``ModelConfig`` (:13-36), ``PagedKVPool`` /
+``PagedKVCache`` (:115-170) and ``TorchModel`` (:195-297), with the same layer
+maths and rounding points (bf16 rotary tables, fp32 RMSNorm statistics cast back
+to the hidden dtype, SwiGLU MLP, tied output embedding).  What changes is where
+the work runs and how a step is assembled (``_hidden_states`` :231-247):
+
+* block tables and context lengths live on the device
+  (``BlockAllocator(device=...)``), and one ``step_metadata`` launch derives the
+  ragged-batch metadata (chunk offsets, positions, slot mapping, context
+  lengths) that the reference rebuilt in Python every step;
+* each layer writes the step's K/V rows with one ``reshape_and_cache`` launch
+  (PagedKVCache.append, :149-153) and attends with one batched decode launch for
+  the single-token rows plus one chunked-prefill launch for the prompt chunks
+  (PagedKVCache.attend, :155-167), instead of 2 x B Python-level calls;
+* the last-token logits are reduced to greedy token ids on the device
+  (PagedBackend._next_output, backend/paged.py:95-99), so only B ints cross
+  PCIe per step.
+
+The projections and the MLP are plain library GEMMs (cuBLAS through torch);
+the attention, the slot write and the metadata are this package's kernels.
+"""
+
+from __future__ import annotations
+
+import json
+import struct
+from dataclasses import dataclass
+from pathlib import Path
+
+import torch
+import torch.nn.functional as F
+
+from . import ops
+from .block_allocator import BlockAllocator
+
+
+@dataclass(frozen=True)
+class ModelConfig:
+    """src/server/torch_model.py:13-36 (the same fields and head_dim rule)."""
+
+    num_layers: int
+    hidden_size: int
+    num_heads: int
+    num_kv_heads: int
+    rope_theta: float
+    rms_norm_eps: float
+
+    @classmethod
+    def from_file(cls, path: Path) -> "ModelConfig":
+        config = json.loads(Path(path).read_text())
+        return cls(
+            num_layers=config["num_hidden_layers"],
+            hidden_size=config["hidden_size"],
+            num_heads=config["num_attention_heads"],
+            num_kv_heads=config["num_key_value_heads"],
+            rope_theta=config["rope_theta"],
+            rms_norm_eps=config["rms_norm_eps"],
+        )
+
+    @property
+    def head_dim(self) -> int:
+        return self.hidden_size // self.num_heads
+
+
+# The Qwen2.5-0.5B shape (24 layers, hidden 896, 14 / 2 heads, head_dim 64).
+QWEN25_05B = ModelConfig(num_layers=24, hidden_size=896, num_heads=14, num_kv_heads=2,
+                         rope_theta=1_000_000.0, rms_norm_eps=1e-6)
+QWEN25_05B_VOCAB = 151936
+QWEN25_05B_INTERMEDIATE = 4864
+
+
+def weight_names(config: ModelConfig) -> list[str]:
+    """Parameter names in checkpoint order (the reference's key names)."""
+    names = ["model.embed_tokens.weight"]
+    for layer in range(config.num_layers):
+        p = f"model.layers.{layer}."
+        names += [p + "input_layernorm.weight"]
+        for proj in ("q_proj", "k_proj", "v_proj"):
+            names += [p + f"self_attn.{proj}.weight", p + f"self_attn.{proj}.bias"]
+        names += [p + "self_attn.o_proj.weight", p + "post_attention_layernorm.weight",
+                  p + "mlp.gate_proj.weight", p + "mlp.up_proj.weight", p + "mlp.down_proj.weight"]
+    names.append("model.norm.weight")
+    return names
+
+
+def weight_shapes(config: ModelConfig, vocab_size: int, intermediate_size: int) -> dict[str, tuple]:
+    hidden, kv = config.hidden_size, config.num_kv_heads * config.head_dim
+    shapes = {"model.embed_tokens.weight": (vocab_size, hidden), "model.norm.weight": (hidden,)}
+    for layer in range(config.num_layers):
+        p = f"model.layers.{layer}."
+        shapes.update({
+            p + "input_layernorm.weight": (hidden,),
+            p + "post_attention_layernorm.weight": (hidden,),
+            p + "self_attn.q_proj.weight": (hidden, hidden), p + "self_attn.q_proj.bias": (hidden,),
+            p + "self_attn.k_proj.weight": (kv, hidden), p + "self_attn.k_proj.bias": (kv,),
+            p + "self_attn.v_proj.weight": (kv, hidden), p + "self_attn.v_proj.bias": (kv,),
+            p + "self_attn.o_proj.weight": (hidden, hidden),
+            p + "mlp.gate_proj.weight": (intermediate_size, hidden),
+            p + "mlp.up_proj.weight": (intermediate_size, hidden),
+            p + "mlp.down_proj.weight": (hidden, intermediate_size),
+        })
+    return shapes
+
+
+def random_weights(config: ModelConfig = QWEN25_05B, vocab_size: int = QWEN25_05B_VOCAB,
+                   intermediate_size: int = QWEN25_05B_INTERMEDIATE, seed: int = 0,
+                   std: float = 0.02) -> dict[str, torch.Tensor]:
+    """Random-init fp32 CPU weights: every matrix, the embedding and every bias
+    N(0, std) drawn from one ``torch.Generator`` seeded ``seed`` in checkpoint
+    order (``weight_names``); RMSNorm weights are 1."""
+    g = torch.Generator().manual_seed(seed)
+    shapes = weight_shapes(config, vocab_size, intermediate_size)
+    weights = {}
+    for name in weight_names(config):
+        if name.endswith("norm.weight"):
+            weights[name] = torch.ones(shapes[name])
+        else:
+            weights[name] = torch.randn(shapes[name], generator=g) * std
+    return weights
+
+
+def load_safetensors(path: Path) -> dict[str, torch.Tensor]:
+    """BF16 safetensors reader (the checkpoint format the reference loads,
+    src/server/torch_model.py:173-187)."""
+    data = bytearray(Path(path).read_bytes())
+    header_size = struct.unpack_from("<Q", data)[0]
+    header = json.loads(data[8: 8 + header_size])
+    header.pop("__metadata__", None)
+    weights = {}
+    for name, entry in header.items():
+        if entry["dtype"] != "BF16":
+            raise ValueError(f"{name} has unsupported dtype {entry['dtype']}")
+        start, end = entry["data_offsets"]
+        tensor = torch.frombuffer(data, dtype=torch.bfloat16, count=(end - start) // 2,
+                                  offset=8 + header_size + start)
+        weights[name] = tensor.reshape(entry["shape"])
+    return weights
+
+
+class PagedKVPool:
+    """Device-resident K/V pool [layers, kv_heads, blocks, block_size, head_dim]
+    with the reference's allocator and a device mirror of its block tables
+    (src/server/torch_model.py:115-137).  ``dtype`` is bf16 as in the reference;
+    fp32 pools serve fp32 parity runs."""
+
+    def __init__(self, config: ModelConfig, num_blocks: int, block_size: int,
+                 device: torch.device | str = "cuda", dtype: torch.dtype = torch.bfloat16,
+                 max_seqs: int = 256, max_blocks_per_seq: int | None = None):
+        self.device = torch.device(device)
+        shape = (config.num_layers, config.num_kv_heads, num_blocks, block_size, config.head_dim)
+        self.keys = torch.zeros(shape, dtype=dtype, device=self.device)
+        self.values = torch.zeros(shape, dtype=dtype, device=self.device)
+        self.block_size = block_size
+        self.num_blocks = num_blocks
+        self.allocator = BlockAllocator(num_blocks, block_size, max_seqs=max_seqs,
+                                        max_blocks_per_seq=max_blocks_per_seq or num_blocks,
+                                        device=self.device)
+
+    @property
+    def free_blocks(self) -> int:
+        return self.allocator.free_blocks
+
+    def block_table(self, seq_id: int) -> list[int]:
+        return self.allocator.block_table(seq_id)
+
+    def new_cache(self, seq_id: int) -> "PagedKVCache":
+        return PagedKVCache(self, seq_id)
+
+    def release(self, cache: "PagedKVCache") -> None:
+        self.allocator.free(cache.seq_id)
+
+
+class PagedKVCache:
+    """One sequence's view of the pool (src/server/torch_model.py:140-170).  The
+    K/V writes and attention of a step are batched by ``TorchModel``; the cache
+    keeps the length bookkeeping."""
+
+    def __init__(self, pool: PagedKVPool, seq_id: int):
+        self._pool = pool
+        self.seq_id = seq_id
+        self.length = 0
+
+    def reserve(self, count: int) -> None:
+        self._pool.allocator.allocate(self.seq_id, self.length + count)
+
+    def advance(self, count: int) -> None:
+        self.length += count
+
+
+class TorchModel:
+    """The reference TorchModel (src/server/torch_model.py:195-297) on one GPU,
+    over a ``PagedKVPool`` on the same device.  ``dtype`` is the compute dtype
+    of the hidden states and weights (bf16 as the checkpoint, or fp32)."""
+
+    def __init__(self, config: ModelConfig, weights: dict[str, torch.Tensor],
+                 device: torch.device | str = "cuda", dtype: torch.dtype = torch.bfloat16,
+                 max_position: int = 32768):
+        self.config = config
+        self.device = torch.device(device)
+        self.dtype = dtype
+        w = {k: v.to(device=self.device, dtype=dtype) for k, v in weights.items()}
+        self.embed = w["model.embed_tokens.weight"]
+        self.final_norm = w["model.norm.weight"]
+        self.layers = []
+        for layer in range(config.num_layers):
+            p = f"model.layers.{layer}."
+            a = p + "self_attn."
+            self.layers.append(dict(
+                ln1=w[p + "input_layernorm.weight"],
+                ln2=w[p + "post_attention_layernorm.weight"],
+                # Q, K and V share one GEMM; gate and up share another.
+                qkv_w=torch.cat([w[a + "q_proj.weight"], w[a + "k_proj.weight"],
+                                 w[a + "v_proj.weight"]]).contiguous(),
+                qkv_b=torch.cat([w[a + "q_proj.bias"], w[a + "k_proj.bias"],
+                                 w[a + "v_proj.bias"]]).contiguous(),
+                o_w=w[a + "o_proj.weight"],
+                gate_up_w=torch.cat([w[p + "mlp.gate_proj.weight"],
+                                     w[p + "mlp.up_proj.weight"]]).contiguous(),
+                down_w=w[p + "mlp.down_proj.weight"],
+            ))
+        self.intermediate_size = self.layers[0]["down_w"].shape[1] if self.layers else 0
+        self.vocab_size = self.embed.shape[0]
+        # Rotary tables exactly as the reference makes them (fp32 angles on the
+        # CPU, cos/sin rounded to bf16, torch_model.py:199-200, 289-292), built
+        # once for every position and gathered per step on the device.
+        steps = torch.arange(0, config.head_dim, 2, dtype=torch.float)
+        inverse_frequencies = 1.0 / (config.rope_theta ** (steps / config.head_dim))
+        positions = torch.arange(max_position)
+        frequencies = positions[:, None].float() * inverse_frequencies
+        angles = torch.cat((frequencies, frequencies), dim=-1)
+        self.cos = angles.cos().to(torch.bfloat16).to(device=self.device, dtype=dtype)
+        self.sin = angles.sin().to(torch.bfloat16).to(device=self.device, dtype=dtype)
+        self.max_position = max_position
+        self._host = None  # pinned staging buffer for per-step row metadata
+        self._host_free = None  # event: the last copy out of it has completed
+
+    @classmethod
+    def load(cls, model_dir: Path, device="cuda", dtype=torch.bfloat16) -> "TorchModel":
+        model_dir = Path(model_dir)
+        config = ModelConfig.from_file(model_dir / "config.json")
+        return cls(config, load_safetensors(model_dir / "model.safetensors"), device, dtype)
+
+    # ---------------------------------------------------------------- public
+
+    @torch.inference_mode()
+    def forward_batch(self, groups: list[tuple[list[int], PagedKVCache]]) -> torch.Tensor:
+        """Each (tokens, cache) pair's last-token logits [B, vocab] on the device
+        (torch_model.py:223-229)."""
+        last = self._last_hidden(groups)
+        return F.linear(last, self.embed)
+
+    @torch.inference_mode()
+    def next_tokens(self, groups: list[tuple[list[int], PagedKVCache]]) -> list[int]:
+        """Greedy next token of each group: argmax of the float last-token
+        logits (first index on ties), reduced on the device."""
+        logits = self.forward_batch(groups)
+        ids = logits.float().argmax(dim=-1).to(torch.int32)
+        host = torch.empty(ids.shape, dtype=torch.int32, pin_memory=True)
+        host.copy_(ids, non_blocking=True)
+        torch.cuda.current_stream(self.device).synchronize()
+        ops.take_status(self.device)
+        return host.tolist()
+
+    # ---------------------------------------------------------------- step
+
+    def _stage(self, values: list[int]) -> torch.Tensor:
+        """One pinned host buffer -> one H2D copy of the step's int32 metadata."""
+        n = len(values)
+        if self._host_free is not None:
+            self._host_free.synchronize()  # the previous step's copy has left the buffer
+        if self._host is None or self._host.numel() < n:
+            self._host = torch.empty(max(n, 1024) * 2, dtype=torch.int32, pin_memory=True)
+        self._host[:n] = torch.tensor(values, dtype=torch.int32)
+        staged = self._host[:n].to(self.device, non_blocking=True)
+        self._host_free = torch.cuda.Event()
+        self._host_free.record(torch.cuda.current_stream(self.device))
+        return staged
+
+    def _last_hidden(self, groups) -> torch.Tensor:
+        config = self.config
+        pool = groups[0][1]._pool
+        for tokens, cache in groups:
+            cache.reserve(len(tokens))
+        alloc = pool.allocator
+        alloc.sync_device()
+        R = len(groups)
+        lengths = [len(tokens) for tokens, _ in groups]
+        T = sum(lengths)
+        starts = [cache.length for _, cache in groups]
+        if max(s + n for s, n in zip(starts, lengths)) > self.max_position:
+            raise RuntimeError(f"positions beyond the rotary table ({self.max_position})")
+        rows = [alloc.row(cache.seq_id) for _, cache in groups]
+        flat = [t for tokens, _ in groups for t in tokens]
+        ends = [sum(lengths[: i + 1]) - 1 for i in range(R)]
+        staged = self._stage(rows + starts + lengths + ends + flat)
+        rows_d, start_d, n_d, ends_d, tokens_d = (staged[:R], staged[R:2 * R],
+                                                  staged[2 * R:3 * R], staged[3 * R:4 * R],
+                                                  staged[4 * R:])
+        cu_q, positions, slots, ctx = ops.step_metadata(
+            alloc.device_tables, start_d, n_d, T, pool.block_size, pool.num_blocks,
+            seq_rows=rows_d)
+        # Leading single-token rows run through the batched decode kernel, the
+        # rest (prompt chunks) through the chunked-prefill kernel.
+        n_dec = 0
+        while n_dec < R and lengths[n_dec] == 1:
+            n_dec += 1
+        max_chunk = max(lengths[n_dec:], default=0)
+        pre_cu = (cu_q[n_dec:] - n_dec) if n_dec < R else None
+
+        hidden = self.embed.index_select(0, tokens_d.long())
+        cos = self.cos.index_select(0, positions.long())
+        sin = self.sin.index_select(0, positions.long())
+        H, Hkv, D = config.num_heads, config.num_kv_heads, config.head_dim
+        scaling = D ** -0.5
+        for layer, lw in enumerate(self.layers):
+            normed = self._rms_norm(hidden, lw["ln1"])
+            qkv = F.linear(normed, lw["qkv_w"], lw["qkv_b"])
+            q = qkv[:, : H * D].view(T, H, D)
+            k = qkv[:, H * D: (H + Hkv) * D].view(T, Hkv, D)
+            v = qkv[:, (H + Hkv) * D:].view(T, Hkv, D)
+            q = q * cos[:, None] + _rotate_half(q) * sin[:, None]
+            k = k * cos[:, None] + _rotate_half(k) * sin[:, None]
+            kp, vp = pool.keys[layer], pool.values[layer]
+            ops.reshape_and_cache(k, v, kp, vp, slots)
+            attended = torch.empty((T, H, D), dtype=q.dtype, device=self.device)
+            if n_dec:
+                ops.paged_attention_batched(q[:n_dec], kp, vp, alloc.device_tables, ctx[:n_dec],
+                                            scaling, seq_rows=rows_d[:n_dec],
+                                            out=attended[:n_dec])
+            if n_dec < R:
+                ops.prefill_attention(q[n_dec:], kp, vp, alloc.device_tables, pre_cu,
+                                      ctx[n_dec:], scaling, max_query_len=max_chunk,
+                                      seq_rows=rows_d[n_dec:], out=attended[n_dec:])
+            hidden = hidden + F.linear(attended.view(T, H * D), lw["o_w"])
+            normed = self._rms_norm(hidden, lw["ln2"])
+            gate_up = F.linear(normed, lw["gate_up_w"])
+            gate, up = gate_up.split(self.intermediate_size, dim=-1)
+            hidden = hidden + F.linear(F.silu(gate) * up, lw["down_w"])
+        for (tokens, cache) in groups:
+            cache.advance(len(tokens))
+        return self._rms_norm(hidden.index_select(0, ends_d.long()), self.final_norm)
+
+    def _rms_norm(self, hidden: torch.Tensor, weight: torch.Tensor) -> torch.Tensor:
+        wide = hidden.to(torch.float32)
+        variance = wide.pow(2).mean(-1, keepdim=True)
+        normalized = wide * torch.rsqrt(variance + self.config.rms_norm_eps)
+        return weight * normalized.to(hidden.dtype)
+
+
+def _rotate_half(x: torch.Tensor) -> torch.Tensor:
+    first, second = x.chunk(2, dim=-1)
+    return torch.cat((-second, first), dim=-1)
+
+
+__all__ = ["ModelConfig", "PagedKVPool", "PagedKVCache", "TorchModel", "QWEN25_05B",
+           "random_weights", "weight_names", "load_safetensors"]

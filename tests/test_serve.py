@@ -1,0 +1,147 @@
+"""Host logic of the GPU backend and the offline scheduler, on the CPU with a
+fake model (no kernels): batch composition (backend/paged.py:60-99), admission
+and completion (scheduler.py:112-163), block budgets (kv_budget.py:19-36)."""
+
+import pytest
+import torch
+
+from batchstream_inference_engine_b200.backend import PagedBackend, QwenIds, StepOutput
+from batchstream_inference_engine_b200.serve import BlockBudget, Request, engine_workload, serve
+from batchstream_inference_engine_b200.torch_model import ModelConfig
+
+TINY = ModelConfig(num_layers=1, hidden_size=8, num_heads=2, num_kv_heads=1, rope_theta=1e4,
+                   rms_norm_eps=1e-6)
+
+
+class FakeModel:
+    """Records each step's (seq_id, tokens) rows; the next token of a row is
+    1000 + its sequence's cache length after the step (deterministic)."""
+
+    def __init__(self, eog_at=None):
+        self.config = TINY
+        self.device = torch.device("cpu")
+        self.dtype = torch.float32
+        self.max_position = 4096
+        self.steps = []
+        self.eog_at = eog_at or {}
+
+    def next_tokens(self, groups):
+        self.steps.append([(cache.seq_id, list(tokens)) for tokens, cache in groups])
+        out = []
+        for tokens, cache in groups:
+            cache.reserve(len(tokens))
+            cache.advance(len(tokens))
+            out.append(self.eog_at.get((cache.seq_id, cache.length), 1000 + cache.length))
+        return out
+
+
+def make_backend(model=None, num_blocks=64, prefill_chunk=8):
+    return PagedBackend(model or FakeModel(), num_blocks, 16, prefill_chunk)
+
+
+def test_generating_rows_come_first_then_chunks_under_the_budget():
+    model = FakeModel()
+    b = make_backend(model, prefill_chunk=8)
+    a = b.start_sequence(list(range(5)))
+    c = b.start_sequence(list(range(10, 22)))
+    out = b.step()
+    # Budget 8: all 5 of a, 3 of c; only a is done with its prompt.
+    assert model.steps[-1] == [(a, [0, 1, 2, 3, 4]), (c, [10, 11, 12])]
+    assert out == {a: StepOutput(1005, False)}
+    out = b.step()
+    # a generates first, then c's next 8 prompt tokens.
+    assert model.steps[-1] == [(a, [1005]), (c, [13, 14, 15, 16, 17, 18, 19, 20])]
+    assert out == {a: StepOutput(1006, False)}
+    out = b.step()
+    assert model.steps[-1] == [(a, [1006]), (c, [21])]
+    assert out == {a: StepOutput(1007, False), c: StepOutput(1012, False)}
+
+
+def test_end_of_generation_stops_a_sequence():
+    model = FakeModel(eog_at={(0, 4): 151645})
+    b = make_backend(model)
+    s = b.start_sequence([1, 2, 3])
+    assert b.step() == {s: StepOutput(1003, False)}
+    assert b.step() == {s: StepOutput(151645, True)}
+    assert b.step() == {}
+    b.release_sequence(s)
+    assert b.blocks_in_use == 0
+
+
+def test_blocks_follow_the_reference_allocator():
+    b = make_backend()
+    s = b.start_sequence(list(range(40)))
+    for _ in range(5):
+        b.step()
+    # 40 prompt tokens + 1 generated (the last step's token is not cached yet).
+    assert b.pool.block_table(s) == [63, 62, 61]
+    b.release_sequence(s)
+    assert b.pool.allocator._free[-3:] == [63, 62, 61]
+
+
+def test_serve_admits_in_order_up_to_the_limit_and_completes_at_max_tokens():
+    model = FakeModel()
+    b = make_backend(model, num_blocks=64, prefill_chunk=64)
+    specs = [([1] * 5, 3), ([2] * 5, 2), ([3] * 5, 4)]
+    requests = serve(b, specs, max_concurrent=2, budget=BlockBudget(64, 16))
+    assert [len(r.tokens) for r in requests] == [3, 2, 4]
+    assert all(r.done and not r.failed for r in requests)
+    # The third request waits until one of the first two completes.
+    first_rows = [sid for sid, _ in model.steps[0]]
+    assert first_rows == [0, 1]
+    assert b.blocks_in_use == 0
+
+
+def test_serve_holds_the_head_until_the_budget_fits():
+    model = FakeModel()
+    b = make_backend(model, num_blocks=4, prefill_chunk=64)
+    # Each request reserves ceil((prompt + max_tokens) / 16) blocks: 3, then 2.
+    specs = [([1] * 30, 10), ([2] * 10, 10)]
+    requests = serve(b, specs, max_concurrent=8, budget=BlockBudget(4, 16))
+    assert all(r.done for r in requests)
+    # Never both active: the second only starts after the first completed.
+    assert all(len(step) == 1 for step in model.steps)
+
+
+def test_serve_fails_every_active_request_on_a_step_error():
+    class Broken(FakeModel):
+        def next_tokens(self, groups):
+            raise RuntimeError("device-side status")
+
+    b = make_backend(Broken())
+    requests = serve(b, [([1, 2], 4), ([3], 4)], max_concurrent=8, budget=BlockBudget(64, 16))
+    assert all(r.failed and r.done for r in requests)
+    assert b.blocks_in_use == 0
+
+
+def test_budget_rounds_to_blocks():
+    budget = BlockBudget(10, 16)
+    assert budget.fits_ever(160) and not budget.fits_ever(161)
+    assert budget.try_reserve(17) and budget.available == 8
+    budget.release(17)
+    assert budget.available == 10
+
+
+def test_request_too_large_is_rejected():
+    with pytest.raises(RuntimeError):
+        serve(make_backend(), [([1] * 100, 100)], 8, BlockBudget(4, 16))
+
+
+def test_engine_workload_shape():
+    specs = engine_workload()
+    assert len(specs) == 24
+    assert all(4 <= len(p) <= 277 and 16 <= m <= 128 for p, m in specs)
+    assert all(0 <= t < 151936 for p, _ in specs for t in p)
+    assert engine_workload() == specs
+
+
+def test_qwen_ids_vocabulary():
+    v = QwenIds()
+    assert v.is_end_of_generation(151643) and v.is_end_of_generation(151645)
+    assert not v.is_end_of_generation(0)
+    with pytest.raises(RuntimeError):
+        v.tokenize("text")
+
+
+def test_request_kv_tokens():
+    assert Request([1, 2, 3], 5).kv_tokens == 8
