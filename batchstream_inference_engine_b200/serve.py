@@ -56,44 +56,66 @@ class Request:
         return len(self.prompt_tokens) + self.max_tokens
 
 
-def serve(backend, specs, max_concurrent: int, budget: BlockBudget, on_step=None) -> list[Request]:
-    """Runs every (prompt_tokens, max_tokens) in ``specs`` to completion and
-    returns the requests in submission order.  ``on_step(outputs)`` is called
-    after each backend step."""
-    requests = [Request(list(p), int(m)) for p, m in specs]
-    for r in requests:
-        if not budget.fits_ever(r.kv_tokens):
-            raise RuntimeError("request can never fit in the KV budget")
-    waiting = deque(requests)
-    active: dict[int, Request] = {}
+class OfflineScheduler:
+    """One turn of the loop per ``step()``: admit, run one backend step, record
+    and complete.  ``idle`` once every request is done."""
 
-    def complete(seq_id: int, request: Request) -> None:
-        del active[seq_id]
-        budget.release(request.kv_tokens)
-        backend.release_sequence(seq_id)
+    def __init__(self, backend, specs, max_concurrent: int, budget: BlockBudget):
+        self.backend = backend
+        self.max_concurrent = max_concurrent
+        self.budget = budget
+        self.requests = [Request(list(p), int(m)) for p, m in specs]
+        for r in self.requests:
+            if not budget.fits_ever(r.kv_tokens):
+                raise RuntimeError("request can never fit in the KV budget")
+        self.waiting = deque(self.requests)
+        self.active: dict[int, Request] = {}
+
+    @property
+    def idle(self) -> bool:
+        return not self.waiting and not self.active
+
+    def _complete(self, seq_id: int, request: Request) -> None:
+        del self.active[seq_id]
+        self.budget.release(request.kv_tokens)
+        self.backend.release_sequence(seq_id)
         request.done = True
 
-    while waiting or active:
-        while waiting and len(active) < max_concurrent and budget.try_reserve(waiting[0].kv_tokens):
-            request = waiting.popleft()
-            active[backend.start_sequence(request.prompt_tokens)] = request
-        if not active:
-            raise RuntimeError("the budget cannot admit the next request")
+    def step(self) -> dict[int, int]:
+        """Returns {seq_id: token} of the step (empty when idle)."""
+        while (self.waiting and len(self.active) < self.max_concurrent
+               and self.budget.try_reserve(self.waiting[0].kv_tokens)):
+            request = self.waiting.popleft()
+            self.active[self.backend.start_sequence(request.prompt_tokens)] = request
+        if not self.active:
+            if self.waiting:
+                raise RuntimeError("the budget cannot admit the next request")
+            return {}
         try:
-            outputs = backend.step()
+            outputs = self.backend.step()
         except RuntimeError:
-            for seq_id, request in list(active.items()):
+            for seq_id, request in list(self.active.items()):
                 request.failed = True
-                complete(seq_id, request)
-            continue
-        if on_step is not None:
-            on_step(outputs)
+                self._complete(seq_id, request)
+            return {}
         for seq_id, output in outputs.items():
-            request = active[seq_id]
+            request = self.active[seq_id]
             request.tokens.append(output.token)
             if output.finished or len(request.tokens) >= request.max_tokens:
-                complete(seq_id, request)
-    return requests
+                self._complete(seq_id, request)
+        return {seq_id: output.token for seq_id, output in outputs.items()}
+
+
+def serve(backend, specs, max_concurrent: int, budget: BlockBudget, on_step=None) -> list[Request]:
+    """Runs every (prompt_tokens, max_tokens) in ``specs`` to completion and
+    returns the requests in submission order.  ``on_step(tokens)`` is called
+    after each backend step with its {seq_id: token}."""
+    scheduler = OfflineScheduler(backend, specs, max_concurrent, budget)
+    while not scheduler.idle:
+        tokens = scheduler.step()
+        if on_step is not None:
+            on_step(tokens)
+    return scheduler.requests
 
 
 def engine_workload(num_requests: int = 24, seed: int = 0, vocab_size: int = 151936,

@@ -234,6 +234,11 @@ class TorchModel:
         self.cos = angles.cos().to(torch.bfloat16).to(device=self.device, dtype=dtype)
         self.sin = angles.sin().to(torch.bfloat16).to(device=self.device, dtype=dtype)
         self.max_position = max_position
+        # Per-step accounting for benchmarks: forwards, tokens and rows
+        # processed, attention FLOPs (QK^T + PV over visible keys), launches of
+        # this package's kernels, bytes copied host->device and device->host.
+        self.stats = dict(steps=0, tokens=0, rows=0, attn_flops=0, launches=0, h2d_bytes=0,
+                          d2h_bytes=0)
         self._host = None  # pinned staging buffer for per-step row metadata
         self._host_free = None  # event: the last copy out of it has completed
 
@@ -260,6 +265,7 @@ class TorchModel:
         ids = logits.float().argmax(dim=-1).to(torch.int32)
         host = torch.empty(ids.shape, dtype=torch.int32, pin_memory=True)
         host.copy_(ids, non_blocking=True)
+        self.stats["d2h_bytes"] += 4 * ids.numel()
         torch.cuda.current_stream(self.device).synchronize()
         ops.take_status(self.device)
         return host.tolist()
@@ -275,6 +281,7 @@ class TorchModel:
             self._host = torch.empty(max(n, 1024) * 2, dtype=torch.int32, pin_memory=True)
         self._host[:n] = torch.tensor(values, dtype=torch.int32)
         staged = self._host[:n].to(self.device, non_blocking=True)
+        self.stats["h2d_bytes"] += 4 * n
         self._host_free = torch.cuda.Event()
         self._host_free.record(torch.cuda.current_stream(self.device))
         return staged
@@ -285,7 +292,7 @@ class TorchModel:
         for tokens, cache in groups:
             cache.reserve(len(tokens))
         alloc = pool.allocator
-        alloc.sync_device()
+        self.stats["h2d_bytes"] += 16 * alloc.sync_device()
         R = len(groups)
         lengths = [len(tokens) for tokens, _ in groups]
         T = sum(lengths)
@@ -308,6 +315,13 @@ class TorchModel:
         while n_dec < R and lengths[n_dec] == 1:
             n_dec += 1
         max_chunk = max(lengths[n_dec:], default=0)
+        st = self.stats
+        st["steps"] += 1
+        st["tokens"] += T
+        st["rows"] += R
+        st["attn_flops"] += config.num_layers * 4 * config.num_heads * config.head_dim * sum(
+            n * s + n * (n + 1) // 2 for s, n in zip(starts, lengths))
+        st["launches"] += 1 + config.num_layers * (1 + (n_dec > 0) + (n_dec < R))
         pre_cu = (cu_q[n_dec:] - n_dec) if n_dec < R else None
 
         hidden = self.embed.index_select(0, tokens_d.long())

@@ -53,6 +53,7 @@ WORKLOADS = {
     "decode_d64": dict(kind="decode", heads=14, kv_heads=2, head_dim=64),
     "decode_d128": dict(kind="decode", heads=28, kv_heads=4, head_dim=128),
     "prefill_d64": dict(kind="prefill", heads=14, kv_heads=2, head_dim=64),
+    "engine": dict(kind="engine", heads=14, kv_heads=2, head_dim=64),
 }
 SEQS_PER_GPU = 256
 BLOCK = 16
@@ -61,13 +62,21 @@ POOL_FRACTION = 0.6
 PREFILL_CHUNKS = 8
 PREFILL_CHUNK = 512
 PREFILL_ROTATIONS = 16
+ENGINE_REQUESTS = 1024      # per GPU, all queued at the start
+ENGINE_CONCURRENT = 256     # max concurrent sequences per GPU
+ENGINE_PREFILL = 512        # prompt tokens per step
+ENGINE_PROMPT = (4, 2048)
+ENGINE_MAX_TOKENS = (32, 512)
+# Default --steps / --warmup per workload kind (engine steps reach steady
+# state only after the first admissions' prompts are through).
+DEFAULT_STEPS = {"decode": (1000, 20), "prefill": (1000, 20), "engine": (600, 600)}
 
 
 def parse_args():
     p = argparse.ArgumentParser()
     p.add_argument("--gpus", type=int, default=1)
-    p.add_argument("--steps", type=int, default=1000)
-    p.add_argument("--warmup", type=int, default=20)
+    p.add_argument("--steps", type=int, default=None)
+    p.add_argument("--warmup", type=int, default=None)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
     p.add_argument("--workload", choices=sorted(WORKLOADS), default="decode_d64")
     p.add_argument("--cpu-seconds", type=float, default=10.0,
@@ -75,7 +84,11 @@ def parse_args():
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--pool-gb", type=float, default=0.0,
                    help="pool size per GPU in GB (default: 60%% of device memory)")
-    return p.parse_args()
+    args = p.parse_args()
+    steps, warmup = DEFAULT_STEPS[WORKLOADS[args.workload]["kind"]]
+    args.steps = steps if args.steps is None else args.steps
+    args.warmup = warmup if args.warmup is None else args.warmup
+    return args
 
 
 # ------------------------------------------------------------------ workload
@@ -763,12 +776,167 @@ def time_cpu_prefill(priors, heads, kv_heads, head_dim, seconds):
             "cores": min(cores, len(cases)), "kind": "port", "sample": sample}
 
 
+def engine_specs(rank: int):
+    from batchstream_inference_engine_b200.serve import engine_workload
+
+    return engine_workload(ENGINE_REQUESTS, seed=1000 + rank, prompt_range=ENGINE_PROMPT,
+                           max_tokens_range=ENGINE_MAX_TOKENS)
+
+
+def model_flops(stats: dict, config, vocab: int, intermediate: int) -> int:
+    """GEMM FLOPs of the processed tokens (projections, MLP) + the output
+    projection of the rows + the attention over visible keys."""
+    hd = config.hidden_size
+    kv = config.num_kv_heads * config.head_dim
+    per_token = config.num_layers * 2 * (hd * (hd + 2 * kv) + hd * hd + 3 * hd * intermediate)
+    return per_token * stats["tokens"] + 2 * hd * vocab * stats["rows"] + stats["attn_flops"]
+
+
+def run_engine(args):
+    import torch
+    import torch.distributed as dist
+
+    from batchstream_inference_engine_b200 import ops
+    from batchstream_inference_engine_b200.backend import PagedBackend
+    from batchstream_inference_engine_b200.replicas import TokenGather
+    from batchstream_inference_engine_b200.serve import BlockBudget, OfflineScheduler
+    from batchstream_inference_engine_b200.torch_model import (QWEN25_05B, QWEN25_05B_INTERMEDIATE,
+                                                              QWEN25_05B_VOCAB, TorchModel,
+                                                              random_weights)
+
+    world, rank, dev = setup_process()
+    model = TorchModel(QWEN25_05B, random_weights(), device=dev, dtype=torch.bfloat16)
+    blocks = ENGINE_CONCURRENT * -(-(ENGINE_PROMPT[1] + ENGINE_MAX_TOKENS[1]) // BLOCK)
+    backend = PagedBackend(model, blocks, BLOCK, ENGINE_PREFILL, max_seqs=ENGINE_CONCURRENT)
+    sched = OfflineScheduler(backend, engine_specs(rank), ENGINE_CONCURRENT,
+                             BlockBudget(blocks, BLOCK))
+    gather = TokenGather(ENGINE_CONCURRENT, dev)
+
+    def engine_step():
+        tokens = sched.step()
+        _, per_rank = gather.exchange(not sched.idle, tokens)
+        return sum(len(d) for d in per_rank)
+
+    for _ in range(args.warmup):
+        engine_step()
+    stream = torch.cuda.current_stream(dev)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    before = dict(model.stats)
+    generated = 0
+    with ClockSampler(dev) as clocks:
+        t0 = torch.cuda.Event(enable_timing=True)
+        t1 = torch.cuda.Event(enable_timing=True)
+        t0.record(stream)
+        for _ in range(args.steps):
+            generated += engine_step()
+        t1.record(stream)
+        torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+    ops.take_status(dev)
+    ms = t0.elapsed_time(t1)
+    delta = {k: model.stats[k] - before[k] for k in model.stats}
+    flops = model_flops(delta, QWEN25_05B, QWEN25_05B_VOCAB, QWEN25_05B_INTERMEDIATE)
+    (ms,), (job_flops, job_tokens) = max_over_ranks([ms], [float(flops), float(delta["tokens"])],
+                                                     dev, world)
+    result = None
+    if rank == 0:
+        peak, peak_note = measured_peak("bf16_tflops_sustained", 1400.0)
+        value = generated / (ms / 1e3)  # every rank's tokens arrive through the gather
+        result = {
+            "metric": "engine tokens/s",
+            "value": round(value, 1),
+            "unit": "tokens/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": round(ms / args.steps, 4),
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "bf16",
+            "data": "synthetic (seeded token-id prompts, random-init weights seed 0 N(0,0.02))",
+            "config": {
+                "workload": f"engine: random-init Qwen2.5-0.5B-shaped replica per GPU, "
+                            f"{ENGINE_REQUESTS} requests per GPU queued at start, prompts "
+                            f"U{list(ENGINE_PROMPT)}, max_tokens U{list(ENGINE_MAX_TOKENS)}, "
+                            f"{ENGINE_CONCURRENT} concurrent, {ENGINE_PREFILL}-token prefill "
+                            f"budget per step, greedy, block 16",
+                "step": "one engine step: admit + batched forward (metadata, slot writes, "
+                        "decode + chunked-prefill attention, GEMMs) + device argmax + "
+                        "token gather",
+                "processed_tokens_per_s": round(job_tokens / (ms / 1e3), 1),
+                "l2": "inputs larger than L2 (weights 1 GB, KV pool per GPU "
+                      f"{2 * 24 * 2 * blocks * BLOCK * 64 * 2 / 1e9:.1f} GB)",
+                "parallelism": f"dp{world} replicas, NCCL all_gather of sampled tokens per step",
+            },
+            "roofline": {
+                "bound": "tensor",
+                "kernel": "whole engine step (cuBLAS GEMMs + this package's attention kernels)",
+                "achieved": round(job_flops / world / (ms / 1e3) / 1e12, 2),
+                "peak": peak,
+                "peak_source": peak_note,
+                "unit": "TFLOP/s",
+                "frac": round(job_flops / world / (ms / 1e3) / 1e12 / peak, 4),
+                "traffic": None,
+            },
+            "e2e": {"value": round(value, 1), "unit": "tokens/s",
+                    "h2d_bytes_per_step": round(delta["h2d_bytes"] / args.steps),
+                    "d2h_bytes_per_step": round(delta["d2h_bytes"] / args.steps),
+                    "path": "the engine step is the public API: host scheduler -> pinned "
+                            "metadata copy -> kernels -> token ids copied back"},
+            "gpu_launches": delta["launches"],
+            "clocks": clocks.summary(),
+        }
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0 and not args.no_cpu_baseline and world == 1:
+        result["cpu_baseline"] = time_cpu_engine(args.cpu_seconds)
+    if rank == 0:
+        print(json.dumps(result), flush=True)
+
+
+def time_cpu_engine(seconds, concurrent=16):
+    """The oracle's CPU restatement of the reference model step (bf16, all host
+    threads for torch) on the engine workload with `concurrent` sequences,
+    stepped until `seconds` have passed; generated tokens per second."""
+    import torch
+
+    from batchstream_inference_engine_b200.serve import BlockBudget, OfflineScheduler
+    from batchstream_inference_engine_b200.torch_model import QWEN25_05B, random_weights
+    from oracle.engine import cpu_backend
+
+    cores = os.cpu_count() or 1
+    torch.set_num_threads(cores)
+    blocks = concurrent * -(-(ENGINE_PROMPT[1] + ENGINE_MAX_TOKENS[1]) // BLOCK)
+    backend = cpu_backend(random_weights(), torch.bfloat16, QWEN25_05B, blocks, BLOCK,
+                          ENGINE_PREFILL, max_seqs=concurrent)
+    sched = OfflineScheduler(backend, engine_specs(0), concurrent, BlockBudget(blocks, BLOCK))
+    sched.step()  # warm-up
+    generated, steps = 0, 0
+    start = time.perf_counter()
+    while time.perf_counter() - start < seconds:
+        generated += len(sched.step())
+        steps += 1
+    elapsed = time.perf_counter() - start
+    return {"value": round(generated / elapsed, 3), "unit": "tokens/s", "cores": cores,
+            "kind": "port",
+            "sample": f"{steps} engine steps of the workload with {concurrent} concurrent "
+                      f"sequences through the oracle's CPU restatement of the reference "
+                      f"model step (bf16), {elapsed:.1f} s, {generated} tokens generated"}
+
+
 def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
     w = WORKLOADS[args.workload]
     H, Hkv, D = w["heads"], w["kv_heads"], w["head_dim"]
+    if w["kind"] == "engine":
+        return run_reference_engine(args)
     prefill = w["kind"] == "prefill"
     # Each step is a bounded sample of the workload (decode: 64 of its sequences,
     # about a quarter of its KV bytes; prefill: the rank's 8 chunks), so the
@@ -810,6 +978,30 @@ def run_reference(args):
     }), flush=True)
 
 
+def run_reference_engine(args):
+    """Engine workload on the host cores through the oracle's restatement of the
+    reference model step: each step a bounded sample (a few seconds of CPU
+    engine steps at 16 concurrent sequences)."""
+    per_step = max(2.0, min(args.cpu_seconds, 10.0))
+    vals, base = [], None
+    for _ in range(max(1, min(args.steps, 3))):
+        base = time_cpu_engine(per_step)
+        vals.append(base["value"])
+    value = statistics.median(vals)
+    base["value"] = value
+    print(json.dumps({
+        "metric": "engine tokens/s", "impl": "reference", "value": value, "unit": "tokens/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded token-id prompts, random-init weights seed 0 N(0,0.02))",
+        "config": {"workload": "engine: oracle CPU restatement of the reference model step, "
+                               "16 concurrent sequences, on host cores"},
+        "cpu_baseline": base,
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
 def main():
     args = parse_args()
     kind = WORKLOADS[args.workload]["kind"]
@@ -817,6 +1009,8 @@ def main():
         run_reference(args)
     elif kind == "prefill":
         run_prefill(args)
+    elif kind == "engine":
+        run_engine(args)
     else:
         run_decode(args)
 
