@@ -7,6 +7,7 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include <cmath>
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
@@ -574,8 +575,10 @@ int bs_prefill_attention(const void* query, int64_t query_token_stride, const in
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   BS_CHECK(ws != nullptr, "workspace is null");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  // The tensor-core path folds the scale into the running maximum: it needs a
+  // positive scale (other scales take the per-token path).
   const bool fast = !(flags & BS_PREFILL_PER_TOKEN) && dtype == BS_BF16 && head_dim == 64 &&
-                    block_size == 16 && query_token_stride == num_heads * head_dim &&
+                    scaling > 0.0 && block_size == 16 && query_token_stride == num_heads * head_dim &&
                     aligned16(query) && aligned16(key_pool) && aligned16(value_pool) &&
                     (output_token_stride * 2) % 16 == 0 && aligned16(output);
   if (fast) {
@@ -603,6 +606,10 @@ int bs_prefill_attention(const void* query, int64_t query_token_stride, const in
     p.num_blocks = static_cast<int32_t>(num_blocks);
     p.qtiles = static_cast<int32_t>((max_query_len + 127) / 128);
     p.scale = static_cast<float>(scaling);
+    {
+      int e = 0;
+      p.exact_scale = std::frexp(static_cast<double>(p.scale), &e) == 0.5 ? 1 : 0;
+    }
     p.status = reinterpret_cast<uint32_t*>(ws);
     const int64_t grid = num_rows * num_heads * p.qtiles;
     if (grid > kInt32Max) return fail(BS_ERR_UNSUPPORTED, "too many query tiles");

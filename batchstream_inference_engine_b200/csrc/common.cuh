@@ -174,6 +174,16 @@ __device__ __forceinline__ float round_bf16(float x) {
   return __bfloat162float(__float2bfloat16_rn(x));
 }
 
+// Two values rounded to nearest bf16 (ties to even) and widened back, through
+// one packed conversion (cvt.rn.bf16x2.f32 issues several times faster than two
+// single cvt.rn.bf16.f32 on sm_100).  Same results as round_bf16 on each.
+__device__ __forceinline__ void round_bf16x2(float& a, float& b) {
+  uint32_t d;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(d) : "f"(b), "f"(a));  // d = {b : a}
+  a = __uint_as_float(d << 16);
+  b = __uint_as_float(d & 0xFFFF0000u);
+}
+
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&v);

@@ -6,24 +6,34 @@
 // chunk and full over the cached part — the reference's _read_blocks + attend
 // with _causal_mask (src/server/torch_model.py:39-64, 165-167, 295-297).
 //
-// One CTA per (chunk, query head, 128-token query tile).  Warp 4 is the issuer:
-// it loads the query tile with one TMA box of a [T, H, D] tensor map (128 tokens
-// x 64 dims, 128-byte swizzle), streams the sequence's K and V 16-token blocks
-// through the block table into a two-stage ring (one TMA box per block), and
-// from one thread issues
-//     S  = Q K^T   tcgen05.mma kind::f16, M=128 N=128 K=64, S in TMEM (128 cols)
-//     O += P V     tcgen05.mma kind::f16, M=128 N=64 K=128, O in TMEM (64 cols)
-// with operands read straight from swizzled shared memory (K-major Q, K and P;
-// V as an MN-major operand).  Warps 0-3 own the 128 query rows (TMEM lane = row):
-// they read their row of S with tcgen05.ld, apply the reference's rounding
-// points (bf16(bf16(q.k) * scale)), the causal and length masks and an online
-// softmax in base 2 with no cross-thread reductions, rescale O in TMEM when a
-// row maximum grows, and write P (bf16) into shared memory for the next MMA.
+// One CTA per (chunk, query head, 128-token query tile); CTAs are numbered so
+// the query tiles with the most keys start first.  Three roles, one warp each
+// for the first two:
+//   * loader (warp 5): the query tile as one TMA box of a [T, H, D] tensor map,
+//     then the sequence's K and V through the block table into two 3-stage
+//     rings (64 keys = 4 blocks per stage, one TMA box per block).  A K stage is
+//     refilled once the S product that read it has completed, a V stage once
+//     its P V product has; K runs two tiles ahead of V, which gives either load
+//     about three softmax periods to land.  Block-table entries come from a
+//     32-entry register window fetched one window ahead;
+//   * MMA issuer (warp 4), from one thread:
+//       S  = Q K^T   tcgen05.mma kind::f16, M=128 N=64 K=64  -> TMEM, 2 buffers
+//       O += P V     tcgen05.mma kind::f16, M=128 N=64 K=64  -> TMEM
+//     in the order PV(j), S(j+2): the tensor core computes the scores two tiles
+//     ahead while the softmax warps work on tile j+1;
+//   * softmax (warps 0-3) own the 128 query
+// rows (TMEM lane = row): they read their row of S (tcgen05.ld), apply the
+// reference's rounding points (bf16(bf16(q.k) * scale); the second rounding is
+// exact and skipped when the scale is a power of two) through packed
+// conversions, mask only on tiles that reach past a row's position or the
+// context, run an online softmax in base 2 that rescales O in TMEM only when a
+// row maximum grows by more than 2^8, and write P (bf16) into one of two
+// shared-memory buffers for the P V product.
 //
 // Waits are bounded (a status bit instead of a hang) and their outcome is made
 // warp-uniform before any warp-collective tcgen05 instruction; before TMEM is
-// freed the issuer drains every MMA and TMA load it started, also on the error
-// path.  V rows of keys no row of the tile can see are zeroed before the P V
+// freed the MMA warp drains every MMA and the loader every TMA load it started,
+// also on the error path.  V rows of keys no row of the tile can see are zeroed before the P V
 // product, so stale or NaN shared-memory and pool contents never reach the result.
 #include "prefill.cuh"
 
@@ -32,15 +42,18 @@ namespace bsb {
 namespace {
 
 constexpr int kRows = 128;   // query rows per CTA (TMEM lanes)
-constexpr int kKeys = 128;   // keys per KV tile
+constexpr int kKeys = 64;    // keys per KV tile (4 blocks)
 constexpr int kD = 64;
-constexpr int kThreads = 160;  // warps 0-3 softmax, warp 4 issuer
-constexpr int kTileBytes = kKeys * kD * 2;  // 16 KiB (K or V of one tile)
-constexpr int kQBytes = kRows * kD * 2;
-constexpr int kPBytes = kRows * kKeys * 2;  // two [128][64] regions
-constexpr int kSmemBytes = 1024 + kQBytes + 2 * 2 * kTileBytes + kPBytes;
-constexpr uint32_t kTmemCols = 256;  // S: [0, 128), O: [128, 192)
+constexpr int kStages = 3;
+constexpr int kThreads = 192;  // warps 0-3 softmax, warp 4 MMA issuer, warp 5 loader
+constexpr int kTileBytes = kKeys * kD * 2;  // 8 KiB: K or V of one tile
+constexpr int kQBytes = kRows * kD * 2;     // 16 KiB
+constexpr int kPBytes = kRows * kKeys * 2;  // 16 KiB per P buffer
+constexpr int kSmemBytes = 1024 + kQBytes + kStages * 2 * kTileBytes + 2 * kPBytes;
+constexpr uint32_t kTmemCols = 256;  // S0 [0, 64), S1 [64, 128), O [128, 192)
+constexpr uint32_t kTmemO = 128;
 constexpr float kLog2eP = 1.4426950408889634f;
+constexpr float kRescaleSlack = 8.f;  // rescale O when a row max grows by > 2^8
 
 __device__ __forceinline__ uint64_t umma_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
   // sm100 shared-memory matrix descriptor: start, leading and stride byte
@@ -123,36 +136,56 @@ __device__ __forceinline__ void tma_load_3d(void* smem_dst, const CUtensorMap* m
       : "memory");
 }
 
+// Lane-wise maximum of two packed bf16 pairs.
+__device__ __forceinline__ uint32_t max_bf16x2(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("max.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+
 // Byte offset of element (r, c) in a [rows][64] bf16 tile with 128-byte swizzle.
 __device__ __forceinline__ uint32_t swz128(int r, int c) {
   return r * 128 + ((((c >> 3) ^ (r & 7))) << 4) + (c & 7) * 2;
 }
 
-__global__ void __launch_bounds__(kThreads, 1)
+// Query tile index of CTA b: tiles with the most keys first (the last query
+// tile of every chunk, then the one before, ...), heads innermost.
+__device__ __forceinline__ void cta_work(const PrefillArgs& a, int b, int& r, int& h, int& t0) {
+  const int H = a.num_heads;
+  h = b % H;
+  const int item = b / H;                 // 0 .. num_rows * qtiles - 1
+  const int t = a.qtiles - 1 - item / a.num_rows;
+  r = item % a.num_rows;
+  t0 = t * kRows;
+}
+
+__global__ void __launch_bounds__(kThreads, 2)
     prefill_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap kmap,
                    const __grid_constant__ CUtensorMap vmap, const PrefillArgs a) {
   extern __shared__ uint8_t smem_raw[];
-  __shared__ uint64_t q_full, kv_full[2], s_full, p_full, o_full, mma_done;
+  // o_full completes once per P V product (the rescale waits for the previous
+  // tile's); o_last once, after the last one: a parity wait on o_full could not
+  // tell "done" from "two products behind" at the end.
+  __shared__ uint64_t q_full, k_full[kStages], k_empty[kStages], v_full[kStages],
+      v_empty[kStages], s_full[2], p_full[2], o_full, o_last, mma_done;
   __shared__ uint32_t tmem_base;
 
   const uint32_t raw = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + (((raw + 1023u) & ~1023u) - raw);
   uint8_t* sQ = smem;
-  // Stage st holds K at sK(st) and V right after it.
+  // Stage st holds K at sK(st) and V right after it; P buffer b at sP(b).
   auto sK = [&](int st) { return smem + kQBytes + st * 2 * kTileBytes; };
   auto sV = [&](int st) { return smem + kQBytes + st * 2 * kTileBytes + kTileBytes; };
-  uint8_t* sP = smem + kQBytes + 4 * kTileBytes;
+  auto sP = [&](int b) { return smem + kQBytes + kStages * 2 * kTileBytes + b * kPBytes; };
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   pdl_wait();
 
-  const int H = a.num_heads;
-  const int r = blockIdx.x / (H * a.qtiles);
-  const int h = (blockIdx.x / a.qtiles) % H;
-  const int t0 = (blockIdx.x % a.qtiles) * kRows;
+  int r, h, t0;
+  cta_work(a, blockIdx.x, r, h, t0);
   const int tok0 = __ldg(a.cu_q + r);
   const int n = __ldg(a.cu_q + r + 1) - tok0;
-  if (t0 == 0 && tid == 0 && n > a.qtiles * kRows) set_status(a.status, kStatusBadLength);
+  if (t0 == 0 && h == 0 && tid == 0 && n > a.qtiles * kRows) set_status(a.status, kStatusBadLength);
   if (t0 >= n) return;
   const int ctx = __ldg(a.context_lens + r);
   const int prior = ctx - n;
@@ -170,11 +203,18 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (tid == 0) {
     mbar_init(&q_full, 1);
-    mbar_init(&kv_full[0], 1);
-    mbar_init(&kv_full[1], 1);
-    mbar_init(&s_full, 1);
-    mbar_init(&p_full, kRows);
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&k_full[s], 1);
+      mbar_init(&k_empty[s], 1);
+      mbar_init(&v_full[s], 1);
+      mbar_init(&v_empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&s_full[b], 1);
+      mbar_init(&p_full[b], kRows);
+    }
     mbar_init(&o_full, 1);
+    mbar_init(&o_last, 1);
     mbar_init(&mma_done, 1);
     fence_barrier_init();
   }
@@ -187,194 +227,265 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  const uint32_t tS = tmem_base;
-  const uint32_t tO = tmem_base + 128;
+  const uint32_t tmem = tmem_base;
 
-  constexpr uint32_t kIdescS = umma_idesc(128, 128, 0, 0);
-  constexpr uint32_t kIdescO = umma_idesc(128, 64, 0, 1);
+  constexpr uint32_t kIdescS = umma_idesc(128, kKeys, 0, 0);
+  constexpr uint32_t kIdescO = umma_idesc(128, kD, 0, 1);
+  // A wait's outcome is the same for the whole warp (and the warp converged)
+  // before any warp-collective instruction follows it.
+  auto wait_all = [&](uint64_t* bar, uint32_t parity) {
+    return __all_sync(0xffffffffu, mbar_wait(bar, parity)) != 0;
+  };
 
-  if (warp == 4) {
-    // ---------------------------------------------------------------- issuer
-    // Loads one KV tile: lanes 0-7 look up their block, lane 0 issues.
-    auto load_kv = [&](int j, int st) {
-      const int b = j * 8 + (lane & 7);
-      int32_t blk = -1;
-      if (lane < 8 && b * 16 < kv_end) {
-        blk = __ldg(table + b);
-        if (blk < 0 || blk >= a.num_blocks) {
-          set_status(a.status, kStatusBadBlock);
-          blk = -1;
-        }
-      }
-      const uint32_t valid = __ballot_sync(0xffffffffu, blk >= 0) & 0xffu;
-      if (lane == 0) mbar_arrive_expect_tx(&kv_full[st], __popc(valid) * 2u * 2048u);
-      __syncwarp();
-      if (lane < 8 && blk >= 0) {
-        const int32_t y = (kvh * a.num_blocks + blk) * 16;
-        tma_load_2d(sK(st) + lane * 2048, &kmap, &kv_full[st], 0, y);
-        tma_load_2d(sV(st) + lane * 2048, &vmap, &kv_full[st], 0, y);
-      }
+  if (warp == 5) {
+    // ---------------------------------------------------------------- loader
+    // Table window: lane i holds entry 32 w + i of window w (0 past the row).
+    auto fetch = [&](int w) {
+      const int e = w * 32 + lane;
+      return (e < a.max_blocks && e * 16 < kv_end) ? __ldg(table + e) : 0;
     };
-    auto issue_s = [&](int st) {
-      if (lane == 0) {
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          umma_f16(tS, umma_desc(smem_u32(sQ) + 32 * k, 16, 1024),
-                   umma_desc(smem_u32(sK(st)) + 32 * k, 16, 1024), kIdescS, k > 0 ? 1u : 0u);
-        }
-        umma_commit(&s_full);
-      }
-      __syncwarp();
-    };
-    // A wait's outcome is the same for the whole warp (and the warp converged)
-    // before any warp-collective instruction follows it.
-    auto wait_all = [&](uint64_t* bar, uint32_t parity) {
-      return __all_sync(0xffffffffu, mbar_wait(bar, parity)) != 0;
-    };
-    int loads = 0;  // KV tiles whose loads were issued
-    int ready = 0;  // KV tiles whose loads were seen complete
+    int32_t win_cur = fetch(0), win_next = fetch(1);
+    int win = 0;
     if (lane == 0) {
       mbar_arrive_expect_tx(&q_full, kQBytes);
       tma_load_3d(sQ, &qmap, &q_full, 0, h, tok0 + t0);
     }
-    load_kv(0, 0);
-    loads = 1;
-    if (ntiles > 1) {
-      load_kv(1, 1);
-      loads = 2;
-    }
-    const bool q_ready = wait_all(&q_full, 0);
-    bool ok = q_ready && wait_all(&kv_full[0], 0);
-    if (ok) {
-      ready = 1;
-      tc_fence_after();
-      issue_s(0);
-    }
-    for (int j = 0; j < ntiles && ok; ++j) {
-      ok = wait_all(&p_full, j & 1);
-      if (!ok) break;
-      tc_fence_after();
-      const int st = j & 1;
-      if (lane == 0) {
-#pragma unroll
-        for (int k = 0; k < 8; ++k) {
-          umma_f16(tO, umma_desc(smem_u32(sP) + (k >> 2) * 16384 + 32 * (k & 3), 16, 1024),
-                   umma_desc(smem_u32(sV(st)) + 2048 * k, 16384, 1024), kIdescO,
-                   (j > 0 || k > 0) ? 1u : 0u);
+    // Block of tile t held by lane (lanes 0-3), -1 when absent.  Tiles are
+    // asked for in increasing order, V lagging K by two.
+    auto block_of = [&](int t, int32_t wv) {
+      const int b = t * 4 + (lane & 3);
+      int32_t blk = __shfl_sync(0xffffffffu, wv, (t * 4) % 32 + (lane & 3));
+      if (lane >= 4 || b * 16 >= kv_end) return -1;
+      if (blk < 0 || blk >= a.num_blocks) {
+        set_status(a.status, kStatusBadBlock);
+        return -1;
+      }
+      return blk;
+    };
+    // One ring's tile t: expect its bytes on `full`, one box per block.
+    auto load = [&](const CUtensorMap* map, uint8_t* dst, uint64_t* full, int32_t blk) {
+      const uint32_t valid = __ballot_sync(0xffffffffu, blk >= 0) & 0xfu;
+      if (lane == 0) mbar_arrive_expect_tx(full, __popc(valid) * 2048u);
+      __syncwarp();
+      if (blk >= 0) tma_load_2d(dst + lane * 2048, map, full, 0, (kvh * a.num_blocks + blk) * 16);
+    };
+    bool ok = true;
+    int k_loads = 0, v_loads = 0;
+    int32_t hold_even = -1, hold_odd = -1;  // V's blocks lag K's by two tiles
+    for (int i = 0; i < ntiles + 2 && ok; ++i) {
+      // V(i - 2)'s blocks, taken before K(i) (same parity) replaces them.
+      const int32_t vblk = (i & 1) ? hold_odd : hold_even;
+      if (i < ntiles) {
+        const int st = i % kStages;
+        if (i >= kStages) {
+          // K stage st is free once S of tile i - 3 has read it.
+          ok = wait_all(&k_empty[st], ((i - kStages) / kStages) & 1);
+          if (!ok) break;
         }
-        umma_commit(&o_full);
+        if ((i * 4) / 32 != win) {
+          win_cur = win_next;
+          ++win;
+          win_next = fetch(win + 1);
+        }
+        const int32_t blk = block_of(i, win_cur);
+        load(&kmap, sK(st), &k_full[st], blk);
+        k_loads = i + 1;
+        if (i & 1) hold_odd = blk; else hold_even = blk;
+      }
+      const int t = i - 2;
+      if (t >= 0 && t < ntiles) {
+        const int st = t % kStages;
+        if (t >= kStages) {
+          // V stage st is free once P V of tile t - 3 has read it.
+          ok = wait_all(&v_empty[st], ((t - kStages) / kStages) & 1);
+          if (!ok) break;
+        }
+        load(&vmap, sV(st), &v_full[st], vblk);
+        v_loads = t + 1;
+      }
+    }
+    // Drain: the loads of the last stages still hold their newest phase.
+    bool drained = wait_all(&q_full, 0);
+    for (int t = max(0, k_loads - kStages); t < k_loads; ++t) {
+      drained = wait_all(&k_full[t % kStages], (t / kStages) & 1) && drained;
+    }
+    for (int t = max(0, v_loads - kStages); t < v_loads; ++t) {
+      drained = wait_all(&v_full[t % kStages], (t / kStages) & 1) && drained;
+    }
+    if ((!ok || !drained) && lane == 0) set_status(a.status, kStatusWaitTimeout);
+  } else if (warp == 4) {
+    // ---------------------------------------------------------------- MMA issuer
+    auto issue_s = [&](int j) {
+      if (lane == 0) {
+        const int st = j % kStages;
+        const uint32_t d = tmem + (j & 1) * kKeys;
+#pragma unroll
+        for (int k = 0; k < kD / 16; ++k) {
+          umma_f16(d, umma_desc(smem_u32(sQ) + 32 * k, 16, 1024),
+                   umma_desc(smem_u32(sK(st)) + 32 * k, 16, 1024), kIdescS, k > 0 ? 1u : 0u);
+        }
+        umma_commit(&s_full[j & 1]);
+        umma_commit(&k_empty[st]);
       }
       __syncwarp();
-      if (j + 1 < ntiles) {
-        ok = wait_all(&kv_full[(j + 1) & 1], ((j + 1) >> 1) & 1);
-        if (!ok) break;
-        ready = j + 2;
-        issue_s((j + 1) & 1);
+    };
+    bool ok = wait_all(&q_full, 0);
+    // Scores of the first two tiles.
+    for (int j = 0; j < 2 && j < ntiles && ok; ++j) {
+      ok = wait_all(&k_full[j % kStages], (j / kStages) & 1);
+      if (!ok) break;
+      tc_fence_after();
+      issue_s(j);
+    }
+    for (int j = 0; j < ntiles && ok; ++j) {
+      const int st = j % kStages;
+      ok = wait_all(&p_full[j & 1], (j >> 1) & 1) && wait_all(&v_full[st], (j / kStages) & 1);
+      if (!ok) break;
+      tc_fence_after();
+      if (lane == 0) {
+        const uint32_t p0 = smem_u32(sP(j & 1));
+        const uint32_t v0 = smem_u32(sV(st));
+#pragma unroll
+        for (int k = 0; k < kKeys / 16; ++k) {
+          umma_f16(tmem + kTmemO, umma_desc(p0 + 32 * k, 16, 1024),
+                   umma_desc(v0 + 2048 * k, 8192, 1024), kIdescO, (j > 0 || k > 0) ? 1u : 0u);
+        }
+        umma_commit(&o_full);
+        umma_commit(&v_empty[st]);
+        if (j == ntiles - 1) umma_commit(&o_last);
       }
+      __syncwarp();
       if (j + 2 < ntiles) {
-        // Stage j & 1 is free once the P V product of tile j has read it.
-        ok = wait_all(&o_full, j & 1);
+        // S buffer j & 1 is free: softmax(j) read it before arriving on p_full.
+        ok = wait_all(&k_full[(j + 2) % kStages], ((j + 2) / kStages) & 1);
         if (!ok) break;
-        load_kv(j + 2, st);
-        loads = j + 3;
+        tc_fence_after();
+        issue_s(j + 2);
       }
     }
-    // Drain: no MMA may still use TMEM and no TMA load may still write shared
-    // memory once the CTA frees them.  The commit tracks every MMA issued above.
+    // Drain: no MMA may still use TMEM once the CTA frees it.  The commit
+    // tracks every MMA issued above.
     if (lane == 0) umma_commit(&mma_done);
     __syncwarp();
-    bool drained = wait_all(&mma_done, 0);
-    if (!q_ready) drained = wait_all(&q_full, 0) && drained;
-    for (int t = ready; t < loads; ++t) drained = wait_all(&kv_full[t & 1], (t >> 1) & 1) && drained;
+    const bool drained = wait_all(&mma_done, 0);
     if ((!ok || !drained) && lane == 0) set_status(a.status, kStatusWaitTimeout);
   } else {
     // ---------------------------------------------------------------- softmax
     const int row = tid;  // TMEM lane and query row
     const int qpos = prior + t0 + row;  // position of this row's token
     const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
-    auto wait_all = [&](uint64_t* bar, uint32_t parity) {
-      return __all_sync(0xffffffffu, mbar_wait(bar, parity)) != 0;
-    };
-    float m_run = -INFINITY, l_run = 0.f;
+    // z = score * scale * log2(e); rows keep m (max z used for P) and l.
+    const float zscale = (a.exact_scale ? a.scale : 1.f) * kLog2eP;
+    float m_used = -INFINITY, l_run = 0.f;
     bool ok = true;
     for (int j = 0; j < ntiles; ++j) {
-      ok = wait_all(&s_full, j & 1);
+      ok = wait_all(&s_full[j & 1], (j >> 1) & 1);
       if (!ok) break;
       tc_fence_after();
-      float s[kKeys];
-#pragma unroll
-      for (int c0 = 0; c0 < kKeys; c0 += 32) {
-        uint32_t v[32];
-        tmem_ld32(tS + lane_base + c0, v);
+      // Scores rounded to bf16 (the reference's first rounding), kept as packed
+      // pairs: lane bits [15:0] hold key 2i, [31:16] key 2i + 1.
+      uint32_t sp[kKeys / 2];
+      {
+        uint32_t v0[32], v1[32];
+        tmem_ld32(tmem + lane_base + (j & 1) * kKeys, v0);
+        tmem_ld32(tmem + lane_base + (j & 1) * kKeys + 32, v1);
         tmem_wait_ld();
 #pragma unroll
-        for (int c = 0; c < 32; ++c) s[c0 + c] = __uint_as_float(v[c]);
+        for (int i = 0; i < 16; ++i) {
+          sp[i] = pack_bf16x2(__uint_as_float(v0[2 * i]), __uint_as_float(v0[2 * i + 1]));
+          sp[16 + i] = pack_bf16x2(__uint_as_float(v1[2 * i]), __uint_as_float(v1[2 * i + 1]));
+        }
       }
-      float m_tile = -INFINITY;
-      const int key0 = j * kKeys;
+      if (!a.exact_scale) {
 #pragma unroll
-      for (int c = 0; c < kKeys; ++c) {
-        const int key = key0 + c;
-        float x = round_bf16(round_bf16(s[c]) * a.scale) * kLog2eP;
-        x = (key <= qpos && key < ctx) ? x : -INFINITY;
-        s[c] = x;
-        m_tile = fmaxf(m_tile, x);
+        for (int i = 0; i < kKeys / 2; ++i) {
+          sp[i] = pack_bf16x2(__uint_as_float(sp[i] << 16) * a.scale,
+                              __uint_as_float(sp[i] & 0xFFFF0000u) * a.scale);
+        }
       }
-      // Key 0 is visible to every row, so m_new is finite from tile 0 on.
-      const float m_new = fmaxf(m_run, m_tile);
-      const float corr = m_new > m_run ? fast_exp2(m_run - m_new) : 1.f;
-      if (j > 0) {
+      const int key0 = j * kKeys;
+      // Tiles wholly at or before the first row's position need no mask;
+      // masked keys become bf16 -inf.
+      if (key0 + kKeys - 1 > prior + t0) {
+#pragma unroll
+        for (int i = 0; i < kKeys / 2; ++i) {
+          const int k0 = key0 + 2 * i;
+          const bool lo = k0 <= qpos && k0 < ctx, hi = k0 + 1 <= qpos && k0 + 1 < ctx;
+          sp[i] = (lo ? (sp[i] & 0xFFFFu) : 0xFF80u) | (hi ? (sp[i] & 0xFFFF0000u) : 0xFF800000u);
+        }
+      }
+      uint32_t mp[4] = {sp[0], sp[1], sp[2], sp[3]};
+#pragma unroll
+      for (int i = 4; i < kKeys / 2; ++i) mp[i & 3] = max_bf16x2(mp[i & 3], sp[i]);
+      const uint32_t m2 = max_bf16x2(max_bf16x2(mp[0], mp[1]), max_bf16x2(mp[2], mp[3]));
+      const float m_tile = fmaxf(__uint_as_float(m2 << 16), __uint_as_float(m2 & 0xFFFF0000u));
+      const float m_tile_z = m_tile * zscale;
+      // Key 0 is visible to every row, so m_used is finite from tile 0 on.
+      const bool grow = m_tile_z > m_used + kRescaleSlack;
+      if (j == 0) {
+        m_used = m_tile_z;
+      } else if (__any_sync(0xffffffffu, grow)) {
+        // tcgen05.ld/st are warp-collective: the warp rescales if any row
+        // grew past the slack (factor 1 for the others).
         ok = wait_all(&o_full, (j - 1) & 1);  // P V of the previous tile is done
         if (!ok) break;
         tc_fence_after();
-        // tcgen05.ld/st are warp-collective: the warp rescales if any row grew
-        // (factor 1 for the others).
-        if (__any_sync(0xffffffffu, m_new > m_run)) {
+        const float m_new = grow ? m_tile_z : m_used;
+        const float corr = grow ? fast_exp2(m_used - m_new) : 1.f;
 #pragma unroll
-          for (int c0 = 0; c0 < kD; c0 += 32) {
-            uint32_t v[32];
-            tmem_ld32(tO + lane_base + c0, v);
-            tmem_wait_ld();
+        for (int c0 = 0; c0 < kD; c0 += 32) {
+          uint32_t v[32];
+          tmem_ld32(tmem + kTmemO + lane_base + c0, v);
+          tmem_wait_ld();
 #pragma unroll
-            for (int c = 0; c < 32; ++c) v[c] = __float_as_uint(__uint_as_float(v[c]) * corr);
-            tmem_st32(tO + lane_base + c0, v);
-          }
-          tmem_wait_st();
+          for (int c = 0; c < 32; ++c) v[c] = __float_as_uint(__uint_as_float(v[c]) * corr);
+          tmem_st32(tmem + kTmemO + lane_base + c0, v);
         }
+        tmem_wait_st();
+        l_run *= corr;
+        m_used = m_new;
       }
-      m_run = m_new;
-      float psum = 0.f;
-      uint8_t* prow = sP;
+      // P = 2^(z - m_used) <= 2^8, packed to bf16 into P buffer j & 1 (free:
+      // s_full of tile j implies the P V of tile j - 2 that read it is done).
+      // Sums kept in 8 partials (key index mod 8), two per packed register.
+      float2 ps[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f),
+                      make_float2(0.f, 0.f)};
+      const float2 zs = make_float2(zscale, zscale), mm = make_float2(-m_used, -m_used);
+      uint8_t* prow = sP(j & 1);
 #pragma unroll
-      for (int ch = 0; ch < kKeys / 8; ++ch) {  // 16-byte chunks of the P row
-        float p[8];
+      for (int ch = 0; ch < kKeys / 8; ++ch) {
+        uint32_t w[4];
 #pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          p[e] = fast_exp2(s[ch * 8 + e] - m_new);
-          psum += p[e];
+        for (int e = 0; e < 4; ++e) {
+          const uint32_t u = sp[ch * 4 + e];
+          const float2 z = __ffma2_rn(make_float2(__uint_as_float(u << 16),
+                                                  __uint_as_float(u & 0xFFFF0000u)), zs, mm);
+          const float2 pe = make_float2(fast_exp2(z.x), fast_exp2(z.y));
+          ps[e] = __fadd2_rn(ps[e], pe);
+          w[e] = pack_bf16x2(pe.x, pe.y);
         }
-        uint4 w;
-        w.x = pack_bf16x2(p[0], p[1]);
-        w.y = pack_bf16x2(p[2], p[3]);
-        w.z = pack_bf16x2(p[4], p[5]);
-        w.w = pack_bf16x2(p[6], p[7]);
-        const int col = (ch & 7) * 8;
-        *reinterpret_cast<uint4*>(prow + (ch >> 3) * 16384 + swz128(row, col)) = w;
+        *reinterpret_cast<uint4*>(prow + swz128(row, ch * 8)) = make_uint4(w[0], w[1], w[2], w[3]);
       }
-      l_run = l_run * corr + psum;
+      l_run += ((ps[0].x + ps[0].y) + (ps[1].x + ps[1].y)) + ((ps[2].x + ps[2].y) + (ps[3].x + ps[3].y));
       // Keys no row of this CTA sees (past the context, or past the last row's
       // position): their V rows hold stale pool data or never-loaded shared
       // memory, possibly NaN, which would poison 0 * V in the tensor core.
-      if (key0 + row >= kv_end) {
+      if (j == ntiles - 1 && row < kKeys && key0 + kKeys > kv_end) {
+        // The V tile must have landed before its tail rows are overwritten.
+        ok = wait_all(&v_full[j % kStages], (j / kStages) & 1);
+        if (!ok) break;
+      }
+      if (row < kKeys && key0 + row >= kv_end) {
         uint4 z = make_uint4(0u, 0u, 0u, 0u);
+        uint8_t* vrow = sV(j % kStages) + row * 128;
 #pragma unroll
-        for (int c = 0; c < 8; ++c) *reinterpret_cast<uint4*>(sV(j & 1) + row * 128 + c * 16) = z;
+        for (int c = 0; c < 8; ++c) *reinterpret_cast<uint4*>(vrow + c * 16) = z;
       }
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       tc_fence_before();
-      mbar_arrive(&p_full);
+      mbar_arrive(&p_full[j & 1]);
     }
-    if (ok) ok = wait_all(&o_full, (ntiles - 1) & 1);
+    if (ok) ok = wait_all(&o_last, 0);
     if (ok) {
       tc_fence_after();
       // Every lane reads its TMEM row (warp-collective); rows past the chunk
@@ -387,7 +498,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
       for (int c0 = 0; c0 < kD; c0 += 32) {
         uint32_t v[32];
-        tmem_ld32(tO + lane_base + c0, v);
+        tmem_ld32(tmem + kTmemO + lane_base + c0, v);
         tmem_wait_ld();
         if (store) {
 #pragma unroll
@@ -409,7 +520,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   if (warp == 0) {
     tc_fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tS),
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
                  "r"(kTmemCols));
   }
 }
@@ -424,6 +535,9 @@ int launch_prefill_tc(const PrefillArgs& a, const CUtensorMap& qmap, const CUten
   if (!configured) {
     cudaError_t e = cudaFuncSetAttribute(prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          kSmemBytes);
+    if (e != cudaSuccess) return static_cast<int>(e);
+    // All of the unified L1 as shared memory: two CTAs per SM.
+    e = cudaFuncSetAttribute(prefill_kernel, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
     if (e != cudaSuccess) return static_cast<int>(e);
     configured = true;
   }

@@ -18,6 +18,9 @@ struct PrefillArgs {
   int32_t bt_rows, max_blocks;
   int32_t num_rows, num_heads, num_kv_heads, groups, num_blocks, qtiles;
   float scale;
+  // Non-zero when scale is a power of two: bf16(bf16(q.k) * scale) then equals
+  // bf16(q.k) * scale exactly and the second rounding is skipped.
+  int32_t exact_scale;
   uint32_t* status;
 };
 
