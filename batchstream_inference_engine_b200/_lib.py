@@ -26,6 +26,7 @@ EXPORTS = (
     "bs_prefill_attention",
     "bs_prefill_attention_workspace_bytes",
     "bs_reshape_and_cache",
+    "bs_decode_append",
     "bs_step_metadata",
     "bs_take_status",
 )
@@ -69,6 +70,11 @@ _SIGNATURES = {
     ),
     "bs_reshape_and_cache": (
         [_p, _p, _i64, _i64, _i32, _p, _i64, _p, _p, _i32, _i64, _i64, _i64, _i64, _p, _p],
+        ctypes.c_int,
+    ),
+    "bs_decode_append": (
+        [_p, _p, _i64, _p, _i64, _i64, _i64, _p, _p, _i64, _i64, _i32, _p, _p, _i32, _i64, _i64,
+         _i64, _i64, _p, _p, _p, _p],
         ctypes.c_int,
     ),
     "bs_step_metadata": (

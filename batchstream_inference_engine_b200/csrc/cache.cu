@@ -13,6 +13,8 @@
 //     context[r]   = start_pos[r] + n_new[r]
 // bit-exact with the reference allocator's locate().
 //
+// Decode append (one new token per row) fuses both for decode steps.
+//
 // Slot write.  k/v rows [T, Hkv, D] (any token stride) land at
 // pool[h, slot / bs, slot % bs, :] with 16-byte vector loads and stores; an fp32
 // input into a bf16 pool is rounded to nearest-even, as torch's indexed
@@ -228,6 +230,85 @@ __global__ void __launch_bounds__(256)
   }
 }
 
+// Decode append: one new token per row (a pure decode step).  One warp per
+// row: lane 0 locates the token's slot through the row's block table
+// (BlockAllocator.locate, src/server/block_allocator.py:28-30) and writes
+// context_lens[r] = start_pos[r] + 1 and slots[r]; the warp then copies the
+// row's K and V [Hkv, D] into the pool (PagedKVCache.append,
+// src/server/torch_model.py:149-153) with 16-byte accesses when VEC.  It
+// replaces the metadata + slot-write pair for decode steps and lets the next
+// kernel launch at once.
+template <typename Tin, typename Tpool, bool VEC>
+__global__ void __launch_bounds__(256)
+    decode_append_kernel(const int32_t* __restrict__ seq_rows, const int32_t* __restrict__ start_pos,
+                         int32_t R, const int32_t* __restrict__ block_tables, int64_t bt_stride,
+                         int32_t bt_rows, int32_t max_blocks, int32_t block_size,
+                         int32_t num_blocks, const Tin* __restrict__ k, const Tin* __restrict__ v,
+                         int64_t k_stride, int64_t v_stride, int32_t Hkv, int32_t D,
+                         Tpool* __restrict__ k_pool, Tpool* __restrict__ v_pool,
+                         int64_t pool_slots, int32_t* __restrict__ context_lens,
+                         int32_t* __restrict__ slots, uint32_t* status) {
+  pdl_trigger();
+  pdl_wait();
+  const int32_t r = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (r >= R) return;
+  int32_t slot = -1;
+  if (lane == 0) {
+    const int32_t pos = start_pos[r];
+    const int32_t row = seq_rows != nullptr ? seq_rows[r] : r;
+    const int32_t bi = pos / block_size;
+    if (row < 0 || row >= bt_rows || pos < 0 || bi >= max_blocks) {
+      set_status(status, row < 0 || row >= bt_rows ? kStatusBadRow : kStatusBadLength);
+    } else {
+      const int32_t blk = block_tables[static_cast<int64_t>(row) * bt_stride + bi];
+      if (blk < 0 || blk >= num_blocks) {
+        set_status(status, kStatusBadBlock);
+      } else {
+        slot = blk * block_size + pos % block_size;
+      }
+    }
+    context_lens[r] = pos + 1;
+    slots[r] = slot;
+  }
+  slot = __shfl_sync(0xffffffffu, slot, 0);
+  if (slot < 0) return;
+  const int32_t per = VEC ? Hkv * (D >> 3) : Hkv * D;  // vectors (or elements) per tensor
+  for (int32_t i = lane; i < 2 * per; i += 32) {
+    const bool is_v = i >= per;
+    const int32_t e = is_v ? i - per : i;
+    const int32_t h = e / (VEC ? (D >> 3) : D);
+    const int32_t c = (e % (VEC ? (D >> 3) : D)) * (VEC ? 8 : 1);
+    const Tin* src = (is_v ? v + r * v_stride : k + r * k_stride) + h * D + c;
+    Tpool* dst = (is_v ? v_pool : k_pool) + (h * pool_slots + slot) * D + c;
+    if (VEC) {
+      float x[8];
+      load8(src, x);
+      store8(dst, x);
+    } else {
+      *dst = from_float<Tpool>(as_float<Tin>(*src));
+    }
+  }
+}
+
+template <typename Tin, typename Tpool>
+int launch_decode_append_t(const int32_t* seq_rows, const int32_t* start_pos, int32_t R,
+                           const int32_t* bt, int64_t bt_stride, int32_t bt_rows,
+                           int32_t max_blocks, int32_t bs, int32_t nb, const void* k,
+                           const void* v, int64_t ks, int64_t vs, int32_t Hkv, int32_t D, void* kp,
+                           void* vp, int64_t pool_slots, bool vec, int32_t* ctx, int32_t* slots,
+                           uint32_t* status, cudaStream_t stream) {
+  if (R == 0) return 0;
+  cudaLaunchConfig_t cfg = pdl_config((R + 7) / 8, 256, stream);
+  cudaLaunchAttribute attr[1];
+  pdl_attr(cfg, attr);
+  auto kernel = vec ? decode_append_kernel<Tin, Tpool, true> : decode_append_kernel<Tin, Tpool, false>;
+  return static_cast<int>(cudaLaunchKernelEx(
+      &cfg, kernel, seq_rows, start_pos, R, bt, bt_stride, bt_rows, max_blocks, bs, nb,
+      static_cast<const Tin*>(k), static_cast<const Tin*>(v), ks, vs, Hkv, D,
+      static_cast<Tpool*>(kp), static_cast<Tpool*>(vp), pool_slots, ctx, slots, status));
+}
+
 template <typename Tin, typename Tpool>
 int launch_slot_write_t(const void* k, const void* v, int64_t ks, int64_t vs, const int32_t* slots,
                         int32_t T, int32_t Hkv, int32_t D, void* kp, void* vp, int64_t pool_slots,
@@ -263,6 +344,25 @@ int launch_step_metadata(const int32_t* seq_rows, const int32_t* start_pos, cons
   return static_cast<int>(cudaLaunchKernelEx(
       &cfg, step_metadata_kernel, seq_rows, start_pos, n_new, R, block_tables, bt_stride, bt_rows,
       max_blocks, block_size, num_blocks, T, cu_q, positions, slots, context_lens, status));
+}
+
+int launch_decode_append(const int32_t* seq_rows, const int32_t* start_pos, int32_t R,
+                         const int32_t* block_tables, int64_t bt_stride, int32_t bt_rows,
+                         int32_t max_blocks, int32_t block_size, int32_t num_blocks,
+                         const void* k, const void* v, int64_t k_stride, int64_t v_stride,
+                         int in_bf16, int32_t Hkv, int32_t D, void* k_pool, void* v_pool,
+                         int pool_bf16, int64_t pool_slots, bool vec, int32_t* context_lens,
+                         int32_t* slots, uint32_t* status, cudaStream_t stream) {
+#define BS_APPEND(TI, TP)                                                                      \
+  return launch_decode_append_t<TI, TP>(seq_rows, start_pos, R, block_tables, bt_stride,       \
+                                        bt_rows, max_blocks, block_size, num_blocks, k, v,     \
+                                        k_stride, v_stride, Hkv, D, k_pool, v_pool, pool_slots, \
+                                        vec, context_lens, slots, status, stream)
+  if (in_bf16 && pool_bf16) BS_APPEND(__nv_bfloat16, __nv_bfloat16);
+  if (in_bf16) BS_APPEND(__nv_bfloat16, float);
+  if (pool_bf16) BS_APPEND(float, __nv_bfloat16);
+  BS_APPEND(float, float);
+#undef BS_APPEND
 }
 
 // in_bf16 / pool_bf16: element types of the k/v rows and of the pool.

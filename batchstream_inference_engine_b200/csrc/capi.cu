@@ -27,6 +27,13 @@ int launch_step_metadata(const int32_t* seq_rows, const int32_t* start_pos, cons
                          int32_t num_blocks, int32_t T, int32_t* cu_q, int32_t* positions,
                          int32_t* slots, int32_t* context_lens, uint32_t* status,
                          cudaStream_t stream);
+int launch_decode_append(const int32_t* seq_rows, const int32_t* start_pos, int32_t R,
+                         const int32_t* block_tables, int64_t bt_stride, int32_t bt_rows,
+                         int32_t max_blocks, int32_t block_size, int32_t num_blocks,
+                         const void* k, const void* v, int64_t k_stride, int64_t v_stride,
+                         int in_bf16, int32_t Hkv, int32_t D, void* k_pool, void* v_pool,
+                         int pool_bf16, int64_t pool_slots, bool vec, int32_t* context_lens,
+                         int32_t* slots, uint32_t* status, cudaStream_t stream);
 int launch_slot_write(const void* k, const void* v, int64_t k_stride, int64_t v_stride,
                       int in_bf16, const int32_t* slots, int32_t T, int32_t Hkv, int32_t D,
                       void* k_pool, void* v_pool, int pool_bf16, int64_t pool_slots, bool vec,
@@ -664,6 +671,49 @@ int bs_prefill_attention(const void* query, int64_t query_token_stride, const in
   a.status = reinterpret_cast<uint32_t*>(ws);
   a.lens_ready = 0;
   return launch_decode(a, dtype, grid_max, st);
+}
+
+int bs_decode_append(const int32_t* seq_rows, const int32_t* start_pos, int64_t num_rows,
+                     const int32_t* block_tables, int64_t table_stride, int64_t table_rows,
+                     int64_t max_blocks_per_seq, const void* key, const void* value,
+                     int64_t key_row_stride, int64_t value_row_stride, int32_t input_dtype,
+                     void* key_pool, void* value_pool, int32_t pool_dtype, int64_t num_kv_heads,
+                     int64_t num_blocks, int64_t block_size, int64_t head_dim,
+                     int32_t* context_lens, int32_t* slot_mapping, uint32_t* status,
+                     void* stream) {
+  BS_CHECK(input_dtype == BS_BF16 || input_dtype == BS_F32, "input dtype must be bf16 or fp32");
+  BS_CHECK(pool_dtype == BS_BF16 || pool_dtype == BS_F32, "pool dtype must be bf16 or fp32");
+  BS_CHECK(num_rows >= 0 && num_rows <= kInt32Max, "num_rows out of range");
+  BS_CHECK(num_kv_heads > 0 && num_blocks > 0 && block_size > 0 && head_dim > 0,
+           "sizes must be positive");
+  BS_CHECK(max_blocks_per_seq > 0 && max_blocks_per_seq <= table_stride,
+           "max_blocks_per_seq must be in [1, table_stride]");
+  BS_CHECK(table_rows > 0 && table_rows <= kInt32Max, "table_rows out of range");
+  BS_CHECK(key_row_stride >= num_kv_heads * head_dim && value_row_stride >= num_kv_heads * head_dim,
+           "row strides must cover kv_heads * head_dim");
+  if (num_kv_heads * num_blocks * block_size > kInt32Max * 64ll ||
+      num_blocks * block_size > kInt32Max) {
+    return fail(BS_ERR_UNSUPPORTED, "pool too large");
+  }
+  if (num_rows == 0) return BS_OK;
+  BS_CHECK(start_pos && block_tables && key && value && key_pool && value_pool && context_lens &&
+               slot_mapping,
+           "null pointer argument");
+  const int in_sz = dtype_size(input_dtype), pool_sz = dtype_size(pool_dtype);
+  const bool vec = head_dim % 8 == 0 && aligned16(key) && aligned16(value) &&
+                   aligned16(key_pool) && aligned16(value_pool) &&
+                   (key_row_stride * in_sz) % 16 == 0 && (value_row_stride * in_sz) % 16 == 0 &&
+                   (head_dim * pool_sz) % 16 == 0;
+  const int rc = bsb::launch_decode_append(
+      seq_rows, start_pos, static_cast<int32_t>(num_rows), block_tables, table_stride,
+      static_cast<int32_t>(table_rows), static_cast<int32_t>(max_blocks_per_seq),
+      static_cast<int32_t>(block_size), static_cast<int32_t>(num_blocks), key, value,
+      key_row_stride, value_row_stride, input_dtype == BS_BF16, static_cast<int32_t>(num_kv_heads),
+      static_cast<int32_t>(head_dim), key_pool, value_pool, pool_dtype == BS_BF16,
+      num_blocks * block_size, vec, context_lens, slot_mapping, status,
+      static_cast<cudaStream_t>(stream));
+  if (rc != 0) return cuda_fail(static_cast<cudaError_t>(rc), "decode append launch");
+  return BS_OK;
 }
 
 int bs_reshape_and_cache(const void* key, const void* value, int64_t key_token_stride,

@@ -275,10 +275,59 @@ def step_metadata(block_tables: torch.Tensor, start_pos: torch.Tensor, n_new: to
     return cu_q, positions[:num_tokens], slots[:num_tokens], context[:R]
 
 
+def decode_append(key: torch.Tensor, value: torch.Tensor, key_pool: torch.Tensor,
+                  value_pool: torch.Tensor, block_tables: torch.Tensor, start_pos: torch.Tensor,
+                  seq_rows: torch.Tensor | None = None, max_blocks_per_seq: int | None = None,
+                  context_lens: torch.Tensor | None = None, slots: torch.Tensor | None = None):
+    """One decode step's K/V append in one launch: row r ([Hkv, D] of key/value)
+    lands at position start_pos[r] of its sequence.  Returns (context_lens,
+    slot_mapping) int32 [B] — what step_metadata + reshape_and_cache give for a
+    step of one new token per row (PagedKVCache.append,
+    src/server/torch_model.py:149-153, through BlockAllocator.locate)."""
+    device = _require_cuda("decode_append", key, value, key_pool, value_pool, block_tables,
+                           start_pos, seq_rows)
+    Hkv, NB, bs, D = key_pool.shape
+    B = start_pos.numel()
+    for name, t in (("block_tables", block_tables), ("start_pos", start_pos)):
+        if t.dtype != torch.int32:
+            raise RuntimeError(f"{name} must be int32")
+    if seq_rows is not None and (seq_rows.dtype != torch.int32 or seq_rows.numel() < B):
+        raise RuntimeError("seq_rows must be int32 with one entry per row")
+    if key.dtype != value.dtype or value_pool.shape != key_pool.shape:
+        raise RuntimeError("key/value dtypes or pool shapes disagree")
+    if not (key_pool.is_contiguous() and value_pool.is_contiguous()):
+        raise RuntimeError("pools must be contiguous")
+    k2 = key.reshape(key.size(0), -1) if key.dim() != 2 else key
+    v2 = value.reshape(value.size(0), -1) if value.dim() != 2 else value
+    if k2.size(0) < B or v2.size(0) < B or k2.size(1) != Hkv * D or v2.size(1) != Hkv * D:
+        raise RuntimeError("key/value must be [B, kv_heads, head_dim]")
+    if k2.stride(1) != 1:
+        k2 = k2.contiguous()
+    if v2.stride(1) != 1:
+        v2 = v2.contiguous()
+    if block_tables.stride(1) != 1:
+        block_tables = block_tables.contiguous()
+    ctx = context_lens if context_lens is not None else torch.empty(
+        max(B, 1), dtype=torch.int32, device=device)
+    sl = slots if slots is not None else torch.empty(max(B, 1), dtype=torch.int32, device=device)
+    mb = block_tables.size(1) if max_blocks_per_seq is None else int(max_blocks_per_seq)
+    ws = workspace_for(device, 0)
+    with torch.cuda.device(device):
+        stream = torch.cuda.current_stream(device).cuda_stream
+        check(lib().bs_decode_append(
+            seq_rows.data_ptr() if seq_rows is not None else None, start_pos.data_ptr(), B,
+            block_tables.data_ptr(), block_tables.stride(0), block_tables.size(0), mb,
+            k2.data_ptr(), v2.data_ptr(), k2.stride(0), v2.stride(0), dtype_code(key.dtype),
+            key_pool.data_ptr(), value_pool.data_ptr(), dtype_code(key_pool.dtype), Hkv, NB, bs, D,
+            ctx.data_ptr(), sl.data_ptr(), ws.data_ptr(), stream))
+    return ctx[:B], sl[:B]
+
+
 __all__ = [
     "paged_attention",
     "paged_attention_batched",
     "reshape_and_cache",
+    "decode_append",
     "step_metadata",
     "take_status",
     "workspace_for",

@@ -302,18 +302,28 @@ class TorchModel:
         rows = [alloc.row(cache.seq_id) for _, cache in groups]
         flat = [t for tokens, _ in groups for t in tokens]
         ends = [sum(lengths[: i + 1]) - 1 for i in range(R)]
-        staged = self._stage(rows + starts + lengths + ends + flat)
-        rows_d, start_d, n_d, ends_d, tokens_d = (staged[:R], staged[R:2 * R],
-                                                  staged[2 * R:3 * R], staged[3 * R:4 * R],
-                                                  staged[4 * R:])
-        cu_q, positions, slots, ctx = ops.step_metadata(
-            alloc.device_tables, start_d, n_d, T, pool.block_size, pool.num_blocks,
-            seq_rows=rows_d)
+        # Context lengths after the step are known here: the decode kernel gets
+        # them as final at launch (lens_ready) and partitions its work while the
+        # K/V write before it is still running.
+        after = [st + n for st, n in zip(starts, lengths)]
+        staged = self._stage(rows + starts + lengths + ends + after + flat)
+        rows_d, start_d, n_d, ends_d, ctx_d, tokens_d = (
+            staged[:R], staged[R:2 * R], staged[2 * R:3 * R], staged[3 * R:4 * R],
+            staged[4 * R:5 * R], staged[5 * R:])
         # Leading single-token rows run through the batched decode kernel, the
         # rest (prompt chunks) through the chunked-prefill kernel.
         n_dec = 0
         while n_dec < R and lengths[n_dec] == 1:
             n_dec += 1
+        decode_only = n_dec == R
+        if decode_only:
+            # One token per row: positions are the start positions, and each
+            # layer's decode_append locates the slots and writes the lengths.
+            positions, slots, ctx = start_d, None, None
+        else:
+            cu_q, positions, slots, ctx = ops.step_metadata(
+                alloc.device_tables, start_d, n_d, T, pool.block_size, pool.num_blocks,
+                seq_rows=rows_d)
         max_chunk = max(lengths[n_dec:], default=0)
         st = self.stats
         st["steps"] += 1
@@ -321,7 +331,8 @@ class TorchModel:
         st["rows"] += R
         st["attn_flops"] += config.num_layers * 4 * config.num_heads * config.head_dim * sum(
             n * s + n * (n + 1) // 2 for s, n in zip(starts, lengths))
-        st["launches"] += 1 + config.num_layers * (1 + (n_dec > 0) + (n_dec < R))
+        st["launches"] += (0 if decode_only else 1) + config.num_layers * (
+            1 + (n_dec > 0) + (n_dec < R))
         pre_cu = (cu_q[n_dec:] - n_dec) if n_dec < R else None
 
         hidden = self.embed.index_select(0, tokens_d.long())
@@ -338,12 +349,16 @@ class TorchModel:
             q = q * cos[:, None] + _rotate_half(q) * sin[:, None]
             k = k * cos[:, None] + _rotate_half(k) * sin[:, None]
             kp, vp = pool.keys[layer], pool.values[layer]
-            ops.reshape_and_cache(k, v, kp, vp, slots)
+            if decode_only:
+                ctx, slots = ops.decode_append(k, v, kp, vp, alloc.device_tables, start_d,
+                                               seq_rows=rows_d, context_lens=ctx, slots=slots)
+            else:
+                ops.reshape_and_cache(k, v, kp, vp, slots)
             attended = torch.empty((T, H, D), dtype=q.dtype, device=self.device)
             if n_dec:
-                ops.paged_attention_batched(q[:n_dec], kp, vp, alloc.device_tables, ctx[:n_dec],
+                ops.paged_attention_batched(q[:n_dec], kp, vp, alloc.device_tables, ctx_d[:n_dec],
                                             scaling, seq_rows=rows_d[:n_dec],
-                                            out=attended[:n_dec])
+                                            out=attended[:n_dec], lens_ready=True)
             if n_dec < R:
                 ops.prefill_attention(q[n_dec:], kp, vp, alloc.device_tables, pre_cu,
                                       ctx[n_dec:], scaling, max_query_len=max_chunk,

@@ -9,9 +9,9 @@ tables are random over a pool sized to 60% of the GPU's memory.  With N GPUs,
 longest-first partition into shards with equal KV tokens (weak scaling: per-GPU
 work is fixed).
 
-One step = one decode step of one layer for the whole batch: device metadata
-(positions, slots, context lengths) -> slot write of the step's new K/V token
--> split-K batched decode attention.  `value` is decode algorithmic bytes
+One step = one decode step of one layer for the whole batch: decode append
+(slot lookup through the device block tables, write of the step's new K/V
+token, context lengths) -> split-K batched decode attention.  `value` is decode algorithmic bytes
 (K/V of every context token + q + out + tables + lengths) per second over the
 whole step, max over ranks.  Four batches with disjoint random tables rotate so
 consecutive steps read different KV blocks (888 MB footprint > 126 MB L2).
@@ -242,6 +242,54 @@ def timed_replays(graphs, steps, warmup, dev, world):
     return t0.elapsed_time(t1), kernel_ms, clocks.summary()
 
 
+def capture_steps(step, rotations, dev):
+    """One CUDA graph per rotation holding a whole step (PDL edges between its
+    launches are kept inside the graph)."""
+    import torch
+
+    stream = torch.cuda.current_stream(dev)
+    capture = torch.cuda.Stream(dev)
+    capture.wait_stream(stream)
+    graphs = []
+    with torch.cuda.stream(capture):
+        for r in range(rotations):
+            step(r)
+        torch.cuda.synchronize(dev)
+        for r in range(rotations):
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=capture):
+                step(r)
+            graphs.append(g)
+    torch.cuda.synchronize(dev)
+    return graphs, capture
+
+
+def timed_graph_steps(graphs, steps, warmup, dev, world):
+    """Replays whole-step graphs; returns (total ms of `steps` steps, clocks)."""
+    import torch
+    import torch.distributed as dist
+
+    stream = torch.cuda.current_stream(dev)
+    for i in range(warmup):
+        graphs[i % len(graphs)].replay()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    with ClockSampler(dev) as clocks:
+        t0 = torch.cuda.Event(enable_timing=True)
+        t1 = torch.cuda.Event(enable_timing=True)
+        t0.record(stream)
+        torch.cuda.nvtx.range_push("timed")
+        for i in range(steps):
+            graphs[i % len(graphs)].replay()
+        torch.cuda.nvtx.range_pop()
+        t1.record(stream)
+        torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+    return t0.elapsed_time(t1), clocks.summary()
+
+
 def max_over_ranks(values, sums, dev, world):
     """Max over ranks of `values`, sum over ranks of `sums` (floats)."""
     import torch
@@ -446,25 +494,32 @@ def run_decode(args):
     k_new = torch.randn((ROTATIONS, B, Hkv, D), generator=gen, device=dev).bfloat16()
     v_new = torch.randn((ROTATIONS, B, Hkv, D), generator=gen, device=dev).bfloat16()
     start_pos = torch.tensor(lens - 1, dtype=torch.int32, device=dev)
-    n_new = torch.ones(B, dtype=torch.int32, device=dev)
     out = torch.empty((B, H, D), dtype=torch.bfloat16, device=dev)
     units = Hkv * sum(blocks)
     scale = D ** -0.5
 
+    # The host knows every context length (start + 1), so the decode kernel
+    # partitions its work before waiting on the append (lens_ready) and its
+    # prologue overlaps the append kernel (programmatic dependent launch).
+    lens_d = torch.tensor(lens, dtype=torch.int32, device=dev)
+
     def prep(r):
-        _, _, slots, ctx = ops.step_metadata(tables[r], start_pos, n_new, B, BLOCK, nb)
-        ops.reshape_and_cache(k_new[r], v_new[r], k_pool, v_pool, slots)
-        return ctx
+        ops.decode_append(k_new[r], v_new[r], k_pool, v_pool, tables[r], start_pos)
+        return lens_d
 
     def decode(r, ctx):
         ops.paged_attention_batched(q[r], k_pool, v_pool, tables[r], ctx, scale, out=out,
-                                    units_hint=units)
+                                    units_hint=units, lens_ready=True)
 
-    # Each step is replayed from two CUDA graphs (metadata + slot write, then the
-    # decode) so the device timings carry no host launch overhead.
+    # The step (append + decode) is replayed from one CUDA graph per rotation:
+    # `value` and ms_per_step.  The decode kernel alone is timed from a second
+    # set of graphs that split the step, with events between the two halves.
+    step_graphs, step_capture = capture_steps(lambda r: decode(r, prep(r)), ROTATIONS, dev)
+    total_ms, clock = timed_graph_steps(step_graphs, args.steps, args.warmup, dev, world)
     graphs, capture = capture_graphs(prep, decode, ROTATIONS, args.warmup, dev)
-    total_ms, decode_ms, clock = timed_replays(graphs, args.steps, args.warmup, dev, world)
+    _, decode_ms, _ = timed_replays(graphs, args.steps, args.warmup, dev, world)
     take_all_status(capture, dev)
+    take_all_status(step_capture, dev)
     step_bytes = algorithmic_bytes(lens, H, Hkv, D)
 
     # End to end through the public API from pinned host buffers: every step
@@ -495,8 +550,7 @@ def run_decode(args):
         ddelta.copy_(hdelta, non_blocking=True)
         flat = e2e_table.view(-1)
         flat.index_copy_(0, ddelta[0] + ddelta[1], last_entry.to(torch.int32))
-        _, _, slots, ctx = ops.step_metadata(e2e_table, dstart, n_new, B, BLOCK, nb)
-        ops.reshape_and_cache(dk, dv, k_pool, v_pool, slots)
+        ctx, _ = ops.decode_append(dk, dv, k_pool, v_pool, e2e_table, dstart)
         ops.paged_attention_batched(dq, k_pool, v_pool, e2e_table, ctx, scale, out=out,
                                     units_hint=units)
         hout.copy_(out, non_blocking=True)
@@ -532,7 +586,7 @@ def run_decode(args):
                 "pool_blocks": nb,
                 "l2": f"inputs larger than L2: {ROTATIONS} rotating batches with disjoint tables, "
                       f"{ROTATIONS * step_bytes / 1e6:.0f} MB per GPU",
-                "step": "step metadata + K/V slot write + split-K decode",
+                "step": "decode append (slot lookup + K/V write + lengths) + split-K decode",
                 "parallelism": f"dp{world} replicas, no collective on the path",
             },
             "roofline": {
@@ -550,9 +604,8 @@ def run_decode(args):
             "e2e": {"value": round(job_bytes * args.steps / (e2e_ms / 1e3) / 1e9, 1),
                     "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "ms_per_step": round(e2e_ms / args.steps, 4),
-                    "path": "pinned host -> device, metadata + slot write + decode, "
-                            "device -> pinned host"},
-            "gpu_launches": 3 * args.steps,
+                    "path": "pinned host -> device, decode append + decode, device -> pinned host"},
+            "gpu_launches": 2 * args.steps,
             "clocks": clock,
         }
     if world > 1:

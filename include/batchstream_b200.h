@@ -186,6 +186,26 @@ int bs_reshape_and_cache(const void* key, const void* value, int64_t key_token_s
                          uint32_t* status, void* stream);
 
 /*
+ * One decode step's K/V append: row r (block-table row seq_rows[r], or r when
+ * null) gains one token at position start_pos[r].  Locates its slot through
+ * the block table (BlockAllocator.locate, src/server/block_allocator.py:28-30),
+ * writes key[r] / value[r] ([num_kv_heads, head_dim], row strides in elements)
+ * into pool[h, slot / bs, slot % bs] (PagedKVCache.append,
+ * src/server/torch_model.py:149-153), and writes context_lens[r] =
+ * start_pos[r] + 1 and slot_mapping[r].  The fused form of bs_step_metadata +
+ * bs_reshape_and_cache for steps in which every row decodes one token; a
+ * table entry outside the pool or a bad row sets a status bit and skips the row.
+ */
+int bs_decode_append(const int32_t* seq_rows, const int32_t* start_pos, int64_t num_rows,
+                     const int32_t* block_tables, int64_t table_stride, int64_t table_rows,
+                     int64_t max_blocks_per_seq, const void* key, const void* value,
+                     int64_t key_row_stride, int64_t value_row_stride, int32_t input_dtype,
+                     void* key_pool, void* value_pool, int32_t pool_dtype, int64_t num_kv_heads,
+                     int64_t num_blocks, int64_t block_size, int64_t head_dim,
+                     int32_t* context_lens, int32_t* slot_mapping, uint32_t* status,
+                     void* stream);
+
+/*
  * Step metadata on the device for a ragged batch of `num_rows` rows with
  * n_new[r] new tokens after start_pos[r] cached ones (the reference builds these
  * on the host in TorchModel._hidden_states, src/server/torch_model.py:231-241,

@@ -81,6 +81,53 @@ def test_step_metadata_matches_locate():
 
 @pytest.mark.parametrize("in_dtype", [torch.float32, torch.bfloat16])
 @pytest.mark.parametrize("pool_dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("head_dim", [64, 4])
+def test_decode_append_equals_metadata_plus_slot_write(in_dtype, pool_dtype, head_dim):
+    """One fused launch gives the slots, lengths and pool contents of the
+    two-launch path, and the slots are locate()'s."""
+    alloc, lengths = grown_allocator(seed=3)
+    seqs = list(lengths)
+    start = [lengths[s] - 1 for s in seqs]  # every row decodes its last position
+    B, Hkv = len(seqs), 2
+    rows = torch.tensor([alloc.row(s) for s in seqs], dtype=torch.int32, device=DEV)
+    start_d = torch.tensor(start, dtype=torch.int32, device=DEV)
+    g = torch.Generator(device=DEV).manual_seed(7)
+    k = torch.randn((B, Hkv, head_dim), generator=g, device=DEV).to(in_dtype)
+    v = torch.randn((B, Hkv, head_dim), generator=g, device=DEV).to(in_dtype)
+    shape = (Hkv, alloc.num_blocks, 16, head_dim)
+    pools = [torch.randn(shape, generator=g, device=DEV).to(pool_dtype) for _ in range(2)]
+    ref_k, ref_v = pools[0].clone(), pools[1].clone()
+    _, _, ref_slots, ref_ctx = ops.step_metadata(alloc.device_tables, start_d,
+                                                 torch.ones(B, dtype=torch.int32, device=DEV), B,
+                                                 16, alloc.num_blocks, seq_rows=rows)
+    ops.reshape_and_cache(k, v, ref_k, ref_v, ref_slots)
+    ctx, slots = ops.decode_append(k, v, pools[0], pools[1], alloc.device_tables, start_d,
+                                   seq_rows=rows)
+    assert ops.take_status() == 0
+    assert torch.equal(slots, ref_slots) and torch.equal(ctx, ref_ctx)
+    assert torch.equal(pools[0], ref_k) and torch.equal(pools[1], ref_v)
+    _, want = oracle.slot_mapping([alloc.block_table(s) for s in seqs], start, [1] * B, 16)
+    assert slots.cpu().tolist() == want.tolist()
+
+
+def test_decode_append_bad_table_entry_sets_status():
+    alloc, lengths = grown_allocator(seed=4)
+    seqs = list(lengths)[:5]
+    start = [lengths[s] - 1 for s in seqs]
+    tables = alloc.device_tables.clone()
+    tables[alloc.row(seqs[2]), start[2] // 16] = alloc.num_blocks + 5
+    rows = torch.tensor([alloc.row(s) for s in seqs], dtype=torch.int32, device=DEV)
+    k = torch.zeros((5, 2, 64), dtype=torch.bfloat16, device=DEV)
+    pool = torch.zeros((2, alloc.num_blocks, 16, 64), dtype=torch.bfloat16, device=DEV)
+    _, slots = ops.decode_append(k, k, pool, pool.clone(), tables,
+                                 torch.tensor(start, dtype=torch.int32, device=DEV), seq_rows=rows)
+    with pytest.raises(RuntimeError, match="block table"):
+        ops.take_status()
+    assert slots[2].item() == -1 and slots[0].item() >= 0
+
+
+@pytest.mark.parametrize("in_dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("pool_dtype", [torch.float32, torch.bfloat16])
 @pytest.mark.parametrize("head_dim", [64, 128, 4])
 def test_slot_write_is_an_exact_indexed_store(in_dtype, pool_dtype, head_dim):
     g = torch.Generator(device=DEV).manual_seed(0)
