@@ -258,7 +258,9 @@ __global__ void __launch_bounds__(256)
     const int32_t pos = start_pos[r];
     const int32_t row = seq_rows != nullptr ? seq_rows[r] : r;
     const int32_t bi = pos / block_size;
-    if (row < 0 || row >= bt_rows || pos < 0 || bi >= max_blocks) {
+    if (pos < 0) {
+      // Padding row: nothing written, context length 0.
+    } else if (row < 0 || row >= bt_rows || bi >= max_blocks) {
       set_status(status, row < 0 || row >= bt_rows ? kStatusBadRow : kStatusBadLength);
     } else {
       const int32_t blk = block_tables[static_cast<int64_t>(row) * bt_stride + bi];
@@ -268,7 +270,7 @@ __global__ void __launch_bounds__(256)
         slot = blk * block_size + pos % block_size;
       }
     }
-    context_lens[r] = pos + 1;
+    context_lens[r] = pos < 0 ? 0 : pos + 1;
     slots[r] = slot;
   }
   slot = __shfl_sync(0xffffffffu, slot, 0);

@@ -71,13 +71,14 @@ __device__ __forceinline__ int32_t seq_units(const DecodeArgs& a, int32_t i, int
                                              int32_t& row, bool report) {
   len = __ldg(a.context_lens + i);
   row = a.seq_rows != nullptr ? __ldg(a.seq_rows + i) : i;
+  if (len == 0) return 0;  // padding row: nothing read, its output row left as is
   if (row < 0 || row >= a.bt_rows) {
     if (report) set_status(a.status, kStatusBadRow);
     len = 0;
     return 0;
   }
   const int64_t cap = static_cast<int64_t>(a.max_blocks) * a.block_size;
-  if (len <= 0 || len > cap) {
+  if (len < 0 || len > cap) {
     if (report) set_status(a.status, kStatusBadLength);
     len = 0;
     return 0;

@@ -5,9 +5,11 @@ every engine step each rank contributes the tokens it sampled, and one
 ``all_gather`` (NCCL over NVLink on GPUs, gloo on the CPU) gives every rank the
 whole step's tokens — the serving front end's view of all replicas.
 
-Every rank takes the same collective steps in the same order: a rank with no
-work left still joins each gather (with its ``active`` flag cleared) until all
-ranks report idle.
+The gather of step i runs on its own stream while step i + 1 computes, and is
+collected one step later, so a rank that is briefly faster does not stall on
+the others every step.  Every rank takes the same collective steps in the same
+order: a rank with no work left still joins each gather (with its ``active``
+flag cleared) until all ranks report idle.
 """
 
 from __future__ import annotations
@@ -26,36 +28,88 @@ class TokenGather:
         self.group = group
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
         self.rank = dist.get_rank(group) if dist.is_initialized() else 0
-        width = 2 + 2 * capacity
-        self._send = torch.zeros(width, dtype=torch.int32, device=self.device)
-        self._recv = torch.zeros(self.world * width, dtype=torch.int32, device=self.device)
-        self._host = torch.zeros(width, dtype=torch.int32,
-                                 pin_memory=self.device.type == "cuda")
+        self.width = 2 + 2 * capacity
+        cuda = self.device.type == "cuda"
+        # Two of each buffer: step i's gather may still be in flight while step
+        # i + 1's record is staged; a buffer is reused only after the gather
+        # that read it was waited for.
+        self._host = [torch.zeros(self.width, dtype=torch.int32, pin_memory=cuda)
+                      for _ in range(2)]
+        self._send = [torch.zeros(self.width, dtype=torch.int32, device=self.device)
+                      for _ in range(2)]
+        self._recv = [torch.zeros(self.world * self.width, dtype=torch.int32, device=self.device)
+                      for _ in range(2)]
+        self._stream = torch.cuda.Stream(self.device) if cuda else None
+        self._pending = None  # (work handle or None, buffer index) of the last submit
+        self._turn = 0
 
-    def exchange(self, active: bool, outputs: dict[int, int]) -> tuple[bool, list[dict[int, int]]]:
-        """Contributes this rank's {seq_id: token} of one step; returns (any
-        rank still active, every rank's {seq_id: token})."""
+    def _stage(self, i: int, active: bool, outputs: dict[int, int]) -> torch.Tensor:
         if len(outputs) > self.capacity:
             raise RuntimeError(f"{len(outputs)} tokens in one step, capacity {self.capacity}")
-        rec = self._host
+        rec = self._host[i]
         rec.zero_()
         rec[0] = int(active)
         rec[1] = len(outputs)
         if outputs:
             pairs = torch.tensor([v for kv in outputs.items() for v in kv], dtype=torch.int32)
             rec[2: 2 + pairs.numel()] = pairs
-        self._send.copy_(rec, non_blocking=True)
-        if self.world > 1:
-            dist.all_gather_into_tensor(self._recv, self._send, group=self.group)
-            rows = self._recv.view(self.world, -1).cpu()
-        else:
-            rows = self._send.cpu()[None]
+        return rec
+
+    def _decode(self, rows: torch.Tensor) -> tuple[bool, list[dict[int, int]]]:
         per_rank = []
         for r in range(self.world):
             n = int(rows[r, 1])
             flat = rows[r, 2: 2 + 2 * n].tolist()
             per_rank.append(dict(zip(flat[0::2], flat[1::2])))
         return bool(rows[:, 0].any()), per_rank
+
+    def _start(self, i: int, active: bool, outputs: dict[int, int]):
+        rec = self._stage(i, active, outputs)
+        if self.world == 1:
+            return None
+        send, recv = self._send[i], self._recv[i]
+        send.copy_(rec, non_blocking=True)
+        if self._stream is None:
+            return dist.all_gather_into_tensor(recv, send, group=self.group, async_op=True)
+        self._stream.wait_stream(torch.cuda.current_stream(self.device))
+        with torch.cuda.stream(self._stream):
+            return dist.all_gather_into_tensor(recv, send, group=self.group, async_op=True)
+
+    def _finish(self, work, i: int) -> tuple[bool, list[dict[int, int]]]:
+        if self.world == 1:
+            return self._decode(self._host[i][None])
+        work.wait()
+        if self._stream is not None:
+            self._stream.synchronize()
+        return self._decode(self._recv[i].view(self.world, -1).cpu())
+
+    def exchange(self, active: bool, outputs: dict[int, int]) -> tuple[bool, list[dict[int, int]]]:
+        """Contributes this rank's {seq_id: token} of one step and returns, for
+        that same step, (any rank still active, every rank's {seq_id: token})."""
+        if self._pending is not None:
+            raise RuntimeError("exchange() while a submitted gather is still pending")
+        i = self._turn
+        self._turn ^= 1
+        return self._finish(self._start(i, active, outputs), i)
+
+    def submit(self, active: bool, outputs: dict[int, int]):
+        """Starts the gather of one step without waiting for it and returns the
+        previous submitted step's result (None for the first)."""
+        i = self._turn
+        self._turn ^= 1
+        work = self._start(i, active, outputs)
+        previous = self.collect()
+        self._pending = (work, i)
+        return previous
+
+    def collect(self):
+        """Waits for the last submitted gather: (any rank active, per-rank
+        tokens), or None when nothing is pending."""
+        if self._pending is None:
+            return None
+        work, i = self._pending
+        self._pending = None
+        return self._finish(work, i)
 
 
 def shard_requests(specs: list, world: int, rank: int) -> list:

@@ -197,7 +197,8 @@ class TorchModel:
 
     def __init__(self, config: ModelConfig, weights: dict[str, torch.Tensor],
                  device: torch.device | str = "cuda", dtype: torch.dtype = torch.bfloat16,
-                 max_position: int = 32768):
+                 max_position: int = 32768, decode_graphs: bool = True,
+                 max_graph_batch: int = 256):
         self.config = config
         self.device = torch.device(device)
         self.dtype = dtype
@@ -241,6 +242,13 @@ class TorchModel:
                           d2h_bytes=0)
         self._host = None  # pinned staging buffer for per-step row metadata
         self._host_free = None  # event: the last copy out of it has completed
+        # Decode-only steps replay CUDA graphs captured per power-of-two batch
+        # size (rows padded up), on a stream no eager call uses.
+        self.decode_graphs = decode_graphs and self.device.type == "cuda"
+        self.max_graph_batch = max_graph_batch
+        self._graphs: dict[tuple[int, int], tuple] = {}
+        self._graph_stream = None
+        self._graph_pool = None
 
     @classmethod
     def load(cls, model_dir: Path, device="cuda", dtype=torch.bfloat16) -> "TorchModel":
@@ -260,7 +268,11 @@ class TorchModel:
     @torch.inference_mode()
     def next_tokens(self, groups: list[tuple[list[int], PagedKVCache]]) -> list[int]:
         """Greedy next token of each group: argmax of the float last-token
-        logits (first index on ties), reduced on the device."""
+        logits (first index on ties), reduced on the device.  A step in which
+        every group brings one token replays a captured decode graph."""
+        if (self.decode_graphs and len(groups) <= self.max_graph_batch
+                and all(len(tokens) == 1 for tokens, _ in groups)):
+            return self._graph_step(groups)
         logits = self.forward_batch(groups)
         ids = logits.float().argmax(dim=-1).to(torch.int32)
         host = torch.empty(ids.shape, dtype=torch.int32, pin_memory=True)
@@ -371,6 +383,114 @@ class TorchModel:
         for (tokens, cache) in groups:
             cache.advance(len(tokens))
         return self._rms_norm(hidden.index_select(0, ends_d.long()), self.final_norm)
+
+    # ---------------------------------------------------------------- decode graphs
+
+    def _decode_forward(self, pool: PagedKVPool, rows, start, pos, ctx, tokens) -> torch.Tensor:
+        """Greedy ids [B] (int32, on the device) of B single-token rows: row r is
+        block-table row rows[r] at position start[r] with context ctx[r] after
+        the step; start[r] < 0 and ctx[r] == 0 mark a padding row.  Launches
+        only (no host synchronisation), so it can be captured."""
+        config = self.config
+        H, Hkv, D = config.num_heads, config.num_kv_heads, config.head_dim
+        B = tokens.numel()
+        alloc = pool.allocator
+        hidden = self.embed.index_select(0, tokens.long())
+        cos = self.cos.index_select(0, pos.long())[:, None]
+        sin = self.sin.index_select(0, pos.long())[:, None]
+        ctx_w = torch.empty(B, dtype=torch.int32, device=self.device)
+        slots = torch.empty(B, dtype=torch.int32, device=self.device)
+        for layer, lw in enumerate(self.layers):
+            normed = self._rms_norm(hidden, lw["ln1"])
+            qkv = F.linear(normed, lw["qkv_w"], lw["qkv_b"])
+            q = qkv[:, : H * D].view(B, H, D)
+            k = qkv[:, H * D: (H + Hkv) * D].view(B, Hkv, D)
+            v = qkv[:, (H + Hkv) * D:].view(B, Hkv, D)
+            q = q * cos + _rotate_half(q) * sin
+            k = k * cos + _rotate_half(k) * sin
+            kp, vp = pool.keys[layer], pool.values[layer]
+            ops.decode_append(k, v, kp, vp, alloc.device_tables, start, seq_rows=rows,
+                              context_lens=ctx_w, slots=slots)
+            attended = ops.paged_attention_batched(q, kp, vp, alloc.device_tables, ctx,
+                                                   D ** -0.5, seq_rows=rows, lens_ready=True)
+            hidden = hidden + F.linear(attended.view(B, H * D), lw["o_w"])
+            normed = self._rms_norm(hidden, lw["ln2"])
+            gate, up = F.linear(normed, lw["gate_up_w"]).split(self.intermediate_size, dim=-1)
+            hidden = hidden + F.linear(F.silu(gate) * up, lw["down_w"])
+        logits = F.linear(self._rms_norm(hidden, self.final_norm), self.embed)
+        return logits.float().argmax(dim=-1).to(torch.int32)
+
+    def _capture_graphs(self, pool: PagedKVPool) -> None:
+        """Captures every power-of-two batch size up to max_graph_batch for this
+        pool, largest first, so the stream's workspace is sized before the first
+        capture and never moves afterwards."""
+        if self._graph_stream is None:
+            self._graph_stream = torch.cuda.Stream(self.device)
+            self._graph_pool = torch.cuda.graph_pool_handle()
+        sizes = []
+        b = 1
+        while b < self.max_graph_batch:
+            sizes.append(b)
+            b *= 2
+        sizes.append(self.max_graph_batch)
+        stream = self._graph_stream
+        stream.wait_stream(torch.cuda.current_stream(self.device))
+        with torch.cuda.stream(stream):
+            for B in sorted(set(sizes), reverse=True):
+                inputs = torch.zeros((5, B), dtype=torch.int32, device=self.device)
+                inputs[1].fill_(-1)  # all padding while warming up and capturing
+                for _ in range(2):
+                    self._decode_forward(pool, *inputs)
+                stream.synchronize()
+                graph = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(graph, pool=self._graph_pool, stream=stream):
+                    ids = self._decode_forward(pool, *inputs)
+                self._graphs[(id(pool), B)] = (inputs, graph, ids)
+            ops.take_status(self.device)
+        torch.cuda.current_stream(self.device).wait_stream(stream)
+
+    def _graph_step(self, groups) -> list[int]:
+        config = self.config
+        pool = groups[0][1]._pool
+        if (id(pool), 1) not in self._graphs:
+            self._capture_graphs(pool)
+        for _, cache in groups:
+            cache.reserve(1)
+        alloc = pool.allocator
+        self.stats["h2d_bytes"] += 16 * alloc.sync_device()
+        R = len(groups)
+        B = 1
+        while B < R:
+            B *= 2
+        B = min(B, self.max_graph_batch)
+        inputs, graph, ids = self._graphs[(id(pool), B)]
+        starts = [cache.length for _, cache in groups]
+        if max(starts) + 1 > self.max_position:
+            raise RuntimeError(f"positions beyond the rotary table ({self.max_position})")
+        pad = B - R
+        rows = [alloc.row(cache.seq_id) for _, cache in groups] + [0] * pad
+        values = (rows + starts + [-1] * pad + starts + [0] * pad
+                  + [s + 1 for s in starts] + [0] * pad
+                  + [tokens[0] for tokens, _ in groups] + [0] * pad)
+        inputs.view(-1).copy_(self._stage(values))
+        graph.replay()
+        host = torch.empty(R, dtype=torch.int32, pin_memory=True)
+        host.copy_(ids[:R], non_blocking=True)
+        torch.cuda.current_stream(self.device).synchronize()
+        with torch.cuda.stream(self._graph_stream):
+            ops.take_status(self.device)  # the graphs' kernels report here
+        ops.take_status(self.device)
+        for _, cache in groups:
+            cache.advance(1)
+        st = self.stats
+        st["steps"] += 1
+        st["tokens"] += R
+        st["rows"] += R
+        st["attn_flops"] += config.num_layers * 4 * config.num_heads * config.head_dim * sum(
+            s + 1 for s in starts)
+        st["launches"] += 2 * config.num_layers
+        st["d2h_bytes"] += 4 * R
+        return host.tolist()
 
     def _rms_norm(self, hidden: torch.Tensor, weight: torch.Tensor) -> torch.Tensor:
         wide = hidden.to(torch.float32)

@@ -829,11 +829,15 @@ def time_cpu_prefill(priors, heads, kv_heads, head_dim, seconds):
             "cores": min(cores, len(cases)), "kind": "port", "sample": sample}
 
 
-def engine_specs(rank: int):
+def engine_specs(world: int, rank: int):
+    """This rank's round-robin share of one global request list
+    (ENGINE_REQUESTS per GPU)."""
+    from batchstream_inference_engine_b200.replicas import shard_requests
     from batchstream_inference_engine_b200.serve import engine_workload
 
-    return engine_workload(ENGINE_REQUESTS, seed=1000 + rank, prompt_range=ENGINE_PROMPT,
-                           max_tokens_range=ENGINE_MAX_TOKENS)
+    specs = engine_workload(ENGINE_REQUESTS * world, seed=1000, prompt_range=ENGINE_PROMPT,
+                            max_tokens_range=ENGINE_MAX_TOKENS)
+    return shard_requests(specs, world, rank)
 
 
 def model_flops(stats: dict, config, vocab: int, intermediate: int) -> int:
@@ -861,17 +865,21 @@ def run_engine(args):
     model = TorchModel(QWEN25_05B, random_weights(), device=dev, dtype=torch.bfloat16)
     blocks = ENGINE_CONCURRENT * -(-(ENGINE_PROMPT[1] + ENGINE_MAX_TOKENS[1]) // BLOCK)
     backend = PagedBackend(model, blocks, BLOCK, ENGINE_PREFILL, max_seqs=ENGINE_CONCURRENT)
-    sched = OfflineScheduler(backend, engine_specs(rank), ENGINE_CONCURRENT,
+    sched = OfflineScheduler(backend, engine_specs(world, rank), ENGINE_CONCURRENT,
                              BlockBudget(blocks, BLOCK))
     gather = TokenGather(ENGINE_CONCURRENT, dev)
 
+    def tokens_in(result):
+        return 0 if result is None else sum(len(d) for d in result[1])
+
     def engine_step():
-        tokens = sched.step()
-        _, per_rank = gather.exchange(not sched.idle, tokens)
-        return sum(len(d) for d in per_rank)
+        # The step's token gather runs while the next step computes; the count
+        # returned is the previous step's (every rank's tokens).
+        return tokens_in(gather.submit(not sched.idle, sched.step()))
 
     for _ in range(args.warmup):
         engine_step()
+    gather.collect()
     stream = torch.cuda.current_stream(dev)
     if world > 1:
         dist.barrier()
@@ -884,6 +892,7 @@ def run_engine(args):
         t0.record(stream)
         for _ in range(args.steps):
             generated += engine_step()
+        generated += tokens_in(gather.collect())
         t1.record(stream)
         torch.cuda.synchronize(dev)
     if world > 1:
@@ -923,7 +932,9 @@ def run_engine(args):
                 "processed_tokens_per_s": round(job_tokens / (ms / 1e3), 1),
                 "l2": "inputs larger than L2 (weights 1 GB, KV pool per GPU "
                       f"{2 * 24 * 2 * blocks * BLOCK * 64 * 2 / 1e9:.1f} GB)",
-                "parallelism": f"dp{world} replicas, NCCL all_gather of sampled tokens per step",
+                "parallelism": f"dp{world} replicas, round-robin request shards, NCCL "
+                               f"all_gather of each step's sampled tokens (side stream, "
+                               f"collected one step later)",
             },
             "roofline": {
                 "bound": "tensor",
@@ -967,7 +978,7 @@ def time_cpu_engine(seconds, concurrent=16):
     blocks = concurrent * -(-(ENGINE_PROMPT[1] + ENGINE_MAX_TOKENS[1]) // BLOCK)
     backend = cpu_backend(random_weights(), torch.bfloat16, QWEN25_05B, blocks, BLOCK,
                           ENGINE_PREFILL, max_seqs=concurrent)
-    sched = OfflineScheduler(backend, engine_specs(0), concurrent, BlockBudget(blocks, BLOCK))
+    sched = OfflineScheduler(backend, engine_specs(1, 0), concurrent, BlockBudget(blocks, BLOCK))
     sched.step()  # warm-up
     generated, steps = 0, 0
     start = time.perf_counter()

@@ -92,6 +92,9 @@ int bs_paged_attention_workspace_bytes(int64_t num_heads, int64_t num_kv_heads, 
  * TorchModel._attention (src/server/torch_model.py:268-270 -> PagedKVCache.attend
  * :155-164).  Sequence b attends over context_lens[b] tokens whose blocks are
  * block_tables[seq_rows ? seq_rows[b] : b][0 .. ceil(len / block_size)).
+ * context_lens[b] == 0 marks a padding row (fixed-size batches, CUDA graphs):
+ * nothing is read for it and its output row is not written; a negative length,
+ * one past the table row or a bad row sets a status bit.
  * `units_hint` is the total number of (kv head, block) pairs of the batch if the
  * caller knows it, else 0; it only sizes the grid.  `flags` may hold
  * BS_LENS_READY: context_lens, block_tables and seq_rows were final before the
@@ -195,6 +198,8 @@ int bs_reshape_and_cache(const void* key, const void* value, int64_t key_token_s
  * start_pos[r] + 1 and slot_mapping[r].  The fused form of bs_step_metadata +
  * bs_reshape_and_cache for steps in which every row decodes one token; a
  * table entry outside the pool or a bad row sets a status bit and skips the row.
+ * A row with start_pos < 0 is padding (fixed-size batches, CUDA graphs):
+ * nothing is written, context_lens = 0 and slot_mapping = -1.
  */
 int bs_decode_append(const int32_t* seq_rows, const int32_t* start_pos, int64_t num_rows,
                      const int32_t* block_tables, int64_t table_stride, int64_t table_rows,

@@ -110,6 +110,25 @@ def test_decode_append_equals_metadata_plus_slot_write(in_dtype, pool_dtype, hea
     assert slots.cpu().tolist() == want.tolist()
 
 
+def test_decode_append_negative_start_is_padding():
+    alloc, lengths = grown_allocator(seed=5)
+    seqs = list(lengths)[:4]
+    start = [lengths[s] - 1 for s in seqs]
+    start[1] = -1
+    rows = torch.tensor([alloc.row(s) for s in seqs], dtype=torch.int32, device=DEV)
+    g = torch.Generator(device=DEV).manual_seed(3)
+    k = torch.randn((4, 2, 64), generator=g, device=DEV).bfloat16()
+    pool_k = torch.zeros((2, alloc.num_blocks, 16, 64), dtype=torch.bfloat16, device=DEV)
+    pool_v = torch.zeros_like(pool_k)
+    ctx, slots = ops.decode_append(k, k, pool_k, pool_v, alloc.device_tables,
+                                   torch.tensor(start, dtype=torch.int32, device=DEV),
+                                   seq_rows=rows)
+    assert ops.take_status() == 0
+    assert ctx.cpu().tolist()[1] == 0 and slots.cpu().tolist()[1] == -1
+    # Exactly the three real rows were written.
+    assert int((pool_k.abs().sum(dim=-1) > 0).sum()) == 3 * 2
+
+
 def test_decode_append_bad_table_entry_sets_status():
     alloc, lengths = grown_allocator(seed=4)
     seqs = list(lengths)[:5]

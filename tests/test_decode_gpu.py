@@ -302,6 +302,19 @@ def test_bad_device_length_sets_status_instead_of_faulting():
         ops.take_status()
 
 
+def test_zero_length_rows_are_padding():
+    lens, tables, bt, q, k, v = ragged_batch(8, 14, 2, 64, torch.bfloat16, median=150, seed=11)
+    padded = torch.tensor(lens, dtype=torch.int32, device=DEV)
+    padded[2] = 0
+    padded[5] = 0
+    out = torch.full_like(q, 7.0)
+    ops.paged_attention_batched(q, k, v, bt, padded, 0.125, out=out)
+    assert ops.take_status() == 0
+    assert bool((out[2] == 7.0).all()) and bool((out[5] == 7.0).all())
+    keep = [i for i in range(8) if i not in (2, 5)]
+    check_against_oracle(out, lens, tables, q, k, v, 7, 0.125, keep)
+
+
 def test_one_workspace_serves_calls_of_any_size_in_any_order():
     """Single-sequence and batched calls of different sizes share one workspace;
     none may leave state that disturbs the next (segment counters stay zero)."""

@@ -66,6 +66,41 @@ def test_two_ranks_gather_every_step_until_all_are_idle():
     assert stream[5] == [{}, {}]
 
 
+def _lagged_worker(rank, world, port, queue):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        gather = TokenGather(capacity=2, device="cpu")
+        results = []
+        for step in range(4):
+            prev = gather.submit(True, {rank: 10 * step + rank})
+            results.append(prev)
+        results.append(gather.collect())
+        queue.put((rank, results))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.timeout(120)
+def test_submitted_gathers_return_one_step_later():
+    ctx = mp.get_context("spawn")
+    queue = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_lagged_worker, args=(r, 2, port, queue)) for r in range(2)]
+    for p in procs:
+        p.start()
+    got = dict(queue.get(timeout=100) for _ in procs)
+    for p in procs:
+        p.join(timeout=30)
+        assert p.exitcode == 0
+    for rank in range(2):
+        res = got[rank]
+        assert res[0] is None
+        for step in range(4):
+            assert res[step + 1] == (True, [{0: 10 * step}, {1: 10 * step + 1}])
+
+
 def test_single_process_gather_without_a_process_group():
     g = TokenGather(capacity=3, device="cpu")
     active, per_rank = g.exchange(True, {7: 11, 9: 13})
@@ -84,5 +119,15 @@ def test_shard_requests_round_robin():
 def test_gather_record_layout():
     g = TokenGather(capacity=2, device="cpu")
     g.exchange(False, {5: 6})
-    assert g._host.tolist() == [0, 1, 5, 6, 0, 0]
-    assert torch.equal(g._send, g._host)
+    assert g._host[0].tolist() == [0, 1, 5, 6, 0, 0]
+    # Turns alternate between the two buffers.
+    g.exchange(True, {})
+    assert g._host[1].tolist() == [1, 0, 0, 0, 0, 0]
+
+
+def test_exchange_refuses_to_overtake_a_pending_submit():
+    g = TokenGather(capacity=2, device="cpu")
+    assert g.submit(True, {1: 2}) is None
+    with pytest.raises(RuntimeError):
+        g.exchange(True, {})
+    assert g.collect() == (True, [{1: 2}])
