@@ -10,8 +10,10 @@
 // the query tiles with the most keys start first.  Three roles, one warp each
 // for the first two:
 //   * loader (warp 5): the query tile as one TMA box of a [T, H, D] tensor map,
-//     then the sequence's K and V through the block table into two 3-stage
-//     rings (64 keys = 4 blocks per stage, one TMA box per block).  A K stage is
+//     then the sequence's K and V through the block table into a 4-stage K ring
+//     and a 3-stage V ring (64 keys = 4 blocks per stage, one TMA box per block).
+//     The loads are latency-bound (the pool is mostly read from L2), so the
+//     rings are as deep as two CTAs per SM allow.  A K stage is
 //     refilled once the S product that read it has completed, a V stage once
 //     its P V product has; K runs two tiles ahead of V, which gives either load
 //     about three softmax periods to land.  Block-table entries come from a
@@ -44,12 +46,14 @@ namespace {
 constexpr int kRows = 128;   // query rows per CTA (TMEM lanes)
 constexpr int kKeys = 64;    // keys per KV tile (4 blocks)
 constexpr int kD = 64;
-constexpr int kStages = 3;
+constexpr int kKStages = 4;  // K ring depth
+constexpr int kVStages = 3;  // V ring depth
 constexpr int kThreads = 192;  // warps 0-3 softmax, warp 4 MMA issuer, warp 5 loader
 constexpr int kTileBytes = kKeys * kD * 2;  // 8 KiB: K or V of one tile
 constexpr int kQBytes = kRows * kD * 2;     // 16 KiB
 constexpr int kPBytes = kRows * kKeys * 2;  // 16 KiB per P buffer
-constexpr int kSmemBytes = 1024 + kQBytes + kStages * 2 * kTileBytes + 2 * kPBytes;
+constexpr int kSmemBytes =
+    1024 + kQBytes + (kKStages + kVStages) * kTileBytes + 2 * kPBytes;
 constexpr uint32_t kTmemCols = 256;  // S0 [0, 64), S1 [64, 128), O [128, 192)
 constexpr uint32_t kTmemO = 128;
 constexpr float kLog2eP = 1.4426950408889634f;
@@ -166,17 +170,19 @@ __global__ void __launch_bounds__(kThreads, 2)
   // o_full completes once per P V product (the rescale waits for the previous
   // tile's); o_last once, after the last one: a parity wait on o_full could not
   // tell "done" from "two products behind" at the end.
-  __shared__ uint64_t q_full, k_full[kStages], k_empty[kStages], v_full[kStages],
-      v_empty[kStages], s_full[2], p_full[2], o_full, o_last, mma_done;
+  __shared__ uint64_t q_full, k_full[kKStages], k_empty[kKStages], v_full[kVStages],
+      v_empty[kVStages], s_full[2], p_full[2], o_full, o_last, mma_done;
   __shared__ uint32_t tmem_base;
 
   const uint32_t raw = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + (((raw + 1023u) & ~1023u) - raw);
   uint8_t* sQ = smem;
-  // Stage st holds K at sK(st) and V right after it; P buffer b at sP(b).
-  auto sK = [&](int st) { return smem + kQBytes + st * 2 * kTileBytes; };
-  auto sV = [&](int st) { return smem + kQBytes + st * 2 * kTileBytes + kTileBytes; };
-  auto sP = [&](int b) { return smem + kQBytes + kStages * 2 * kTileBytes + b * kPBytes; };
+  // K ring, then V ring, then the two P buffers.
+  auto sK = [&](int st) { return smem + kQBytes + st * kTileBytes; };
+  auto sV = [&](int st) { return smem + kQBytes + (kKStages + st) * kTileBytes; };
+  auto sP = [&](int b) {
+    return smem + kQBytes + (kKStages + kVStages) * kTileBytes + b * kPBytes;
+  };
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   pdl_wait();
@@ -203,9 +209,11 @@ __global__ void __launch_bounds__(kThreads, 2)
 
   if (tid == 0) {
     mbar_init(&q_full, 1);
-    for (int s = 0; s < kStages; ++s) {
+    for (int s = 0; s < kKStages; ++s) {
       mbar_init(&k_full[s], 1);
       mbar_init(&k_empty[s], 1);
+    }
+    for (int s = 0; s < kVStages; ++s) {
       mbar_init(&v_full[s], 1);
       mbar_init(&v_empty[s], 1);
     }
@@ -276,10 +284,10 @@ __global__ void __launch_bounds__(kThreads, 2)
       // V(i - 2)'s blocks, taken before K(i) (same parity) replaces them.
       const int32_t vblk = (i & 1) ? hold_odd : hold_even;
       if (i < ntiles) {
-        const int st = i % kStages;
-        if (i >= kStages) {
-          // K stage st is free once S of tile i - 3 has read it.
-          ok = wait_all(&k_empty[st], ((i - kStages) / kStages) & 1);
+        const int st = i % kKStages;
+        if (i >= kKStages) {
+          // K stage st is free once S of tile i - kKStages has read it.
+          ok = wait_all(&k_empty[st], ((i - kKStages) / kKStages) & 1);
           if (!ok) break;
         }
         if ((i * 4) / 32 != win) {
@@ -294,10 +302,10 @@ __global__ void __launch_bounds__(kThreads, 2)
       }
       const int t = i - 2;
       if (t >= 0 && t < ntiles) {
-        const int st = t % kStages;
-        if (t >= kStages) {
-          // V stage st is free once P V of tile t - 3 has read it.
-          ok = wait_all(&v_empty[st], ((t - kStages) / kStages) & 1);
+        const int st = t % kVStages;
+        if (t >= kVStages) {
+          // V stage st is free once P V of tile t - kVStages has read it.
+          ok = wait_all(&v_empty[st], ((t - kVStages) / kVStages) & 1);
           if (!ok) break;
         }
         load(&vmap, sV(st), &v_full[st], vblk);
@@ -306,18 +314,18 @@ __global__ void __launch_bounds__(kThreads, 2)
     }
     // Drain: the loads of the last stages still hold their newest phase.
     bool drained = wait_all(&q_full, 0);
-    for (int t = max(0, k_loads - kStages); t < k_loads; ++t) {
-      drained = wait_all(&k_full[t % kStages], (t / kStages) & 1) && drained;
+    for (int t = max(0, k_loads - kKStages); t < k_loads; ++t) {
+      drained = wait_all(&k_full[t % kKStages], (t / kKStages) & 1) && drained;
     }
-    for (int t = max(0, v_loads - kStages); t < v_loads; ++t) {
-      drained = wait_all(&v_full[t % kStages], (t / kStages) & 1) && drained;
+    for (int t = max(0, v_loads - kVStages); t < v_loads; ++t) {
+      drained = wait_all(&v_full[t % kVStages], (t / kVStages) & 1) && drained;
     }
     if ((!ok || !drained) && lane == 0) set_status(a.status, kStatusWaitTimeout);
   } else if (warp == 4) {
     // ---------------------------------------------------------------- MMA issuer
     auto issue_s = [&](int j) {
       if (lane == 0) {
-        const int st = j % kStages;
+        const int st = j % kKStages;
         const uint32_t d = tmem + (j & 1) * kKeys;
 #pragma unroll
         for (int k = 0; k < kD / 16; ++k) {
@@ -332,14 +340,14 @@ __global__ void __launch_bounds__(kThreads, 2)
     bool ok = wait_all(&q_full, 0);
     // Scores of the first two tiles.
     for (int j = 0; j < 2 && j < ntiles && ok; ++j) {
-      ok = wait_all(&k_full[j % kStages], (j / kStages) & 1);
+      ok = wait_all(&k_full[j % kKStages], (j / kKStages) & 1);
       if (!ok) break;
       tc_fence_after();
       issue_s(j);
     }
     for (int j = 0; j < ntiles && ok; ++j) {
-      const int st = j % kStages;
-      ok = wait_all(&p_full[j & 1], (j >> 1) & 1) && wait_all(&v_full[st], (j / kStages) & 1);
+      const int st = j % kVStages;
+      ok = wait_all(&p_full[j & 1], (j >> 1) & 1) && wait_all(&v_full[st], (j / kVStages) & 1);
       if (!ok) break;
       tc_fence_after();
       if (lane == 0) {
@@ -357,7 +365,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       __syncwarp();
       if (j + 2 < ntiles) {
         // S buffer j & 1 is free: softmax(j) read it before arriving on p_full.
-        ok = wait_all(&k_full[(j + 2) % kStages], ((j + 2) / kStages) & 1);
+        ok = wait_all(&k_full[(j + 2) % kKStages], ((j + 2) / kKStages) & 1);
         if (!ok) break;
         tc_fence_after();
         issue_s(j + 2);
@@ -472,12 +480,12 @@ __global__ void __launch_bounds__(kThreads, 2)
       // memory, possibly NaN, which would poison 0 * V in the tensor core.
       if (j == ntiles - 1 && row < kKeys && key0 + kKeys > kv_end) {
         // The V tile must have landed before its tail rows are overwritten.
-        ok = wait_all(&v_full[j % kStages], (j / kStages) & 1);
+        ok = wait_all(&v_full[j % kVStages], (j / kVStages) & 1);
         if (!ok) break;
       }
       if (row < kKeys && key0 + row >= kv_end) {
         uint4 z = make_uint4(0u, 0u, 0u, 0u);
-        uint8_t* vrow = sV(j % kStages) + row * 128;
+        uint8_t* vrow = sV(j % kVStages) + row * 128;
 #pragma unroll
         for (int c = 0; c < 8; ++c) *reinterpret_cast<uint4*>(vrow + c * 16) = z;
       }
