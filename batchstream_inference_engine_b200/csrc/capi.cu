@@ -138,6 +138,7 @@ int32_t record_stride(int64_t groups, int64_t head_dim) {
 constexpr int64_t kMaxSegments = 1 << 16;
 
 struct WsLayout {
+  int64_t tasks;  // [grid] merge tasks of the tensor-core decode
   int64_t counters, staging, partials, total;
 };
 
@@ -147,7 +148,8 @@ WsLayout ws_layout(int64_t segments, int64_t staging_ints, int64_t grid, int64_t
   w.counters = 256;
   w.staging = w.counters + kMaxSegments * 4;
   w.partials = w.staging + round_up(staging_ints * 4, 256);
-  w.total = w.partials + round_up(2 * grid * rec_stride * 4, 256);
+  w.tasks = w.partials + round_up(2 * grid * rec_stride * 4, 256);
+  w.total = w.tasks + round_up(grid * static_cast<int64_t>(sizeof(bsb::MergeTask)), 256);
   return w;
 }
 
@@ -273,8 +275,10 @@ int cached_pool_map(CUtensorMap* out, const void* base, int64_t rows, int64_t he
   return BS_OK;
 }
 
-int launch_decode(bsb::DecodeArgs& a, int32_t dtype, int grid, cudaStream_t stream) {
+int launch_decode(bsb::DecodeArgs& a, int32_t dtype, int grid, cudaStream_t stream,
+                  bsb::MergeTask* tasks) {
   const bool mma = use_mma_path(dtype, a.block_size, a.head_dim, a.groups);
+  a.tasks = mma ? tasks : nullptr;
   int rc;
   if (mma) {
     CUtensorMap kmap, vmap;
@@ -420,7 +424,8 @@ int bs_paged_attention(const void* query, int32_t query_dtype, int32_t query_ndi
   int64_t grid = (units + 7) / 8;
   if (grid < 1) grid = 1;
   if (grid > grid_max) grid = grid_max;
-  return launch_decode(a, query_dtype, static_cast<int>(grid), st);
+  return launch_decode(a, query_dtype, static_cast<int>(grid), st,
+                       reinterpret_cast<bsb::MergeTask*>(ws + w.tasks));
 }
 
 int bs_paged_attention_batched_workspace_bytes(int64_t num_seqs, int64_t num_heads,
@@ -449,7 +454,9 @@ int bs_paged_attention_batched(const void* query, int64_t query_seq_stride, cons
                                int64_t output_seq_stride, void* workspace,
                                uint64_t workspace_bytes, void* stream) {
   BS_CHECK(dtype == BS_BF16 || dtype == BS_F32, "dtype must be bfloat16 or float32");
-  BS_CHECK((flags & ~BS_LENS_READY) == 0, "unknown flags");
+  BS_CHECK((flags & ~(BS_LENS_READY | BS_AFTER_APPEND)) == 0, "unknown flags");
+  BS_CHECK(!(flags & BS_AFTER_APPEND) || (flags & BS_LENS_READY),
+           "BS_AFTER_APPEND needs BS_LENS_READY");
   BS_CHECK(num_seqs >= 0, "num_seqs must be non-negative");
   BS_CHECK(num_kv_heads > 0 && num_heads > 0 && num_heads % num_kv_heads == 0,
            "heads must equal kv_heads * groups");
@@ -516,12 +523,14 @@ int bs_paged_attention_batched(const void* query, int64_t query_seq_stride, cons
   a.seg_counters = reinterpret_cast<int32_t*>(ws + w.counters);
   a.status = reinterpret_cast<uint32_t*>(ws);
   a.lens_ready = (flags & BS_LENS_READY) ? 1 : 0;
+  a.after_append = (flags & BS_AFTER_APPEND) ? 1 : 0;
   int64_t grid = grid_max;
   if (units_hint > 0) {
     const int64_t want = (units_hint + 3) / 4;
     if (want < grid) grid = want;
   }
-  return launch_decode(a, dtype, static_cast<int>(grid), static_cast<cudaStream_t>(stream));
+  return launch_decode(a, dtype, static_cast<int>(grid), static_cast<cudaStream_t>(stream),
+                       reinterpret_cast<bsb::MergeTask*>(ws + w.tasks));
 }
 
 int bs_prefill_attention_workspace_bytes(int64_t num_tokens, int64_t num_heads,
@@ -670,7 +679,7 @@ int bs_prefill_attention(const void* query, int64_t query_token_stride, const in
   a.seg_counters = reinterpret_cast<int32_t*>(ws + w.counters);
   a.status = reinterpret_cast<uint32_t*>(ws);
   a.lens_ready = 0;
-  return launch_decode(a, dtype, grid_max, st);
+  return launch_decode(a, dtype, grid_max, st, reinterpret_cast<bsb::MergeTask*>(ws + w.tasks));
 }
 
 int bs_decode_append(const int32_t* seq_rows, const int32_t* start_pos, int64_t num_rows,

@@ -27,6 +27,13 @@ namespace bsb {
 
 constexpr float kLog2e = 1.4426950408889634f;
 
+// A segment cut across CTAs, to be merged after the decode kernel: written by
+// the CTA that holds its last unit (every CTA writes its entry every launch).
+struct MergeTask {
+  int64_t seg_unit, q, rem;  // first unit, and the span split of the launch
+  int32_t seq, kvh, nb, valid;
+};
+
 struct DecodeArgs {
   const void* q;         // [B, H, D]; heads of one sequence contiguous (stride D)
   int64_t q_stride_seq;  // elements between sequences
@@ -50,6 +57,13 @@ struct DecodeArgs {
   // kernel launched just ahead of this one: the span search may then overlap it
   // (programmatic dependent launch); query and pools are read only after it.
   int32_t lens_ready;
+  // With lens_ready: the kernel just ahead wrote at most each sequence's last
+  // pool block, so other blocks and the query may be loaded before it ends.
+  int32_t after_append;
+  // [grid] merge tasks.  When set (tensor-core kernel), cut segments are merged
+  // by decode_merge_kernel after the decode kernel instead of by the last CTA
+  // to finish (atomic counters).
+  MergeTask* tasks;
 };
 
 // Units of a sequence from its raw length and table row (already loaded);
@@ -357,9 +371,8 @@ __device__ __forceinline__ Span compute_warp_spans(const DecodeArgs& a, ScanSmem
 // this CTA's record (O unnormalised, M, L for the G rows; o/m/l in shared memory,
 // O row-major [G][D]) and counts the CTA in.  Returns true (on every lane) when
 // this CTA was the last contributor, which then owes the segment's final merge.
-__device__ __forceinline__ bool warp_write_record(const DecodeArgs& a, const Span& sp,
-                                                  int32_t seq, int32_t kvh, int64_t seg_unit,
-                                                  int32_t nb, const float* o, const float* m,
+__device__ __forceinline__ void warp_store_record(const DecodeArgs& a, const Span& sp,
+                                                  int64_t seg_unit, const float* o, const float* m,
                                                   const float* l, int lane) {
   const int G = a.groups, D = a.head_dim;
   float* rec = a.partials + record_index(blockIdx.x, seg_unit, sp.q, sp.rem) * a.rec_stride;
@@ -368,6 +381,13 @@ __device__ __forceinline__ bool warp_write_record(const DecodeArgs& a, const Spa
     rec[G * D + r] = m[r];
     rec[G * D + G + r] = l[r];
   }
+}
+
+__device__ __forceinline__ bool warp_write_record(const DecodeArgs& a, const Span& sp,
+                                                  int32_t seq, int32_t kvh, int64_t seg_unit,
+                                                  int32_t nb, const float* o, const float* m,
+                                                  const float* l, int lane) {
+  warp_store_record(a, sp, seg_unit, o, m, l, lane);
   __threadfence();
   __syncwarp();
   const int64_t segi = static_cast<int64_t>(seq) * a.num_kv_heads + kvh;

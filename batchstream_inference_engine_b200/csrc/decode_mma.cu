@@ -74,6 +74,7 @@ __global__ void __launch_bounds__(Cfg<D, G16>::W * 32, Cfg<D, G16>::MIN_CTAS)
   __shared__ int64_t slot_unit[W][2];
   // Segments whose last record this CTA wrote: merged by the whole CTA.
   __shared__ int32_t fin_count;
+  __shared__ MergeTask task;  // the cut segment this CTA finishes (tasks mode)
   __shared__ int32_t fin_seq[2 * W], fin_kvh[2 * W], fin_nb[2 * W];
   __shared__ int64_t fin_unit[2 * W];
 
@@ -95,11 +96,21 @@ __global__ void __launch_bounds__(Cfg<D, G16>::W * 32, Cfg<D, G16>::MIN_CTAS)
     prefetch_tensormap(&vmap);
   }
   if (tid < W * 2) slot_seq[tid / 2][tid % 2] = -1;
-  if (tid == 0) fin_count = 0;
+  if (tid == 0) {
+    fin_count = 0;
+    task.valid = 0;
+  }
+  pdl_trigger();  // the merge pass may launch now; it waits for this grid
+  // lens_ready: the work split overlaps the kernel just ahead; after_append:
+  // so do the first loads of blocks that kernel cannot have written.
+  const bool early_loads = a.lens_ready && a.after_append;
   if (!a.lens_ready) pdl_wait();
   const Span sp = compute_warp_spans<W>(a, scan, starts);  // syncs the inits
-  if (a.lens_ready) pdl_wait();  // query, pools and tables' contents from here on
-  if (sp.r0 >= sp.r1) return;
+  if (a.lens_ready && !early_loads) pdl_wait();  // query, pools from here on
+  if (sp.r0 >= sp.r1) {
+    if (a.tasks != nullptr && tid == 0) a.tasks[blockIdx.x].valid = 0;
+    return;
+  }
 
   const int G = a.groups;
   const int64_t Hkv = a.num_kv_heads;
@@ -198,7 +209,14 @@ __global__ void __launch_bounds__(Cfg<D, G16>::W * 32, Cfg<D, G16>::MIN_CTAS)
     }
   };
 
-  for (int s = 0; s < S && s < ntiles; ++s) issue(s);
+  int issued = 0;
+  if (early_loads) {
+    // Stages up to (not including) the first block that ends a segment: the
+    // append ahead may still be writing that one.
+    for (; issued < S && issued < ntiles && cb != cnb - 1; ++issued) issue(issued);
+    pdl_wait();
+  }
+  for (; issued < S && issued < ntiles; ++issued) issue(issued);
 
   // ---------------------------------------------------------------- compute
   const int g = lane >> 2, t = lane & 3;
@@ -451,6 +469,19 @@ __global__ void __launch_bounds__(Cfg<D, G16>::W * 32, Cfg<D, G16>::MIN_CTAS)
       for (int e = lane; e < G * D; e += 32) {
         out[e] = __float2bfloat16_rn(mine[e] / mine[G * D + G + e / D]);
       }
+    } else if (a.tasks != nullptr) {
+      // Cut across CTAs: leave this CTA's record; the segment is merged after
+      // the kernel, listed by the CTA that holds its last unit.
+      warp_store_record(a, sp, seg_unit, mine, mine + G * D, mine + G * D + G, lane);
+      if (lane == 0 && seg_unit < sp.r0 && seg_unit + nb <= sp.r1) {
+        task.seg_unit = seg_unit;
+        task.q = sp.q;
+        task.rem = sp.rem;
+        task.seq = seq;
+        task.kvh = kvh;
+        task.nb = nb;
+        task.valid = 1;
+      }
     } else if (warp_write_record(a, sp, seq, kvh, seg_unit, nb, mine, mine + G * D,
                                  mine + G * D + G, lane)) {
       if (lane == 0) {
@@ -465,6 +496,10 @@ __global__ void __launch_bounds__(Cfg<D, G16>::W * 32, Cfg<D, G16>::MIN_CTAS)
   // Segments crossing CTAs for which this CTA came last: merge with all threads.
   // The stages and slots are free now and serve as scratch.
   __syncthreads();
+  if (a.tasks != nullptr) {
+    if (tid == 0) a.tasks[blockIdx.x] = task;
+    return;
+  }
   const int nfin = fin_count;
   for (int f = 0; f < nfin; ++f) {
     cta_merge_records<__nv_bfloat16>(a, sp, fin_seq[f], fin_kvh[f], fin_unit[f], fin_nb[f],
@@ -497,6 +532,19 @@ int launch_one(const DecodeArgs& a, const CUtensorMap& kmap, const CUtensorMap& 
   return static_cast<int>(cudaLaunchKernelEx(&cfg, decode_mma_kernel<D, G16>, kmap, vmap, a));
 }
 
+// Merges, after the decode kernel, the cut segments its CTAs listed: one CTA
+// per decode CTA, all threads on the records of one segment.
+__global__ void __launch_bounds__(128) decode_merge_kernel(const DecodeArgs a) {
+  extern __shared__ float merge_scratch[];
+  pdl_wait();
+  const MergeTask t = a.tasks[blockIdx.x];
+  if (!t.valid) return;
+  Span sp{};
+  sp.q = t.q;
+  sp.rem = t.rem;
+  cta_merge_records<__nv_bfloat16>(a, sp, t.seq, t.kvh, t.seg_unit, t.nb, merge_scratch);
+}
+
 template <int D, bool G16>
 int occupancy_one() {
   using C = Cfg<D, G16>;
@@ -515,11 +563,35 @@ int occupancy_one() {
 int launch_decode_mma(const DecodeArgs& a, const CUtensorMap& kmap, const CUtensorMap& vmap,
                       int grid, cudaStream_t stream) {
   const bool g16 = a.groups > 8;
+  int rc;
   if (a.head_dim == 64)
-    return g16 ? launch_one<64, true>(a, kmap, vmap, grid, stream)
-               : launch_one<64, false>(a, kmap, vmap, grid, stream);
-  return g16 ? launch_one<128, true>(a, kmap, vmap, grid, stream)
+    rc = g16 ? launch_one<64, true>(a, kmap, vmap, grid, stream)
+             : launch_one<64, false>(a, kmap, vmap, grid, stream);
+  else
+    rc = g16 ? launch_one<128, true>(a, kmap, vmap, grid, stream)
              : launch_one<128, false>(a, kmap, vmap, grid, stream);
+  if (rc != 0 || a.tasks == nullptr) return rc;
+  // Merge pass: at most `grid` records per segment.
+  const int smem = static_cast<int>((2 * static_cast<int64_t>(grid) * a.groups + 2 * a.groups) *
+                                    sizeof(float));
+  static int configured_smem = 0;
+  if (smem > configured_smem) {
+    cudaError_t e = cudaFuncSetAttribute(decode_merge_kernel,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return static_cast<int>(e);
+    configured_smem = smem;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(128);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return static_cast<int>(cudaLaunchKernelEx(&cfg, decode_merge_kernel, a));
 }
 
 int decode_mma_ctas_per_sm(int head_dim, int groups) {

@@ -153,7 +153,8 @@ def paged_attention_batched(query: torch.Tensor, key_pool: torch.Tensor, value_p
                             block_tables: torch.Tensor, context_lens: torch.Tensor, scaling: float,
                             seq_rows: torch.Tensor | None = None, out: torch.Tensor | None = None,
                             max_blocks_per_seq: int | None = None,
-                            units_hint: int = 0, lens_ready: bool = False) -> torch.Tensor:
+                            units_hint: int = 0, lens_ready: bool = False,
+                            after_append: bool = False) -> torch.Tensor:
     """Decode attention for a whole ragged batch in one launch.
 
     query [B, H, D]; key_pool/value_pool [Hkv, NB, bs, D] (one layer of the
@@ -205,7 +206,7 @@ def paged_attention_batched(query: torch.Tensor, key_pool: torch.Tensor, value_p
             block_tables.data_ptr(), block_tables.stride(0), block_tables.size(0),
             seq_rows.data_ptr() if seq_rows is not None else None, context_lens.data_ptr(),
             B, H, Hkv, D, bs, NB, mb, code, float(scaling), int(units_hint),
-            1 if lens_ready else 0, out.data_ptr(),
+            (1 if lens_ready else 0) | (2 if after_append else 0), out.data_ptr(),
             out.stride(0), ws.data_ptr(), ws.numel(), stream))
     return out
 

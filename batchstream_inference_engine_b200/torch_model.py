@@ -370,7 +370,8 @@ class TorchModel:
             if n_dec:
                 ops.paged_attention_batched(q[:n_dec], kp, vp, alloc.device_tables, ctx_d[:n_dec],
                                             scaling, seq_rows=rows_d[:n_dec],
-                                            out=attended[:n_dec], lens_ready=True)
+                                            out=attended[:n_dec], lens_ready=True,
+                                            after_append=True)
             if n_dec < R:
                 ops.prefill_attention(q[n_dec:], kp, vp, alloc.device_tables, pre_cu,
                                       ctx[n_dec:], scaling, max_query_len=max_chunk,
@@ -412,7 +413,8 @@ class TorchModel:
             ops.decode_append(k, v, kp, vp, alloc.device_tables, start, seq_rows=rows,
                               context_lens=ctx_w, slots=slots)
             attended = ops.paged_attention_batched(q, kp, vp, alloc.device_tables, ctx,
-                                                   D ** -0.5, seq_rows=rows, lens_ready=True)
+                                                   D ** -0.5, seq_rows=rows, lens_ready=True,
+                                                   after_append=True)
             hidden = hidden + F.linear(attended.view(B, H * D), lw["o_w"])
             normed = self._rms_norm(hidden, lw["ln2"])
             gate, up = F.linear(normed, lw["gate_up_w"]).split(self.intermediate_size, dim=-1)

@@ -499,8 +499,9 @@ def run_decode(args):
     scale = D ** -0.5
 
     # The host knows every context length (start + 1), so the decode kernel
-    # partitions its work before waiting on the append (lens_ready) and its
-    # prologue overlaps the append kernel (programmatic dependent launch).
+    # partitions its work before waiting on the append (lens_ready), and the
+    # append writes only each sequence's last block, so the first loads of the
+    # other blocks overlap it too (after_append; programmatic dependent launch).
     lens_d = torch.tensor(lens, dtype=torch.int32, device=dev)
 
     def prep(r):
@@ -509,7 +510,7 @@ def run_decode(args):
 
     def decode(r, ctx):
         ops.paged_attention_batched(q[r], k_pool, v_pool, tables[r], ctx, scale, out=out,
-                                    units_hint=units, lens_ready=True)
+                                    units_hint=units, lens_ready=True, after_append=True)
 
     # The step (append + decode) is replayed from one CUDA graph per rotation:
     # `value` and ms_per_step.  The decode kernel alone is timed from a second

@@ -102,6 +102,11 @@ int bs_paged_attention_workspace_bytes(int64_t num_heads, int64_t num_kv_heads, 
  * search may overlap that kernel (query and pools are always read after it).
  */
 #define BS_LENS_READY 0x1
+/* With BS_LENS_READY: the kernel launched just ahead wrote nothing this call
+ * reads except, at most, each sequence's last pool block (a decode append or
+ * slot write of the step's new token), so every other block and the query
+ * may be read before it finishes. */
+#define BS_AFTER_APPEND 0x2
 int bs_paged_attention_batched(const void* query, int64_t query_seq_stride, const void* key_pool,
                                const void* value_pool, const int32_t* block_tables,
                                int64_t table_stride, int64_t table_rows, const int32_t* seq_rows,

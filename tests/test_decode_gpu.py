@@ -302,6 +302,30 @@ def test_bad_device_length_sets_status_instead_of_faulting():
         ops.take_status()
 
 
+def test_early_loads_after_an_append_give_the_same_bits():
+    # Decode launched right behind the append that writes each sequence's new
+    # token, with the first loads of the other blocks issued before it ends.
+    lens, tables, bt, q, k, v = ragged_batch(48, 14, 2, 64, torch.bfloat16, median=400, seed=13)
+    B = len(lens)
+    g = torch.Generator(device=DEV).manual_seed(5)
+    k_new = torch.randn((B, 2, 64), generator=g, device=DEV).bfloat16()
+    v_new = torch.randn((B, 2, 64), generator=g, device=DEV).bfloat16()
+    start = torch.tensor([n - 1 for n in lens], dtype=torch.int32, device=DEV)
+    lens_d = torch.tensor(lens, dtype=torch.int32, device=DEV)
+    k1, v1 = k.clone(), v.clone()
+    ops.decode_append(k_new, v_new, k1, v1, bt, start)
+    plain = ops.paged_attention_batched(q, k1, v1, bt, lens_d, 0.125)
+    k2, v2 = k.clone(), v.clone()
+    for _ in range(3):
+        ops.decode_append(k_new, v_new, k2, v2, bt, start)
+        early = ops.paged_attention_batched(q, k2, v2, bt, lens_d, 0.125, lens_ready=True,
+                                            after_append=True)
+        assert torch.equal(early, plain)
+    assert ops.take_status() == 0
+    with pytest.raises(RuntimeError, match="BS_LENS_READY"):
+        ops.paged_attention_batched(q, k2, v2, bt, lens_d, 0.125, after_append=True)
+
+
 def test_zero_length_rows_are_padding():
     lens, tables, bt, q, k, v = ragged_batch(8, 14, 2, 64, torch.bfloat16, median=150, seed=11)
     padded = torch.tensor(lens, dtype=torch.int32, device=DEV)
