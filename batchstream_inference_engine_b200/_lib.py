@@ -29,6 +29,10 @@ EXPORTS = (
     "bs_decode_append",
     "bs_step_metadata",
     "bs_take_status",
+    "bs_rms_norm",
+    "bs_rope_append",
+    "bs_silu_mul",
+    "bs_kernel_launches",
 )
 
 _i32, _i64, _u64, _p, _dbl = ctypes.c_int32, ctypes.c_int64, ctypes.c_uint64, ctypes.c_void_p, ctypes.c_double
@@ -82,6 +86,17 @@ _SIGNATURES = {
         ctypes.c_int,
     ),
     "bs_take_status": ([_p, _p, ctypes.POINTER(ctypes.c_uint32)], ctypes.c_int),
+    "bs_rms_norm": (
+        [_p, _i64, _i64, _p, _i64, _p, _p, _i64, _i64, _dbl, _i32, _p, _i64, _p, _i64, _p, _p],
+        ctypes.c_int,
+    ),
+    "bs_rope_append": (
+        [_p, _i64, _i32, _p, _p, _i64, _p, _p, _i64, _i64, _i64, _i64, _p, _p, _p, _i32, _i64,
+         _i64, _p, _p],
+        ctypes.c_int,
+    ),
+    "bs_silu_mul": ([_p, _i64, _i64, _i64, _i32, _p, _p], ctypes.c_int),
+    "bs_kernel_launches": ([], ctypes.c_uint64),
 }
 
 _lib: ctypes.CDLL | None = None

@@ -274,7 +274,7 @@ __global__ void __launch_bounds__(256)
     slots[r] = slot;
   }
   slot = __shfl_sync(0xffffffffu, slot, 0);
-  if (slot < 0) return;
+  if (slot < 0 || k == nullptr) return;  // padding row, or locate-only call
   const int32_t per = VEC ? Hkv * (D >> 3) : Hkv * D;  // vectors (or elements) per tensor
   for (int32_t i = lane; i < 2 * per; i += 32) {
     const bool is_v = i >= per;

@@ -7,6 +7,7 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include <atomic>
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
@@ -27,6 +28,17 @@ int launch_step_metadata(const int32_t* seq_rows, const int32_t* start_pos, cons
                          int32_t num_blocks, int32_t T, int32_t* cu_q, int32_t* positions,
                          int32_t* slots, int32_t* context_lens, uint32_t* status,
                          cudaStream_t stream);
+int launch_rms_norm(const void* x, int64_t x_stride, const void* add, int64_t add_stride,
+                    const int32_t* index, int32_t x_rows, const void* w, int32_t rows,
+                    int32_t hidden, float eps, void* out, int64_t out_stride, void* sum_out,
+                    int64_t sum_stride, bool bf16, uint32_t* status, cudaStream_t stream);
+int launch_rope_append(const void* qkv, int64_t qkv_stride, const void* cos_t, const void* sin_t,
+                       int32_t num_pos, const int32_t* pos, const int32_t* slots, int32_t ntok,
+                       int32_t H, int32_t Hkv, int32_t D, void* q_out, void* k_pool,
+                       void* v_pool, int64_t pool_slots, bool bf16, bool pool_bf16, int sms,
+                       uint32_t* status, cudaStream_t stream);
+int launch_silu_mul(const void* gate_up, int64_t stride, int32_t ntok, int32_t inter, void* out,
+                    bool bf16, int sms, cudaStream_t stream);
 int launch_decode_append(const int32_t* seq_rows, const int32_t* start_pos, int32_t R,
                          const int32_t* block_tables, int64_t bt_stride, int32_t bt_rows,
                          int32_t max_blocks, int32_t block_size, int32_t num_blocks,
@@ -43,6 +55,12 @@ int launch_slot_write(const void* k, const void* v, int64_t k_stride, int64_t v_
 namespace {
 
 thread_local std::string g_error;
+
+// Kernels this library has enqueued (or recorded into a stream capture) in
+// this process; read by bs_kernel_launches().
+std::atomic<uint64_t> g_launches{0};
+
+void count_launches(int n) { g_launches.fetch_add(static_cast<uint64_t>(n)); }
 
 int fail(int code, const char* fmt, ...) {
   char buf[512];
@@ -290,6 +308,7 @@ int launch_decode(bsb::DecodeArgs& a, int32_t dtype, int grid, cudaStream_t stre
     rc = bsb::launch_decode_simt(a, dtype == BS_BF16, grid, stream);
   }
   if (rc != 0) return cuda_fail(static_cast<cudaError_t>(rc), "decode kernel launch");
+  count_launches(a.tasks != nullptr ? 2 : 1);  // the merge pass runs with tasks
   return BS_OK;
 }
 
@@ -302,6 +321,8 @@ extern "C" {
 const char* bs_last_error(void) { return g_error.c_str(); }
 
 const char* bs_version(void) { return "batchstream_b200 0.1 (sm_100a)"; }
+
+uint64_t bs_kernel_launches(void) { return g_launches.load(); }
 
 int bs_paged_attention_workspace_bytes(int64_t num_heads, int64_t num_kv_heads, int64_t head_dim,
                                        int64_t block_table_len, int32_t dtype,
@@ -631,6 +652,7 @@ int bs_prefill_attention(const void* query, int64_t query_token_stride, const in
     if (grid > kInt32Max) return fail(BS_ERR_UNSUPPORTED, "too many query tiles");
     rc = bsb::launch_prefill_tc(p, qmap, kmap, vmap, static_cast<int>(grid), st);
     if (rc != 0) return cuda_fail(static_cast<cudaError_t>(rc), "prefill kernel launch");
+    count_launches(1);
     return BS_OK;
   }
   // Per-token path: token i of a chunk is a decode query over its causal length.
@@ -653,6 +675,7 @@ int bs_prefill_attention(const void* query, int64_t query_token_stride, const in
   int rc = bsb::launch_expand_rows(cu_q, context_lens, seq_rows, static_cast<int32_t>(num_rows),
                                    static_cast<int32_t>(num_tokens), token_lens, token_rows, st);
   if (rc != 0) return cuda_fail(static_cast<cudaError_t>(rc), "prefill row expansion");
+  count_launches(1);
   bsb::DecodeArgs a{};
   a.q = query;
   a.q_stride_seq = query_token_stride;
@@ -705,8 +728,8 @@ int bs_decode_append(const int32_t* seq_rows, const int32_t* start_pos, int64_t 
     return fail(BS_ERR_UNSUPPORTED, "pool too large");
   }
   if (num_rows == 0) return BS_OK;
-  BS_CHECK(start_pos && block_tables && key && value && key_pool && value_pool && context_lens &&
-               slot_mapping,
+  BS_CHECK((key == nullptr) == (value == nullptr), "key and value must both be given or both NULL");
+  BS_CHECK(start_pos && block_tables && key_pool && value_pool && context_lens && slot_mapping,
            "null pointer argument");
   const int in_sz = dtype_size(input_dtype), pool_sz = dtype_size(pool_dtype);
   const bool vec = head_dim % 8 == 0 && aligned16(key) && aligned16(value) &&
@@ -722,6 +745,86 @@ int bs_decode_append(const int32_t* seq_rows, const int32_t* start_pos, int64_t 
       num_blocks * block_size, vec, context_lens, slot_mapping, status,
       static_cast<cudaStream_t>(stream));
   if (rc != 0) return cuda_fail(static_cast<cudaError_t>(rc), "decode append launch");
+  count_launches(1);
+  return BS_OK;
+}
+
+int bs_rms_norm(const void* x, int64_t x_row_stride, int64_t x_rows, const void* add,
+                int64_t add_row_stride, const int32_t* row_index, const void* weight, int64_t rows,
+                int64_t hidden, double eps, int32_t dtype, void* out, int64_t out_row_stride,
+                void* sum_out, int64_t sum_row_stride, uint32_t* status, void* stream) {
+  BS_CHECK(dtype == BS_BF16 || dtype == BS_F32, "dtype must be bfloat16 or float32");
+  BS_CHECK(rows >= 0 && rows <= kInt32Max && hidden > 0 && hidden <= kInt32Max,
+           "rows or hidden out of range");
+  BS_CHECK(x_rows >= 0 && x_rows <= kInt32Max, "x_rows out of range");
+  BS_CHECK(row_index != nullptr || rows <= x_rows, "rows beyond x without a row index");
+  BS_CHECK(x_row_stride >= hidden && out_row_stride >= hidden, "row strides must cover hidden");
+  BS_CHECK(add == nullptr || add_row_stride >= hidden, "add row stride must cover hidden");
+  BS_CHECK(sum_out == nullptr || sum_row_stride >= hidden, "sum row stride must cover hidden");
+  BS_CHECK(row_index == nullptr || sum_out != x, "sum_out may alias x only without a row index");
+  if (rows == 0) return BS_OK;
+  BS_CHECK(x && weight && out, "null pointer argument");
+  const int rc = bsb::launch_rms_norm(
+      x, x_row_stride, add, add_row_stride, row_index, static_cast<int32_t>(x_rows), weight,
+      static_cast<int32_t>(rows), static_cast<int32_t>(hidden), static_cast<float>(eps), out,
+      out_row_stride, sum_out, sum_row_stride, dtype == BS_BF16, status,
+      static_cast<cudaStream_t>(stream));
+  if (rc != 0) return cuda_fail(static_cast<cudaError_t>(rc), "rms_norm launch");
+  count_launches(1);
+  return BS_OK;
+}
+
+int bs_rope_append(const void* qkv, int64_t qkv_row_stride, int32_t dtype, const void* cos_table,
+                   const void* sin_table, int64_t num_positions, const int32_t* positions,
+                   const int32_t* slot_mapping, int64_t num_tokens, int64_t num_heads,
+                   int64_t num_kv_heads, int64_t head_dim, void* query_out, void* key_pool,
+                   void* value_pool, int32_t pool_dtype, int64_t num_blocks, int64_t block_size,
+                   uint32_t* status, void* stream) {
+  BS_CHECK(dtype == BS_BF16 || dtype == BS_F32, "dtype must be bfloat16 or float32");
+  BS_CHECK(pool_dtype == BS_BF16 || pool_dtype == BS_F32, "pool dtype must be bf16 or fp32");
+  BS_CHECK(num_tokens >= 0 && num_tokens <= kInt32Max, "num_tokens out of range");
+  BS_CHECK(num_heads > 0 && num_kv_heads > 0 && head_dim > 0 && head_dim % 2 == 0,
+           "heads must be positive and head_dim even");
+  BS_CHECK(qkv_row_stride >= (num_heads + 2 * num_kv_heads) * head_dim,
+           "qkv rows must hold q, k and v");
+  BS_CHECK(num_blocks > 0 && block_size > 0, "sizes must be positive");
+  BS_CHECK(num_positions > 0 && num_positions <= kInt32Max, "num_positions out of range");
+  if (num_kv_heads * num_blocks * block_size > kInt32Max * 64ll) {
+    return fail(BS_ERR_UNSUPPORTED, "pool too large");
+  }
+  if (num_tokens == 0) return BS_OK;
+  BS_CHECK(qkv && cos_table && sin_table && positions && slot_mapping && query_out && key_pool &&
+               value_pool,
+           "null pointer argument");
+  DeviceInfo* d = nullptr;
+  if (int rc = current_device_info(&d)) return rc;
+  const int rc = bsb::launch_rope_append(
+      qkv, qkv_row_stride, cos_table, sin_table, static_cast<int32_t>(num_positions), positions,
+      slot_mapping, static_cast<int32_t>(num_tokens), static_cast<int32_t>(num_heads),
+      static_cast<int32_t>(num_kv_heads), static_cast<int32_t>(head_dim), query_out, key_pool,
+      value_pool, num_blocks * block_size, dtype == BS_BF16, pool_dtype == BS_BF16, d->sms,
+      status, static_cast<cudaStream_t>(stream));
+  if (rc != 0) return cuda_fail(static_cast<cudaError_t>(rc), "rope_append launch");
+  count_launches(1);
+  return BS_OK;
+}
+
+int bs_silu_mul(const void* gate_up, int64_t row_stride, int64_t num_tokens, int64_t intermediate,
+                int32_t dtype, void* out, void* stream) {
+  BS_CHECK(dtype == BS_BF16 || dtype == BS_F32, "dtype must be bfloat16 or float32");
+  BS_CHECK(num_tokens >= 0 && num_tokens <= kInt32Max && intermediate > 0 &&
+               intermediate <= kInt32Max,
+           "sizes out of range");
+  BS_CHECK(row_stride >= 2 * intermediate, "rows must hold gate and up");
+  if (num_tokens == 0) return BS_OK;
+  BS_CHECK(gate_up && out, "null pointer argument");
+  DeviceInfo* d = nullptr;
+  if (int rc = current_device_info(&d)) return rc;
+  const int rc = bsb::launch_silu_mul(gate_up, row_stride, static_cast<int32_t>(num_tokens),
+                                      static_cast<int32_t>(intermediate), out, dtype == BS_BF16,
+                                      d->sms, static_cast<cudaStream_t>(stream));
+  if (rc != 0) return cuda_fail(static_cast<cudaError_t>(rc), "silu_mul launch");
+  count_launches(1);
   return BS_OK;
 }
 
@@ -758,6 +861,7 @@ int bs_reshape_and_cache(const void* key, const void* value, int64_t key_token_s
       static_cast<int32_t>(head_dim), key_pool, value_pool, pool_dtype == BS_BF16, pool_slots, vec,
       d->sms, status, static_cast<cudaStream_t>(stream));
   if (rc != 0) return cuda_fail(static_cast<cudaError_t>(rc), "slot write launch");
+  count_launches(1);
   return BS_OK;
 }
 
@@ -785,6 +889,7 @@ int bs_step_metadata(const int32_t* seq_rows, const int32_t* start_pos, const in
       static_cast<int32_t>(num_tokens), cu_q, positions, slot_mapping, context_lens, status,
       static_cast<cudaStream_t>(stream));
   if (rc != 0) return cuda_fail(static_cast<cudaError_t>(rc), "metadata kernel launch");
+  count_launches(1);
   return BS_OK;
 }
 
@@ -804,6 +909,8 @@ int bs_take_status(void* workspace, void* stream, uint32_t* status_out) {
   if (bits & BS_STATUS_WAIT_TIMEOUT) msg += " pipeline wait timed out;";
   if (bits & BS_STATUS_BAD_SLOT) msg += " slot outside the pool;";
   if (bits & BS_STATUS_BAD_ROW) msg += " sequence row outside the block tables;";
+  if (bits & BS_STATUS_BAD_POSITION) msg += " position outside the rotary tables;";
+  if (bits & BS_STATUS_BAD_INDEX) msg += " gathered row index out of range;";
   g_error = msg;
   return BS_ERR_DEVICE;
 }

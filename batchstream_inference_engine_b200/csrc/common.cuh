@@ -25,6 +25,8 @@ enum : uint32_t {
   kStatusWaitTimeout = 1u << 2,  // a pipeline wait gave up
   kStatusBadSlot = 1u << 3,      // slot index outside the pool
   kStatusBadRow = 1u << 4,       // sequence row outside the block-table tensor
+  kStatusBadPosition = 1u << 5,  // position outside the rotary tables
+  kStatusBadIndex = 1u << 6,     // gathered row index outside its tensor
 };
 
 constexpr uint32_t kSpinLimit = 1u << 26;

@@ -1,0 +1,250 @@
+// Fused elementwise steps of the model around the attention path.  Each
+// replaces a chain of small framework ops of the reference's TorchModel
+// (src/server/torch_model.py) with one launch, keeping its rounding points:
+//
+//   rms_norm    (:283-287)  weight * (s_f32 * rsqrt(mean(s_f32^2) + eps)).to(T)
+//               with s = T(x + add), the residual add before it (:272, :281),
+//               optionally over gathered rows (the embedding lookup, :234,
+//               or the last token of each sequence, :228)
+//   rope_append (:262-264, :190-192, :149-153 / 289-292)
+//               q' = T(T(q * cos) + T(rotate_half(q) * sin)), the same for k;
+//               q' to the attention input, k' and v into their pool slots
+//   silu_mul    (:278-281)  T(T(silu(gate)) * up)
+//
+// T is the model dtype (bf16, or fp32 where the roundings vanish); cos/sin are
+// the bf16-rounded rotary tables gathered by position.  All are bandwidth-bound
+// and tiny per step; their value is the launches they remove.
+#include "common.cuh"
+
+namespace bsb {
+namespace {
+
+template <typename T>
+__device__ __forceinline__ float ld(const T* p);
+template <>
+__device__ __forceinline__ float ld<float>(const float* p) { return *p; }
+template <>
+__device__ __forceinline__ float ld<__nv_bfloat16>(const __nv_bfloat16* p) {
+  return __bfloat162float(*p);
+}
+template <typename T>
+__device__ __forceinline__ T st(float x);
+template <>
+__device__ __forceinline__ float st<float>(float x) { return x; }
+template <>
+__device__ __forceinline__ __nv_bfloat16 st<__nv_bfloat16>(float x) {
+  return __float2bfloat16_rn(x);
+}
+// The value a T-typed framework op would produce: rounded to T.
+template <typename T>
+__device__ __forceinline__ float rt(float x);
+template <>
+__device__ __forceinline__ float rt<float>(float x) { return x; }
+template <>
+__device__ __forceinline__ float rt<__nv_bfloat16>(float x) { return round_bf16(x); }
+
+// One CTA per output row r, reading source row i = index ? index[r] : r:
+// s = T(x[i] + add[i]) (s = x[i] without add), sum_out[r] = s, out[r] =
+// RMSNorm(s).  sum_out may be x itself (the residual stream updated in place:
+// every element is read and written by the same thread) when index is null.
+template <typename T>
+__global__ void __launch_bounds__(256)
+    rms_norm_kernel(const T* x, int64_t x_stride, const T* __restrict__ add, int64_t add_stride,
+                    const int32_t* __restrict__ index, int32_t x_rows, const T* __restrict__ w,
+                    int32_t hidden, float eps, T* __restrict__ out, int64_t out_stride, T* sum_out,
+                    int64_t sum_stride, uint32_t* status) {
+  pdl_trigger();
+  pdl_wait();
+  __shared__ float part[8];
+  int64_t src = blockIdx.x;
+  if (index != nullptr) {
+    src = index[blockIdx.x];
+    if (src < 0 || src >= x_rows) {
+      if (threadIdx.x == 0) set_status(status, kStatusBadIndex);
+      return;
+    }
+  }
+  const T* row = x + src * x_stride;
+  const T* arow = add != nullptr ? add + src * add_stride : nullptr;
+  T* srow = sum_out != nullptr ? sum_out + static_cast<int64_t>(blockIdx.x) * sum_stride : nullptr;
+  float ss = 0.f;
+  for (int i = threadIdx.x; i < hidden; i += blockDim.x) {
+    float v = ld<T>(row + i);
+    if (arow != nullptr) v = rt<T>(__fadd_rn(v, ld<T>(arow + i)));
+    if (srow != nullptr) srow[i] = st<T>(v);
+    ss = fmaf(v, v, ss);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  float tot = 0.f;
+  for (int i = 0; i < (blockDim.x >> 5); ++i) tot += part[i];
+  const float inv = rsqrtf(tot / static_cast<float>(hidden) + eps);
+  T* o = out + blockIdx.x * out_stride;
+  for (int i = threadIdx.x; i < hidden; i += blockDim.x) {
+    float v = ld<T>(row + i);  // this thread's own element of s, as computed above
+    if (srow != nullptr) v = ld<T>(srow + i);
+    else if (arow != nullptr) v = rt<T>(__fadd_rn(v, ld<T>(arow + i)));
+    const float normalized = rt<T>(__fmul_rn(v, inv));
+    o[i] = st<T>(__fmul_rn(ld<T>(w + i), normalized));
+  }
+}
+
+// One thread per (token, head, dim pair d, d + D/2) of q and k; v is copied.
+// qkv rows: [H*D | Hkv*D | Hkv*D].  A negative slot skips the pool write (a
+// padding row); a slot past the pool or a position outside [0, num_pos) skips
+// the access and sets a status bit.
+template <typename T, typename Tpool>
+__global__ void __launch_bounds__(256)
+    rope_append_kernel(const T* __restrict__ qkv, int64_t qkv_stride,
+                       const T* __restrict__ cos_t, const T* __restrict__ sin_t,
+                       int32_t num_pos, const int32_t* __restrict__ pos,
+                       const int32_t* __restrict__ slots, int32_t ntok, int32_t H, int32_t Hkv,
+                       int32_t D, T* __restrict__ q_out, Tpool* __restrict__ k_pool,
+                       Tpool* __restrict__ v_pool, int64_t pool_slots, uint32_t* status) {
+  pdl_trigger();
+  pdl_wait();
+  const int32_t half = D >> 1;
+  const int32_t per_tok = (H + 2 * Hkv) * half;
+  const int64_t total = static_cast<int64_t>(ntok) * per_tok;
+  for (int64_t idx = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; idx < total;
+       idx += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int32_t t = static_cast<int32_t>(idx / per_tok);
+    const int32_t r = static_cast<int32_t>(idx - static_cast<int64_t>(t) * per_tok);
+    const int32_t hh = r / half, d = r - hh * half;  // head in [0, H + 2 Hkv)
+    const T* row = qkv + t * qkv_stride + hh * D;
+    const float a = ld<T>(row + d), b = ld<T>(row + d + half);
+    const int32_t slot = hh >= H ? slots[t] : -1;
+    if (slot >= pool_slots) {
+      if (d == 0) set_status(status, kStatusBadSlot);
+      continue;
+    }
+    if (hh >= H + Hkv) {  // v: copied into its slot
+      if (slot >= 0) {
+        Tpool* dst = v_pool + (static_cast<int64_t>(hh - H - Hkv) * pool_slots + slot) * D;
+        dst[d] = st<Tpool>(a);
+        dst[d + half] = st<Tpool>(b);
+      }
+      continue;
+    }
+    const int32_t p = pos[t];
+    if (p < 0 || p >= num_pos) {
+      if (d == 0 && hh == 0) set_status(status, kStatusBadPosition);
+      continue;
+    }
+    const float c0 = ld<T>(cos_t + static_cast<int64_t>(p) * D + d);
+    const float c1 = ld<T>(cos_t + static_cast<int64_t>(p) * D + d + half);
+    const float s0 = ld<T>(sin_t + static_cast<int64_t>(p) * D + d);
+    const float s1 = ld<T>(sin_t + static_cast<int64_t>(p) * D + d + half);
+    // rotate_half(x) = cat(-x2, x1): element d takes -b, element d + half takes a.
+    const float lo = rt<T>(__fadd_rn(rt<T>(__fmul_rn(a, c0)), rt<T>(__fmul_rn(-b, s0))));
+    const float hi = rt<T>(__fadd_rn(rt<T>(__fmul_rn(b, c1)), rt<T>(__fmul_rn(a, s1))));
+    if (hh < H) {
+      T* dst = q_out + (static_cast<int64_t>(t) * H + hh) * D;
+      dst[d] = st<T>(lo);
+      dst[d + half] = st<T>(hi);
+    } else {
+      if (slot >= 0) {
+        Tpool* dst = k_pool + (static_cast<int64_t>(hh - H) * pool_slots + slot) * D;
+        dst[d] = st<Tpool>(lo);
+        dst[d + half] = st<Tpool>(hi);
+      }
+    }
+  }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(256)
+    silu_mul_kernel(const T* __restrict__ gate_up, int64_t stride, int32_t ntok, int32_t inter,
+                    T* __restrict__ out) {
+  pdl_trigger();
+  pdl_wait();
+  const int64_t total = static_cast<int64_t>(ntok) * inter;
+  for (int64_t idx = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; idx < total;
+       idx += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t t = idx / inter;
+    const int32_t i = static_cast<int32_t>(idx - t * inter);
+    const float g = ld<T>(gate_up + t * stride + i);
+    const float u = ld<T>(gate_up + t * stride + inter + i);
+    const float s = rt<T>(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))));
+    out[idx] = st<T>(__fmul_rn(s, u));
+  }
+}
+
+cudaLaunchConfig_t cfg_of(int64_t grid, int threads, cudaStream_t stream,
+                          cudaLaunchAttribute* attr) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(grid));
+  cfg.blockDim = dim3(threads);
+  cfg.stream = stream;
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cfg;
+}
+
+int64_t grid_for(int64_t work, int sms) {
+  int64_t g = (work + 255) / 256;
+  if (g > static_cast<int64_t>(sms) * 8) g = static_cast<int64_t>(sms) * 8;
+  return g < 1 ? 1 : g;
+}
+
+}  // namespace
+
+int launch_rms_norm(const void* x, int64_t x_stride, const void* add, int64_t add_stride,
+                    const int32_t* index, int32_t x_rows, const void* w, int32_t rows,
+                    int32_t hidden, float eps, void* out, int64_t out_stride, void* sum_out,
+                    int64_t sum_stride, bool bf16, uint32_t* status, cudaStream_t stream) {
+  if (rows == 0) return 0;
+  cudaLaunchAttribute attr[1];
+  cudaLaunchConfig_t cfg = cfg_of(rows, 256, stream, attr);
+#define BS_RMS(T)                                                                               \
+  return static_cast<int>(cudaLaunchKernelEx(                                                   \
+      &cfg, rms_norm_kernel<T>, static_cast<const T*>(x), x_stride, static_cast<const T*>(add), \
+      add_stride, index, x_rows, static_cast<const T*>(w), hidden, eps, static_cast<T*>(out),   \
+      out_stride, static_cast<T*>(sum_out), sum_stride, status))
+  if (bf16) BS_RMS(__nv_bfloat16);
+  BS_RMS(float);
+#undef BS_RMS
+}
+
+int launch_rope_append(const void* qkv, int64_t qkv_stride, const void* cos_t, const void* sin_t,
+                       int32_t num_pos, const int32_t* pos, const int32_t* slots, int32_t ntok,
+                       int32_t H, int32_t Hkv, int32_t D, void* q_out, void* k_pool,
+                       void* v_pool, int64_t pool_slots, bool bf16, bool pool_bf16, int sms,
+                       uint32_t* status, cudaStream_t stream) {
+  if (ntok == 0) return 0;
+  const int64_t work = static_cast<int64_t>(ntok) * (H + 2 * Hkv) * (D / 2);
+  cudaLaunchAttribute attr[1];
+  cudaLaunchConfig_t cfg = cfg_of(grid_for(work, sms), 256, stream, attr);
+#define BS_ROPE(T, TP)                                                                          \
+  return static_cast<int>(cudaLaunchKernelEx(                                                   \
+      &cfg, rope_append_kernel<T, TP>, static_cast<const T*>(qkv), qkv_stride,                  \
+      static_cast<const T*>(cos_t), static_cast<const T*>(sin_t), num_pos, pos, slots, ntok, H, \
+      Hkv, D, static_cast<T*>(q_out), static_cast<TP*>(k_pool), static_cast<TP*>(v_pool),      \
+      pool_slots, status))
+  if (bf16 && pool_bf16) BS_ROPE(__nv_bfloat16, __nv_bfloat16);
+  if (bf16) BS_ROPE(__nv_bfloat16, float);
+  if (pool_bf16) BS_ROPE(float, __nv_bfloat16);
+  BS_ROPE(float, float);
+#undef BS_ROPE
+}
+
+int launch_silu_mul(const void* gate_up, int64_t stride, int32_t ntok, int32_t inter, void* out,
+                    bool bf16, int sms, cudaStream_t stream) {
+  if (ntok == 0) return 0;
+  cudaLaunchAttribute attr[1];
+  cudaLaunchConfig_t cfg =
+      cfg_of(grid_for(static_cast<int64_t>(ntok) * inter, sms), 256, stream, attr);
+  if (bf16)
+    return static_cast<int>(cudaLaunchKernelEx(&cfg, silu_mul_kernel<__nv_bfloat16>,
+                                               static_cast<const __nv_bfloat16*>(gate_up), stride,
+                                               ntok, inter, static_cast<__nv_bfloat16*>(out)));
+  return static_cast<int>(cudaLaunchKernelEx(&cfg, silu_mul_kernel<float>,
+                                             static_cast<const float*>(gate_up), stride, ntok,
+                                             inter, static_cast<float*>(out)));
+}
+
+}  // namespace bsb

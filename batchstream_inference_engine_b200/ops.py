@@ -93,6 +93,12 @@ def take_status(device: torch.device | None = None) -> int:
     return bits.value
 
 
+def kernel_launches() -> int:
+    """Kernels this package's library has launched (or recorded into a CUDA
+    graph) in this process."""
+    return int(lib().bs_kernel_launches())
+
+
 def _shape_args(t: torch.Tensor):
     return t.dim(), i64_array(t.shape), i64_array(t.stride())
 
@@ -287,6 +293,11 @@ def decode_append(key: torch.Tensor, value: torch.Tensor, key_pool: torch.Tensor
     src/server/torch_model.py:149-153, through BlockAllocator.locate)."""
     device = _require_cuda("decode_append", key, value, key_pool, value_pool, block_tables,
                            start_pos, seq_rows)
+    if key is None or value is None:
+        if key is not value:
+            raise RuntimeError("key and value must both be given or both be None")
+        return _locate(key_pool, value_pool, block_tables, start_pos, seq_rows,
+                       max_blocks_per_seq, context_lens, slots, device)
     Hkv, NB, bs, D = key_pool.shape
     B = start_pos.numel()
     for name, t in (("block_tables", block_tables), ("start_pos", start_pos)):
@@ -324,13 +335,153 @@ def decode_append(key: torch.Tensor, value: torch.Tensor, key_pool: torch.Tensor
     return ctx[:B], sl[:B]
 
 
+def _locate(key_pool, value_pool, block_tables, start_pos, seq_rows, max_blocks_per_seq,
+            context_lens, slots, device):
+    """decode_append without rows: context lengths and slots only."""
+    Hkv, NB, bs, D = key_pool.shape
+    B = start_pos.numel()
+    for name, t in (("block_tables", block_tables), ("start_pos", start_pos)):
+        if t.dtype != torch.int32:
+            raise RuntimeError(f"{name} must be int32")
+    if seq_rows is not None and (seq_rows.dtype != torch.int32 or seq_rows.numel() < B):
+        raise RuntimeError("seq_rows must be int32 with one entry per row")
+    if block_tables.stride(1) != 1:
+        block_tables = block_tables.contiguous()
+    ctx = context_lens if context_lens is not None else torch.empty(
+        max(B, 1), dtype=torch.int32, device=device)
+    sl = slots if slots is not None else torch.empty(max(B, 1), dtype=torch.int32, device=device)
+    mb = block_tables.size(1) if max_blocks_per_seq is None else int(max_blocks_per_seq)
+    ws = workspace_for(device, 0)
+    with torch.cuda.device(device):
+        stream = torch.cuda.current_stream(device).cuda_stream
+        check(lib().bs_decode_append(
+            seq_rows.data_ptr() if seq_rows is not None else None, start_pos.data_ptr(), B,
+            block_tables.data_ptr(), block_tables.stride(0), block_tables.size(0), mb, None, None,
+            Hkv * D, Hkv * D, dtype_code(key_pool.dtype), key_pool.data_ptr(),
+            value_pool.data_ptr(), dtype_code(key_pool.dtype), Hkv, NB, bs, D, ctx.data_ptr(),
+            sl.data_ptr(), ws.data_ptr(), stream))
+    return ctx[:B], sl[:B]
+
+
+def _rows_2d(name: str, t: torch.Tensor, width: int) -> torch.Tensor:
+    t2 = t if t.dim() == 2 else t.reshape(t.size(0), -1)
+    if t2.size(1) != width:
+        raise RuntimeError(f"{name} rows must hold {width} elements")
+    return t2 if t2.stride(1) == 1 else t2.contiguous()
+
+
+def rms_norm(x: torch.Tensor, weight: torch.Tensor, eps: float, add: torch.Tensor | None = None,
+             row_index: torch.Tensor | None = None, sum_out: torch.Tensor | None = None,
+             out: torch.Tensor | None = None) -> torch.Tensor:
+    """RMSNorm of the reference TorchModel (src/server/torch_model.py:283-287)
+    with the residual add before it fused: per output row r (source row
+    i = row_index[r], or r), s = (x[i] + add[i]) in x's dtype, sum_out[r] = s,
+    and returns weight * (s_f32 * rsqrt(mean(s_f32^2) + eps)).to(dtype).
+    ``sum_out`` may be ``x`` (the residual stream updated in place) only
+    without ``row_index``."""
+    device = _require_cuda("rms_norm", x, weight, add, row_index, sum_out, out)
+    hidden = weight.numel()
+    x2 = _rows_2d("x", x, hidden)
+    if x2.dtype != weight.dtype or (add is not None and add.dtype != x2.dtype):
+        raise RuntimeError("x, add and weight must share a dtype")
+    a2 = _rows_2d("add", add, hidden) if add is not None else None
+    if a2 is not None and a2.size(0) < x2.size(0):
+        raise RuntimeError("add must have a row for every row of x")
+    if row_index is not None:
+        if row_index.dtype != torch.int32:
+            raise RuntimeError("row_index must be int32")
+        rows = row_index.numel()
+    else:
+        rows = x2.size(0)
+    o2 = out if out is not None else torch.empty((rows, hidden), dtype=x2.dtype, device=device)
+    s2 = sum_out
+    for name, t in (("out", o2), ("sum_out", s2)):
+        if t is not None and (t.dim() != 2 or t.stride(1) != 1 or t.size(1) != hidden
+                              or t.size(0) < rows or t.dtype != x2.dtype):
+            raise RuntimeError(f"{name} must be [rows, hidden] with unit inner stride in x's dtype")
+    ws = workspace_for(device, 0)
+    with torch.cuda.device(device):
+        stream = torch.cuda.current_stream(device).cuda_stream
+        check(lib().bs_rms_norm(
+            x2.data_ptr(), x2.stride(0), x2.size(0), a2.data_ptr() if a2 is not None else None,
+            a2.stride(0) if a2 is not None else 0,
+            row_index.data_ptr() if row_index is not None else None, weight.contiguous().data_ptr(),
+            rows, hidden, float(eps), dtype_code(x2.dtype), o2.data_ptr(), o2.stride(0),
+            s2.data_ptr() if s2 is not None else None, s2.stride(0) if s2 is not None else 0,
+            ws.data_ptr(), stream))
+    return o2
+
+
+def rope_append(qkv: torch.Tensor, cos_table: torch.Tensor, sin_table: torch.Tensor,
+                positions: torch.Tensor, slot_mapping: torch.Tensor, key_pool: torch.Tensor,
+                value_pool: torch.Tensor, num_heads: int, query_out: torch.Tensor | None = None
+                ) -> torch.Tensor:
+    """Rotary embedding and K/V append in one launch.  ``qkv`` rows are the
+    fused projection [q heads | k heads | v heads] ([T, (H + 2 Hkv) D]); q and
+    k are rotated with the cos/sin tables gathered at ``positions``
+    (src/server/torch_model.py:190-192, 262-264, same rounding points), q is
+    returned as [T, H, D] and k, v are written at ``slot_mapping`` into the
+    pools [Hkv, blocks, block_size, D] (PagedKVCache.append, :149-153); a
+    negative slot skips the row's write."""
+    device = _require_cuda("rope_append", qkv, cos_table, sin_table, positions, slot_mapping,
+                           key_pool, value_pool, query_out)
+    Hkv, NB, bs, D = key_pool.shape
+    T = positions.numel()
+    if positions.dtype != torch.int32 or slot_mapping.dtype != torch.int32:
+        raise RuntimeError("positions and slot_mapping must be int32")
+    if slot_mapping.numel() < T or qkv.size(0) < T:
+        raise RuntimeError("qkv and slot_mapping need a row per position")
+    if value_pool.shape != key_pool.shape or value_pool.dtype != key_pool.dtype:
+        raise RuntimeError("key/value pools disagree")
+    if not (key_pool.is_contiguous() and value_pool.is_contiguous()):
+        raise RuntimeError("pools must be contiguous")
+    if cos_table.shape != sin_table.shape or cos_table.size(-1) != D or cos_table.dtype != qkv.dtype:
+        raise RuntimeError("cos/sin tables must be [positions, head_dim] in the qkv dtype")
+    q2 = _rows_2d("qkv", qkv, (num_heads + 2 * Hkv) * D)
+    cos_c, sin_c = cos_table.contiguous(), sin_table.contiguous()
+    q_out = query_out if query_out is not None else torch.empty(
+        (T, num_heads, D), dtype=qkv.dtype, device=device)
+    if not q_out.is_contiguous() or q_out.numel() < T * num_heads * D:
+        raise RuntimeError("query_out must be contiguous [T, heads, head_dim]")
+    ws = workspace_for(device, 0)
+    with torch.cuda.device(device):
+        stream = torch.cuda.current_stream(device).cuda_stream
+        check(lib().bs_rope_append(
+            q2.data_ptr(), q2.stride(0), dtype_code(qkv.dtype), cos_c.data_ptr(), sin_c.data_ptr(),
+            cos_c.size(0), positions.data_ptr(), slot_mapping.data_ptr(), T, num_heads, Hkv, D,
+            q_out.data_ptr(), key_pool.data_ptr(), value_pool.data_ptr(),
+            dtype_code(key_pool.dtype), NB, bs, ws.data_ptr(), stream))
+    return q_out
+
+
+def silu_mul(gate_up: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """SwiGLU gating of the reference MLP (src/server/torch_model.py:278-281):
+    rows [gate | up] -> silu(gate) * up, rounded to the dtype after each op."""
+    device = _require_cuda("silu_mul", gate_up, out)
+    if gate_up.dim() != 2 or gate_up.stride(1) != 1 or gate_up.size(1) % 2:
+        raise RuntimeError("gate_up must be [T, 2 * intermediate] with unit inner stride")
+    T, inter = gate_up.size(0), gate_up.size(1) // 2
+    o = out if out is not None else torch.empty((T, inter), dtype=gate_up.dtype, device=device)
+    if not o.is_contiguous() or o.shape != (T, inter) or o.dtype != gate_up.dtype:
+        raise RuntimeError("out must be contiguous [T, intermediate] in the input dtype")
+    with torch.cuda.device(device):
+        stream = torch.cuda.current_stream(device).cuda_stream
+        check(lib().bs_silu_mul(gate_up.data_ptr(), gate_up.stride(0), T, inter,
+                                dtype_code(gate_up.dtype), o.data_ptr(), stream))
+    return o
+
+
 __all__ = [
     "paged_attention",
     "paged_attention_batched",
     "reshape_and_cache",
     "decode_append",
     "step_metadata",
+    "rms_norm",
+    "rope_append",
+    "silu_mul",
     "take_status",
+    "kernel_launches",
     "workspace_for",
     "dtype_code",
     "_lib",

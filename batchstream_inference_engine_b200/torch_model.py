@@ -11,16 +11,20 @@ the work runs and how a step is assembled (``_hidden_states`` :231-247):
   (``BlockAllocator(device=...)``), and one ``step_metadata`` launch derives the
   ragged-batch metadata (chunk offsets, positions, slot mapping, context
   lengths) that the reference rebuilt in Python every step;
-* each layer writes the step's K/V rows with one ``reshape_and_cache`` launch
-  (PagedKVCache.append, :149-153) and attends with one batched decode launch for
-  the single-token rows plus one chunked-prefill launch for the prompt chunks
+* each layer rotates q and k and writes the step's K/V rows in one
+  ``rope_append`` launch (torch_model.py:262-264, PagedKVCache.append
+  :149-153) and attends with one batched decode launch for the single-token
+  rows plus one chunked-prefill launch for the prompt chunks
   (PagedKVCache.attend, :155-167), instead of 2 x B Python-level calls;
+* the residual adds, RMSNorms (:283-287), embedding gather and SwiGLU gating
+  run in fused kernels with the reference's rounding points, so a layer is
+  five of this package's launches around four library GEMMs;
 * the last-token logits are reduced to greedy token ids on the device
   (PagedBackend._next_output, backend/paged.py:95-99), so only B ints cross
   PCIe per step.
 
 The projections and the MLP are plain library GEMMs (cuBLAS through torch);
-the attention, the slot write and the metadata are this package's kernels.
+everything else in a step is this package's kernels.
 """
 
 from __future__ import annotations
@@ -305,6 +309,7 @@ class TorchModel:
             cache.reserve(len(tokens))
         alloc = pool.allocator
         self.stats["h2d_bytes"] += 16 * alloc.sync_device()
+        launches = ops.kernel_launches()
         R = len(groups)
         lengths = [len(tokens) for tokens, _ in groups]
         T = sum(lengths)
@@ -327,63 +332,71 @@ class TorchModel:
         n_dec = 0
         while n_dec < R and lengths[n_dec] == 1:
             n_dec += 1
-        decode_only = n_dec == R
-        if decode_only:
-            # One token per row: positions are the start positions, and each
-            # layer's decode_append locates the slots and writes the lengths.
-            positions, slots, ctx = start_d, None, None
+        if n_dec == R:
+            # One token per row: positions are the start positions; one locate
+            # launch gives the slots.
+            positions = start_d
+            _, slots = ops.decode_append(None, None, pool.keys[0], pool.values[0],
+                                         alloc.device_tables, start_d, seq_rows=rows_d)
+            cu_q = ctx = None
         else:
             cu_q, positions, slots, ctx = ops.step_metadata(
                 alloc.device_tables, start_d, n_d, T, pool.block_size, pool.num_blocks,
                 seq_rows=rows_d)
         max_chunk = max(lengths[n_dec:], default=0)
+        pre_cu = (cu_q[n_dec:] - n_dec) if n_dec < R else None
+
+        def attend(q, kp, vp, attended):
+            if n_dec:
+                ops.paged_attention_batched(q[:n_dec], kp, vp, alloc.device_tables, ctx_d[:n_dec],
+                                            config.head_dim ** -0.5, seq_rows=rows_d[:n_dec],
+                                            out=attended[:n_dec], lens_ready=True,
+                                            after_append=True)
+            if n_dec < R:
+                ops.prefill_attention(q[n_dec:], kp, vp, alloc.device_tables, pre_cu,
+                                      ctx[n_dec:], config.head_dim ** -0.5,
+                                      max_query_len=max_chunk, seq_rows=rows_d[n_dec:],
+                                      out=attended[n_dec:])
+
+        last = self._layers(pool, tokens_d, positions, slots, ends_d, attend)
+        for (tokens, cache) in groups:
+            cache.advance(len(tokens))
         st = self.stats
         st["steps"] += 1
         st["tokens"] += T
         st["rows"] += R
         st["attn_flops"] += config.num_layers * 4 * config.num_heads * config.head_dim * sum(
             n * s + n * (n + 1) // 2 for s, n in zip(starts, lengths))
-        st["launches"] += (0 if decode_only else 1) + config.num_layers * (
-            1 + (n_dec > 0) + (n_dec < R))
-        pre_cu = (cu_q[n_dec:] - n_dec) if n_dec < R else None
+        st["launches"] += ops.kernel_launches() - launches
+        return last
 
-        hidden = self.embed.index_select(0, tokens_d.long())
-        cos = self.cos.index_select(0, positions.long())
-        sin = self.sin.index_select(0, positions.long())
-        H, Hkv, D = config.num_heads, config.num_kv_heads, config.head_dim
-        scaling = D ** -0.5
+    def _layers(self, pool: PagedKVPool, tokens, positions, slots, last_rows, attend):
+        """The decoder stack over T tokens (torch_model.py:233-248, 250-287) with
+        the residual adds, RMSNorms, rotary embedding, K/V append and SwiGLU
+        gating in this package's fused kernels and the projections in library
+        GEMMs.  ``attend(q, key_pool, value_pool, out)`` runs one layer's paged
+        attention.  Returns the final-normed hidden states of rows last_rows."""
+        config = self.config
+        H, D, eps = config.num_heads, config.head_dim, config.rms_norm_eps
+        T = tokens.numel()
+        # Residual stream; layer 0's norm also gathers the embedding rows into it.
+        hidden = torch.empty((T, config.hidden_size), dtype=self.dtype, device=self.device)
+        attended = torch.empty((T, H, D), dtype=self.dtype, device=self.device)
+        q = torch.empty((T, H, D), dtype=self.dtype, device=self.device)
+        delta = None  # the previous sublayer's output, added before the next norm
         for layer, lw in enumerate(self.layers):
-            normed = self._rms_norm(hidden, lw["ln1"])
-            qkv = F.linear(normed, lw["qkv_w"], lw["qkv_b"])
-            q = qkv[:, : H * D].view(T, H, D)
-            k = qkv[:, H * D: (H + Hkv) * D].view(T, Hkv, D)
-            v = qkv[:, (H + Hkv) * D:].view(T, Hkv, D)
-            q = q * cos[:, None] + _rotate_half(q) * sin[:, None]
-            k = k * cos[:, None] + _rotate_half(k) * sin[:, None]
-            kp, vp = pool.keys[layer], pool.values[layer]
-            if decode_only:
-                ctx, slots = ops.decode_append(k, v, kp, vp, alloc.device_tables, start_d,
-                                               seq_rows=rows_d, context_lens=ctx, slots=slots)
+            if layer == 0:
+                normed = ops.rms_norm(self.embed, lw["ln1"], eps, row_index=tokens, sum_out=hidden)
             else:
-                ops.reshape_and_cache(k, v, kp, vp, slots)
-            attended = torch.empty((T, H, D), dtype=q.dtype, device=self.device)
-            if n_dec:
-                ops.paged_attention_batched(q[:n_dec], kp, vp, alloc.device_tables, ctx_d[:n_dec],
-                                            scaling, seq_rows=rows_d[:n_dec],
-                                            out=attended[:n_dec], lens_ready=True,
-                                            after_append=True)
-            if n_dec < R:
-                ops.prefill_attention(q[n_dec:], kp, vp, alloc.device_tables, pre_cu,
-                                      ctx[n_dec:], scaling, max_query_len=max_chunk,
-                                      seq_rows=rows_d[n_dec:], out=attended[n_dec:])
-            hidden = hidden + F.linear(attended.view(T, H * D), lw["o_w"])
-            normed = self._rms_norm(hidden, lw["ln2"])
-            gate_up = F.linear(normed, lw["gate_up_w"])
-            gate, up = gate_up.split(self.intermediate_size, dim=-1)
-            hidden = hidden + F.linear(F.silu(gate) * up, lw["down_w"])
-        for (tokens, cache) in groups:
-            cache.advance(len(tokens))
-        return self._rms_norm(hidden.index_select(0, ends_d.long()), self.final_norm)
+                normed = ops.rms_norm(hidden, lw["ln1"], eps, add=delta, sum_out=hidden)
+            qkv = F.linear(normed, lw["qkv_w"], lw["qkv_b"])
+            kp, vp = pool.keys[layer], pool.values[layer]
+            ops.rope_append(qkv, self.cos, self.sin, positions, slots, kp, vp, H, query_out=q)
+            attend(q, kp, vp, attended)
+            delta = F.linear(attended.view(T, H * D), lw["o_w"])
+            normed = ops.rms_norm(hidden, lw["ln2"], eps, add=delta, sum_out=hidden)
+            delta = F.linear(ops.silu_mul(F.linear(normed, lw["gate_up_w"])), lw["down_w"])
+        return ops.rms_norm(hidden, self.final_norm, eps, add=delta, row_index=last_rows)
 
     # ---------------------------------------------------------------- decode graphs
 
@@ -393,33 +406,17 @@ class TorchModel:
         the step; start[r] < 0 and ctx[r] == 0 mark a padding row.  Launches
         only (no host synchronisation), so it can be captured."""
         config = self.config
-        H, Hkv, D = config.num_heads, config.num_kv_heads, config.head_dim
-        B = tokens.numel()
         alloc = pool.allocator
-        hidden = self.embed.index_select(0, tokens.long())
-        cos = self.cos.index_select(0, pos.long())[:, None]
-        sin = self.sin.index_select(0, pos.long())[:, None]
-        ctx_w = torch.empty(B, dtype=torch.int32, device=self.device)
-        slots = torch.empty(B, dtype=torch.int32, device=self.device)
-        for layer, lw in enumerate(self.layers):
-            normed = self._rms_norm(hidden, lw["ln1"])
-            qkv = F.linear(normed, lw["qkv_w"], lw["qkv_b"])
-            q = qkv[:, : H * D].view(B, H, D)
-            k = qkv[:, H * D: (H + Hkv) * D].view(B, Hkv, D)
-            v = qkv[:, (H + Hkv) * D:].view(B, Hkv, D)
-            q = q * cos + _rotate_half(q) * sin
-            k = k * cos + _rotate_half(k) * sin
-            kp, vp = pool.keys[layer], pool.values[layer]
-            ops.decode_append(k, v, kp, vp, alloc.device_tables, start, seq_rows=rows,
-                              context_lens=ctx_w, slots=slots)
-            attended = ops.paged_attention_batched(q, kp, vp, alloc.device_tables, ctx,
-                                                   D ** -0.5, seq_rows=rows, lens_ready=True,
-                                                   after_append=True)
-            hidden = hidden + F.linear(attended.view(B, H * D), lw["o_w"])
-            normed = self._rms_norm(hidden, lw["ln2"])
-            gate, up = F.linear(normed, lw["gate_up_w"]).split(self.intermediate_size, dim=-1)
-            hidden = hidden + F.linear(F.silu(gate) * up, lw["down_w"])
-        logits = F.linear(self._rms_norm(hidden, self.final_norm), self.embed)
+        _, slots = ops.decode_append(None, None, pool.keys[0], pool.values[0],
+                                     alloc.device_tables, start, seq_rows=rows)
+
+        def attend(q, kp, vp, attended):
+            ops.paged_attention_batched(q, kp, vp, alloc.device_tables, ctx,
+                                        config.head_dim ** -0.5, seq_rows=rows, out=attended,
+                                        lens_ready=True, after_append=True)
+
+        last = self._layers(pool, tokens, pos, slots, None, attend)
+        logits = F.linear(last, self.embed)
         return logits.float().argmax(dim=-1).to(torch.int32)
 
     def _capture_graphs(self, pool: PagedKVPool) -> None:
@@ -445,9 +442,11 @@ class TorchModel:
                     self._decode_forward(pool, *inputs)
                 stream.synchronize()
                 graph = torch.cuda.CUDAGraph()
+                before = ops.kernel_launches()
                 with torch.cuda.graph(graph, pool=self._graph_pool, stream=stream):
                     ids = self._decode_forward(pool, *inputs)
-                self._graphs[(id(pool), B)] = (inputs, graph, ids)
+                # This package's kernels in the graph, launched again by each replay.
+                self._graphs[(id(pool), B)] = (inputs, graph, ids, ops.kernel_launches() - before)
             ops.take_status(self.device)
         torch.cuda.current_stream(self.device).wait_stream(stream)
 
@@ -465,7 +464,7 @@ class TorchModel:
         while B < R:
             B *= 2
         B = min(B, self.max_graph_batch)
-        inputs, graph, ids = self._graphs[(id(pool), B)]
+        inputs, graph, ids, graph_launches = self._graphs[(id(pool), B)]
         starts = [cache.length for _, cache in groups]
         if max(starts) + 1 > self.max_position:
             raise RuntimeError(f"positions beyond the rotary table ({self.max_position})")
@@ -490,20 +489,9 @@ class TorchModel:
         st["rows"] += R
         st["attn_flops"] += config.num_layers * 4 * config.num_heads * config.head_dim * sum(
             s + 1 for s in starts)
-        st["launches"] += 2 * config.num_layers
+        st["launches"] += graph_launches
         st["d2h_bytes"] += 4 * R
         return host.tolist()
-
-    def _rms_norm(self, hidden: torch.Tensor, weight: torch.Tensor) -> torch.Tensor:
-        wide = hidden.to(torch.float32)
-        variance = wide.pow(2).mean(-1, keepdim=True)
-        normalized = wide * torch.rsqrt(variance + self.config.rms_norm_eps)
-        return weight * normalized.to(hidden.dtype)
-
-
-def _rotate_half(x: torch.Tensor) -> torch.Tensor:
-    first, second = x.chunk(2, dim=-1)
-    return torch.cat((-second, first), dim=-1)
 
 
 __all__ = ["ModelConfig", "PagedKVPool", "PagedKVCache", "TorchModel", "QWEN25_05B",

@@ -184,11 +184,13 @@ def capture_graphs(prep, kernel, rotations, warmup, dev):
         graphs = []
         for r in range(rotations):
             ga, gb = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
+            before = ops.kernel_launches()
             with torch.cuda.graph(ga, stream=capture):
                 meta = prep(r)
             with torch.cuda.graph(gb, stream=capture):
                 kernel(r, meta)
-            graphs.append((ga, gb, meta))
+            # This package's kernels in the pair: each replay launches them again.
+            graphs.append((ga, gb, meta, ops.kernel_launches() - before))
         ops.take_status(dev)
     torch.cuda.synchronize(dev)
     return graphs, capture
@@ -214,7 +216,7 @@ def timed_replays(graphs, steps, warmup, dev, world):
 
     stream = torch.cuda.current_stream(dev)
     for i in range(warmup):
-        ga, gb, _ = graphs[i % len(graphs)]
+        ga, gb, *_ = graphs[i % len(graphs)]
         ga.replay()
         gb.replay()
     mids = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
@@ -228,7 +230,7 @@ def timed_replays(graphs, steps, warmup, dev, world):
         t0.record(stream)
         torch.cuda.nvtx.range_push("timed")
         for i in range(steps):
-            ga, gb, _ = graphs[i % len(graphs)]
+            ga, gb, *_ = graphs[i % len(graphs)]
             ga.replay()
             mids[i].record(stream)
             gb.replay()
@@ -244,8 +246,11 @@ def timed_replays(graphs, steps, warmup, dev, world):
 
 def capture_steps(step, rotations, dev):
     """One CUDA graph per rotation holding a whole step (PDL edges between its
-    launches are kept inside the graph)."""
+    launches are kept inside the graph).  Returns (graphs, capture stream,
+    this package's kernel launches per graph)."""
     import torch
+
+    from batchstream_inference_engine_b200 import ops
 
     stream = torch.cuda.current_stream(dev)
     capture = torch.cuda.Stream(dev)
@@ -255,13 +260,21 @@ def capture_steps(step, rotations, dev):
         for r in range(rotations):
             step(r)
         torch.cuda.synchronize(dev)
+        counts = []
         for r in range(rotations):
             g = torch.cuda.CUDAGraph()
+            before = ops.kernel_launches()
             with torch.cuda.graph(g, stream=capture):
                 step(r)
             graphs.append(g)
+            counts.append(ops.kernel_launches() - before)
     torch.cuda.synchronize(dev)
-    return graphs, capture
+    return graphs, capture, counts
+
+
+def replayed_launches(counts, steps):
+    """Kernel launches of `steps` replays cycling through graphs with `counts`."""
+    return sum(counts[i % len(counts)] for i in range(steps))
 
 
 def timed_graph_steps(graphs, steps, warmup, dev, world):
@@ -515,7 +528,8 @@ def run_decode(args):
     # The step (append + decode) is replayed from one CUDA graph per rotation:
     # `value` and ms_per_step.  The decode kernel alone is timed from a second
     # set of graphs that split the step, with events between the two halves.
-    step_graphs, step_capture = capture_steps(lambda r: decode(r, prep(r)), ROTATIONS, dev)
+    step_graphs, step_capture, step_counts = capture_steps(lambda r: decode(r, prep(r)),
+                                                            ROTATIONS, dev)
     total_ms, clock = timed_graph_steps(step_graphs, args.steps, args.warmup, dev, world)
     graphs, capture = capture_graphs(prep, decode, ROTATIONS, args.warmup, dev)
     _, decode_ms, _ = timed_replays(graphs, args.steps, args.warmup, dev, world)
@@ -606,7 +620,7 @@ def run_decode(args):
                     "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "ms_per_step": round(e2e_ms / args.steps, 4),
                     "path": "pinned host -> device, decode append + decode, device -> pinned host"},
-            "gpu_launches": 2 * args.steps,
+            "gpu_launches": replayed_launches(step_counts, args.steps),
             "clocks": clock,
         }
     if world > 1:
@@ -775,7 +789,7 @@ def run_prefill(args):
                     "ms_per_step": round(e2e_ms / args.steps, 4),
                     "path": "pinned host -> device, metadata + slot write + prefill, "
                             "device -> pinned host"},
-            "gpu_launches": 3 * args.steps,
+            "gpu_launches": replayed_launches([g[3] for g in graphs], args.steps),
             "clocks": clock,
         }
     if world > 1:

@@ -51,11 +51,19 @@ enum bs_error {
 #define BS_STATUS_WAIT_TIMEOUT 0x4u
 #define BS_STATUS_BAD_SLOT 0x8u
 #define BS_STATUS_BAD_ROW 0x10u
+#define BS_STATUS_BAD_POSITION 0x20u
+#define BS_STATUS_BAD_INDEX 0x40u
 
 /* Message of the last failing call on this thread ("" if none). */
 const char* bs_last_error(void);
 
 /* Library version string. */
+/*
+ * Kernels this library has launched in this process (each successful entry
+ * adds the kernels it enqueued, e.g. 2 for a tensor-core decode with its merge
+ * pass).  A launch recorded into a CUDA graph counts once at capture.
+ */
+uint64_t bs_kernel_launches(void);
 const char* bs_version(void);
 
 /*
@@ -204,7 +212,9 @@ int bs_reshape_and_cache(const void* key, const void* value, int64_t key_token_s
  * bs_reshape_and_cache for steps in which every row decodes one token; a
  * table entry outside the pool or a bad row sets a status bit and skips the row.
  * A row with start_pos < 0 is padding (fixed-size batches, CUDA graphs):
- * nothing is written, context_lens = 0 and slot_mapping = -1.
+ * nothing is written, context_lens = 0 and slot_mapping = -1.  With key and
+ * value both NULL only context_lens and slot_mapping are written (the slots
+ * for a later bs_rope_append, which then writes the rows).
  */
 int bs_decode_append(const int32_t* seq_rows, const int32_t* start_pos, int64_t num_rows,
                      const int32_t* block_tables, int64_t table_stride, int64_t table_rows,
@@ -229,6 +239,43 @@ int bs_step_metadata(const int32_t* seq_rows, const int32_t* start_pos, const in
                      int64_t num_blocks, int64_t num_tokens, int32_t* cu_q, int32_t* positions,
                      int32_t* slot_mapping, int32_t* context_lens, uint32_t* status,
                      void* stream);
+
+/*
+ * Fused model steps around the attention path, used by the engine's model
+ * step (each replaces a chain of framework ops of the reference TorchModel,
+ * src/server/torch_model.py, with its rounding points; dtype is the model's):
+ *  - bs_rms_norm:    per output row r with source row i = row_index[r] (or r):
+ *                    s = (x[i] + add[i]).to(dtype) (s = x[i] when add is NULL),
+ *                    sum_out[r] = s (when not NULL), and
+ *                    out[r] = weight * (s_f32 * rsqrt(mean(s_f32^2) + eps)).to(dtype)
+ *                    (:283-287, with the residual add of :272/:281 before it).
+ *                    sum_out may be x itself only without row_index; an index
+ *                    outside [0, x_rows) skips the row and sets
+ *                    BS_STATUS_BAD_INDEX in *status.
+ *  - bs_rope_append: rows of qkv = [q heads | k heads | v heads] after the
+ *                    projection; q and k rotated with cos/sin tables [pos, D]
+ *                    (rotate_half RoPE, :190-192, :262-264), q written to
+ *                    query_out [T, H, D], k and v to the pools
+ *                    [kv_heads, num_blocks, block_size, D] at slot_mapping
+ *                    (slots < 0 skipped) — PagedKVCache.append (:149-153).
+ *                    Tables hold num_positions rows; a position outside them
+ *                    or a slot past the pool skips the access and sets
+ *                    BS_STATUS_BAD_POSITION / BS_STATUS_BAD_SLOT in *status.
+ *  - bs_silu_mul:    out[t, i] = silu(gate[t, i]) * up[t, i], rows [gate | up]
+ *                    (:278-281).
+ */
+int bs_rms_norm(const void* x, int64_t x_row_stride, int64_t x_rows, const void* add,
+                int64_t add_row_stride, const int32_t* row_index, const void* weight, int64_t rows,
+                int64_t hidden, double eps, int32_t dtype, void* out, int64_t out_row_stride,
+                void* sum_out, int64_t sum_row_stride, uint32_t* status, void* stream);
+int bs_rope_append(const void* qkv, int64_t qkv_row_stride, int32_t dtype, const void* cos_table,
+                   const void* sin_table, int64_t num_positions, const int32_t* positions,
+                   const int32_t* slot_mapping, int64_t num_tokens, int64_t num_heads,
+                   int64_t num_kv_heads, int64_t head_dim, void* query_out, void* key_pool,
+                   void* value_pool, int32_t pool_dtype, int64_t num_blocks, int64_t block_size,
+                   uint32_t* status, void* stream);
+int bs_silu_mul(const void* gate_up, int64_t row_stride, int64_t num_tokens, int64_t intermediate,
+                int32_t dtype, void* out, void* stream);
 
 /*
  * Waits for `stream`, then reads and clears the status word at the start of a
