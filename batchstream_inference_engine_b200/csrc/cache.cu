@@ -85,7 +85,9 @@ __global__ void __launch_bounds__(kMetaThreads)
 
   if (blockIdx.x == 0) {
     for (int32_t r = tid; r <= R; r += kMetaThreads) cu_q[r] = cu[r];
-    for (int32_t r = tid; r < R; r += kMetaThreads) context_lens[r] = start_pos[r] + max(0, n_new[r]);
+    for (int32_t r = tid; r < R; r += kMetaThreads) {
+      context_lens[r] = start_pos[r] < 0 ? 0 : start_pos[r] + max(0, n_new[r]);
+    }
   }
 
   const int32_t t = blockIdx.x * kMetaThreads + tid;
@@ -102,6 +104,11 @@ __global__ void __launch_bounds__(kMetaThreads)
     if (cu[mid] <= t) lo = mid; else hi = mid - 1;
   }
   const int32_t r = lo;
+  if (start_pos[r] < 0) {  // padding row: its tokens read and write nothing
+    positions[t] = 0;
+    slots[t] = -1;
+    return;
+  }
   const int32_t pos = start_pos[r] + (t - cu[r]);
   positions[t] = pos;
   const int32_t row = seq_rows != nullptr ? seq_rows[r] : r;
@@ -118,35 +125,6 @@ __global__ void __launch_bounds__(kMetaThreads)
     return;
   }
   slots[t] = blk * block_size + pos % block_size;
-}
-
-// 8 elements per thread: 16-byte accesses on the bf16 side, 2 x 16 on fp32.
-__device__ __forceinline__ void load8(const __nv_bfloat16* p, float (&v)[8]) {
-  const uint4 raw = *reinterpret_cast<const uint4*>(p);
-  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw);
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const float2 f = __bfloat1622float2(h[i]);
-    v[2 * i] = f.x;
-    v[2 * i + 1] = f.y;
-  }
-}
-__device__ __forceinline__ void load8(const float* p, float (&v)[8]) {
-  const float4 a = reinterpret_cast<const float4*>(p)[0];
-  const float4 b = reinterpret_cast<const float4*>(p)[1];
-  v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
-  v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
-}
-__device__ __forceinline__ void store8(__nv_bfloat16* p, const float (&v)[8]) {
-  uint4 raw;
-  uint32_t* w = reinterpret_cast<uint32_t*>(&raw);
-#pragma unroll
-  for (int i = 0; i < 4; ++i) w[i] = pack_bf16x2(v[2 * i], v[2 * i + 1]);
-  *reinterpret_cast<uint4*>(p) = raw;
-}
-__device__ __forceinline__ void store8(float* p, const float (&v)[8]) {
-  reinterpret_cast<float4*>(p)[0] = make_float4(v[0], v[1], v[2], v[3]);
-  reinterpret_cast<float4*>(p)[1] = make_float4(v[4], v[5], v[6], v[7]);
 }
 
 // bf16 -> bf16 keeps the raw bits (no float round trip needed, but it is exact).

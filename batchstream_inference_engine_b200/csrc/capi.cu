@@ -31,14 +31,15 @@ int launch_step_metadata(const int32_t* seq_rows, const int32_t* start_pos, cons
 int launch_rms_norm(const void* x, int64_t x_stride, const void* add, int64_t add_stride,
                     const int32_t* index, int32_t x_rows, const void* w, int32_t rows,
                     int32_t hidden, float eps, void* out, int64_t out_stride, void* sum_out,
-                    int64_t sum_stride, bool bf16, uint32_t* status, cudaStream_t stream);
+                    int64_t sum_stride, bool bf16, bool vec, uint32_t* status,
+                    cudaStream_t stream);
 int launch_rope_append(const void* qkv, int64_t qkv_stride, const void* cos_t, const void* sin_t,
                        int32_t num_pos, const int32_t* pos, const int32_t* slots, int32_t ntok,
                        int32_t H, int32_t Hkv, int32_t D, void* q_out, void* k_pool,
                        void* v_pool, int64_t pool_slots, bool bf16, bool pool_bf16, int sms,
                        uint32_t* status, cudaStream_t stream);
 int launch_silu_mul(const void* gate_up, int64_t stride, int32_t ntok, int32_t inter, void* out,
-                    bool bf16, int sms, cudaStream_t stream);
+                    bool bf16, bool vec, int sms, cudaStream_t stream);
 int launch_decode_append(const int32_t* seq_rows, const int32_t* start_pos, int32_t R,
                          const int32_t* block_tables, int64_t bt_stride, int32_t bt_rows,
                          int32_t max_blocks, int32_t block_size, int32_t num_blocks,
@@ -764,10 +765,14 @@ int bs_rms_norm(const void* x, int64_t x_row_stride, int64_t x_rows, const void*
   BS_CHECK(row_index == nullptr || sum_out != x, "sum_out may alias x only without a row index");
   if (rows == 0) return BS_OK;
   BS_CHECK(x && weight && out, "null pointer argument");
+  const bool vec = hidden % 8 == 0 && x_row_stride % 8 == 0 && out_row_stride % 8 == 0 &&
+                   (add == nullptr || add_row_stride % 8 == 0) &&
+                   (sum_out == nullptr || sum_row_stride % 8 == 0) && aligned16(x) &&
+                   aligned16(add) && aligned16(weight) && aligned16(out) && aligned16(sum_out);
   const int rc = bsb::launch_rms_norm(
       x, x_row_stride, add, add_row_stride, row_index, static_cast<int32_t>(x_rows), weight,
       static_cast<int32_t>(rows), static_cast<int32_t>(hidden), static_cast<float>(eps), out,
-      out_row_stride, sum_out, sum_row_stride, dtype == BS_BF16, status,
+      out_row_stride, sum_out, sum_row_stride, dtype == BS_BF16, vec, status,
       static_cast<cudaStream_t>(stream));
   if (rc != 0) return cuda_fail(static_cast<cudaError_t>(rc), "rms_norm launch");
   count_launches(1);
@@ -820,9 +825,11 @@ int bs_silu_mul(const void* gate_up, int64_t row_stride, int64_t num_tokens, int
   BS_CHECK(gate_up && out, "null pointer argument");
   DeviceInfo* d = nullptr;
   if (int rc = current_device_info(&d)) return rc;
+  const bool vec = intermediate % 8 == 0 && row_stride % 8 == 0 && aligned16(gate_up) &&
+                   aligned16(out);
   const int rc = bsb::launch_silu_mul(gate_up, row_stride, static_cast<int32_t>(num_tokens),
                                       static_cast<int32_t>(intermediate), out, dtype == BS_BF16,
-                                      d->sms, static_cast<cudaStream_t>(stream));
+                                      vec, d->sms, static_cast<cudaStream_t>(stream));
   if (rc != 0) return cuda_fail(static_cast<cudaError_t>(rc), "silu_mul launch");
   count_launches(1);
   return BS_OK;

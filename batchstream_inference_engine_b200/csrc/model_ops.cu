@@ -43,60 +43,117 @@ __device__ __forceinline__ float rt<float>(float x) { return x; }
 template <>
 __device__ __forceinline__ float rt<__nv_bfloat16>(float x) { return round_bf16(x); }
 
-// One CTA per output row r, reading source row i = index ? index[r] : r:
+// Rounds 8 values to T as separate T-typed ops would (packed conversions for
+// bf16).
+template <typename T>
+__device__ __forceinline__ void round8(float (&v)[8]);
+template <>
+__device__ __forceinline__ void round8<float>(float (&)[8]) {}
+template <>
+__device__ __forceinline__ void round8<__nv_bfloat16>(float (&v)[8]) {
+#pragma unroll
+  for (int j = 0; j < 8; j += 2) round_bf16x2(v[j], v[j + 1]);
+}
+
+// One warp per output row r, reading source row i = index ? index[r] : r:
 // s = T(x[i] + add[i]) (s = x[i] without add), sum_out[r] = s, out[r] =
 // RMSNorm(s).  sum_out may be x itself (the residual stream updated in place:
-// every element is read and written by the same thread) when index is null.
-template <typename T>
-__global__ void __launch_bounds__(256)
+// every element is read and written by the same lane) when index is null.
+// VEC: 8 elements per access (hidden and every row stride a multiple of 8,
+// 16-byte aligned rows).
+constexpr int kNormRowsPerCta = 4;
+
+template <typename T, bool VEC>
+__global__ void __launch_bounds__(32 * kNormRowsPerCta)
     rms_norm_kernel(const T* x, int64_t x_stride, const T* __restrict__ add, int64_t add_stride,
                     const int32_t* __restrict__ index, int32_t x_rows, const T* __restrict__ w,
-                    int32_t hidden, float eps, T* __restrict__ out, int64_t out_stride, T* sum_out,
-                    int64_t sum_stride, uint32_t* status) {
+                    int32_t rows, int32_t hidden, float eps, T* __restrict__ out,
+                    int64_t out_stride, T* sum_out, int64_t sum_stride, uint32_t* status) {
   pdl_trigger();
   pdl_wait();
-  __shared__ float part[8];
-  int64_t src = blockIdx.x;
+  const int lane = threadIdx.x & 31;
+  const int32_t r = blockIdx.x * kNormRowsPerCta + (threadIdx.x >> 5);
+  if (r >= rows) return;
+  int64_t src = r;
   if (index != nullptr) {
-    src = index[blockIdx.x];
+    src = index[r];
     if (src < 0 || src >= x_rows) {
-      if (threadIdx.x == 0) set_status(status, kStatusBadIndex);
+      if (lane == 0) set_status(status, kStatusBadIndex);
       return;
     }
   }
   const T* row = x + src * x_stride;
   const T* arow = add != nullptr ? add + src * add_stride : nullptr;
-  T* srow = sum_out != nullptr ? sum_out + static_cast<int64_t>(blockIdx.x) * sum_stride : nullptr;
+  T* srow = sum_out != nullptr ? sum_out + static_cast<int64_t>(r) * sum_stride : nullptr;
+  T* orow = out + static_cast<int64_t>(r) * out_stride;
   float ss = 0.f;
-  for (int i = threadIdx.x; i < hidden; i += blockDim.x) {
-    float v = ld<T>(row + i);
-    if (arow != nullptr) v = rt<T>(__fadd_rn(v, ld<T>(arow + i)));
-    if (srow != nullptr) srow[i] = st<T>(v);
-    ss = fmaf(v, v, ss);
+  if constexpr (VEC) {
+    for (int32_t i = lane * 8; i < hidden; i += 256) {
+      float v[8];
+      load8(row + i, v);
+      if (arow != nullptr) {
+        float a[8];
+        load8(arow + i, a);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[j] = __fadd_rn(v[j], a[j]);
+        round8<T>(v);
+      }
+      if (srow != nullptr) store8(srow + i, v);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) ss = fmaf(v[j], v[j], ss);
+    }
+  } else {
+    for (int32_t i = lane; i < hidden; i += 32) {
+      float v = ld<T>(row + i);
+      if (arow != nullptr) v = rt<T>(__fadd_rn(v, ld<T>(arow + i)));
+      if (srow != nullptr) srow[i] = st<T>(v);
+      ss = fmaf(v, v, ss);
+    }
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-  if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = ss;
-  __syncthreads();
-  float tot = 0.f;
-  for (int i = 0; i < (blockDim.x >> 5); ++i) tot += part[i];
-  const float inv = rsqrtf(tot / static_cast<float>(hidden) + eps);
-  T* o = out + blockIdx.x * out_stride;
-  for (int i = threadIdx.x; i < hidden; i += blockDim.x) {
-    float v = ld<T>(row + i);  // this thread's own element of s, as computed above
-    if (srow != nullptr) v = ld<T>(srow + i);
-    else if (arow != nullptr) v = rt<T>(__fadd_rn(v, ld<T>(arow + i)));
-    const float normalized = rt<T>(__fmul_rn(v, inv));
-    o[i] = st<T>(__fmul_rn(ld<T>(w + i), normalized));
+  const float inv = rsqrtf(ss / static_cast<float>(hidden) + eps);
+  // Second pass over this lane's own elements of s (re-read, or recomputed).
+  if constexpr (VEC) {
+    for (int32_t i = lane * 8; i < hidden; i += 256) {
+      float v[8], wt[8];
+      if (srow != nullptr) {
+        load8(srow + i, v);
+      } else {
+        load8(row + i, v);
+        if (arow != nullptr) {
+          float a[8];
+          load8(arow + i, a);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) v[j] = __fadd_rn(v[j], a[j]);
+          round8<T>(v);
+        }
+      }
+      load8(w + i, wt);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[j] = __fmul_rn(v[j], inv);
+      round8<T>(v);  // normalized.to(T)
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[j] = __fmul_rn(wt[j], v[j]);
+      store8(orow + i, v);
+    }
+  } else {
+    for (int32_t i = lane; i < hidden; i += 32) {
+      float v = srow != nullptr ? ld<T>(srow + i) : ld<T>(row + i);
+      if (srow == nullptr && arow != nullptr) v = rt<T>(__fadd_rn(v, ld<T>(arow + i)));
+      const float normalized = rt<T>(__fmul_rn(v, inv));
+      orow[i] = st<T>(__fmul_rn(ld<T>(w + i), normalized));
+    }
   }
 }
 
 // One thread per (token, head, dim pair d, d + D/2) of q and k; v is copied.
 // qkv rows: [H*D | Hkv*D | Hkv*D].  A negative slot skips the pool write (a
 // padding row); a slot past the pool or a position outside [0, num_pos) skips
-// the access and sets a status bit.
+// the access and sets a status bit.  Grid: x over a token's pairs, y over
+// tokens.
 template <typename T, typename Tpool>
-__global__ void __launch_bounds__(256)
+__global__ void __launch_bounds__(128)
     rope_append_kernel(const T* __restrict__ qkv, int64_t qkv_stride,
                        const T* __restrict__ cos_t, const T* __restrict__ sin_t,
                        int32_t num_pos, const int32_t* __restrict__ pos,
@@ -106,13 +163,10 @@ __global__ void __launch_bounds__(256)
   pdl_trigger();
   pdl_wait();
   const int32_t half = D >> 1;
-  const int32_t per_tok = (H + 2 * Hkv) * half;
-  const int64_t total = static_cast<int64_t>(ntok) * per_tok;
-  for (int64_t idx = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; idx < total;
-       idx += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    const int32_t t = static_cast<int32_t>(idx / per_tok);
-    const int32_t r = static_cast<int32_t>(idx - static_cast<int64_t>(t) * per_tok);
-    const int32_t hh = r / half, d = r - hh * half;  // head in [0, H + 2 Hkv)
+  const int32_t r = blockIdx.x * blockDim.x + threadIdx.x;
+  if (r >= (H + 2 * Hkv) * half) return;
+  const int32_t hh = r / half, d = r - hh * half;  // head in [0, H + 2 Hkv)
+  for (int32_t t = blockIdx.y; t < ntok; t += gridDim.y) {
     const T* row = qkv + t * qkv_stride + hh * D;
     const float a = ld<T>(row + d), b = ld<T>(row + d + half);
     const int32_t slot = hh >= H ? slots[t] : -1;
@@ -144,38 +198,50 @@ __global__ void __launch_bounds__(256)
       T* dst = q_out + (static_cast<int64_t>(t) * H + hh) * D;
       dst[d] = st<T>(lo);
       dst[d + half] = st<T>(hi);
-    } else {
-      if (slot >= 0) {
-        Tpool* dst = k_pool + (static_cast<int64_t>(hh - H) * pool_slots + slot) * D;
-        dst[d] = st<Tpool>(lo);
-        dst[d + half] = st<Tpool>(hi);
-      }
+    } else if (slot >= 0) {
+      Tpool* dst = k_pool + (static_cast<int64_t>(hh - H) * pool_slots + slot) * D;
+      dst[d] = st<Tpool>(lo);
+      dst[d + half] = st<Tpool>(hi);
     }
   }
 }
 
-template <typename T>
-__global__ void __launch_bounds__(256)
+// Rows [gate | up] -> silu(gate) * up.  Grid: x over a row's elements (8 per
+// thread when VEC: intermediate and the row stride multiples of 8, 16-byte
+// aligned rows), y over tokens.
+template <typename T, bool VEC>
+__global__ void __launch_bounds__(128)
     silu_mul_kernel(const T* __restrict__ gate_up, int64_t stride, int32_t ntok, int32_t inter,
                     T* __restrict__ out) {
   pdl_trigger();
   pdl_wait();
-  const int64_t total = static_cast<int64_t>(ntok) * inter;
-  for (int64_t idx = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; idx < total;
-       idx += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    const int64_t t = idx / inter;
-    const int32_t i = static_cast<int32_t>(idx - t * inter);
-    const float g = ld<T>(gate_up + t * stride + i);
-    const float u = ld<T>(gate_up + t * stride + inter + i);
-    const float s = rt<T>(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))));
-    out[idx] = st<T>(__fmul_rn(s, u));
+  const int32_t c = (blockIdx.x * blockDim.x + threadIdx.x) * (VEC ? 8 : 1);
+  if (c >= inter) return;
+  for (int32_t t = blockIdx.y; t < ntok; t += gridDim.y) {
+    const T* g = gate_up + t * stride + c;
+    T* o = out + static_cast<int64_t>(t) * inter + c;
+    if constexpr (VEC) {
+      float gv[8], uv[8];
+      load8(g, gv);
+      load8(g + inter, uv);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) gv[j] = __fdiv_rn(gv[j], __fadd_rn(1.0f, expf(-gv[j])));
+      round8<T>(gv);  // silu(gate) in T
+#pragma unroll
+      for (int j = 0; j < 8; ++j) gv[j] = __fmul_rn(gv[j], uv[j]);
+      store8(o, gv);
+    } else {
+      const float gs = ld<T>(g), u = ld<T>(g + inter);
+      const float s = rt<T>(__fdiv_rn(gs, __fadd_rn(1.0f, expf(-gs))));
+      *o = st<T>(__fmul_rn(s, u));
+    }
   }
 }
 
-cudaLaunchConfig_t cfg_of(int64_t grid, int threads, cudaStream_t stream,
+cudaLaunchConfig_t cfg_of(dim3 grid, int threads, cudaStream_t stream,
                           cudaLaunchAttribute* attr) {
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(static_cast<unsigned>(grid));
+  cfg.gridDim = grid;
   cfg.blockDim = dim3(threads);
   cfg.stream = stream;
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -185,28 +251,31 @@ cudaLaunchConfig_t cfg_of(int64_t grid, int threads, cudaStream_t stream,
   return cfg;
 }
 
-int64_t grid_for(int64_t work, int sms) {
-  int64_t g = (work + 255) / 256;
-  if (g > static_cast<int64_t>(sms) * 8) g = static_cast<int64_t>(sms) * 8;
-  return g < 1 ? 1 : g;
-}
+constexpr int32_t kMaxGridY = 65535;
 
 }  // namespace
 
 int launch_rms_norm(const void* x, int64_t x_stride, const void* add, int64_t add_stride,
                     const int32_t* index, int32_t x_rows, const void* w, int32_t rows,
                     int32_t hidden, float eps, void* out, int64_t out_stride, void* sum_out,
-                    int64_t sum_stride, bool bf16, uint32_t* status, cudaStream_t stream) {
+                    int64_t sum_stride, bool bf16, bool vec, uint32_t* status,
+                    cudaStream_t stream) {
   if (rows == 0) return 0;
   cudaLaunchAttribute attr[1];
-  cudaLaunchConfig_t cfg = cfg_of(rows, 256, stream, attr);
-#define BS_RMS(T)                                                                               \
+  cudaLaunchConfig_t cfg = cfg_of(dim3((rows + kNormRowsPerCta - 1) / kNormRowsPerCta),
+                                  32 * kNormRowsPerCta, stream, attr);
+#define BS_RMS(T, V)                                                                            \
   return static_cast<int>(cudaLaunchKernelEx(                                                   \
-      &cfg, rms_norm_kernel<T>, static_cast<const T*>(x), x_stride, static_cast<const T*>(add), \
-      add_stride, index, x_rows, static_cast<const T*>(w), hidden, eps, static_cast<T*>(out),   \
-      out_stride, static_cast<T*>(sum_out), sum_stride, status))
-  if (bf16) BS_RMS(__nv_bfloat16);
-  BS_RMS(float);
+      &cfg, rms_norm_kernel<T, V>, static_cast<const T*>(x), x_stride,                          \
+      static_cast<const T*>(add), add_stride, index, x_rows, static_cast<const T*>(w), rows,    \
+      hidden, eps, static_cast<T*>(out), out_stride, static_cast<T*>(sum_out), sum_stride,      \
+      status))
+  if (bf16) {
+    if (vec) BS_RMS(__nv_bfloat16, true);
+    BS_RMS(__nv_bfloat16, false);
+  }
+  if (vec) BS_RMS(float, true);
+  BS_RMS(float, false);
 #undef BS_RMS
 }
 
@@ -215,10 +284,12 @@ int launch_rope_append(const void* qkv, int64_t qkv_stride, const void* cos_t, c
                        int32_t H, int32_t Hkv, int32_t D, void* q_out, void* k_pool,
                        void* v_pool, int64_t pool_slots, bool bf16, bool pool_bf16, int sms,
                        uint32_t* status, cudaStream_t stream) {
+  (void)sms;
   if (ntok == 0) return 0;
-  const int64_t work = static_cast<int64_t>(ntok) * (H + 2 * Hkv) * (D / 2);
+  const int32_t pairs = (H + 2 * Hkv) * (D / 2);
   cudaLaunchAttribute attr[1];
-  cudaLaunchConfig_t cfg = cfg_of(grid_for(work, sms), 256, stream, attr);
+  cudaLaunchConfig_t cfg =
+      cfg_of(dim3((pairs + 127) / 128, ntok < kMaxGridY ? ntok : kMaxGridY), 128, stream, attr);
 #define BS_ROPE(T, TP)                                                                          \
   return static_cast<int>(cudaLaunchKernelEx(                                                   \
       &cfg, rope_append_kernel<T, TP>, static_cast<const T*>(qkv), qkv_stride,                  \
@@ -233,18 +304,25 @@ int launch_rope_append(const void* qkv, int64_t qkv_stride, const void* cos_t, c
 }
 
 int launch_silu_mul(const void* gate_up, int64_t stride, int32_t ntok, int32_t inter, void* out,
-                    bool bf16, int sms, cudaStream_t stream) {
+                    bool bf16, bool vec, int sms, cudaStream_t stream) {
+  (void)sms;
   if (ntok == 0) return 0;
+  const int32_t per_thread = vec ? 8 : 1;
+  const int32_t threads = (inter + per_thread - 1) / per_thread;
   cudaLaunchAttribute attr[1];
   cudaLaunchConfig_t cfg =
-      cfg_of(grid_for(static_cast<int64_t>(ntok) * inter, sms), 256, stream, attr);
-  if (bf16)
-    return static_cast<int>(cudaLaunchKernelEx(&cfg, silu_mul_kernel<__nv_bfloat16>,
-                                               static_cast<const __nv_bfloat16*>(gate_up), stride,
-                                               ntok, inter, static_cast<__nv_bfloat16*>(out)));
-  return static_cast<int>(cudaLaunchKernelEx(&cfg, silu_mul_kernel<float>,
-                                             static_cast<const float*>(gate_up), stride, ntok,
-                                             inter, static_cast<float*>(out)));
+      cfg_of(dim3((threads + 127) / 128, ntok < kMaxGridY ? ntok : kMaxGridY), 128, stream, attr);
+#define BS_SILU(T, V)                                                                           \
+  return static_cast<int>(cudaLaunchKernelEx(&cfg, silu_mul_kernel<T, V>,                       \
+                                             static_cast<const T*>(gate_up), stride, ntok, inter, \
+                                             static_cast<T*>(out)))
+  if (bf16) {
+    if (vec) BS_SILU(__nv_bfloat16, true);
+    BS_SILU(__nv_bfloat16, false);
+  }
+  if (vec) BS_SILU(float, true);
+  BS_SILU(float, false);
+#undef BS_SILU
 }
 
 }  // namespace bsb

@@ -93,6 +93,26 @@ def take_status(device: torch.device | None = None) -> int:
     return bits.value
 
 
+def decode_workspace_bytes(num_seqs: int, num_heads: int, num_kv_heads: int, head_dim: int,
+                           block_size: int, dtype: torch.dtype) -> int:
+    """Workspace that ``paged_attention_batched`` needs for this shape."""
+    got = ctypes.c_uint64(0)
+    check(lib().bs_paged_attention_batched_workspace_bytes(
+        num_seqs, num_heads, num_kv_heads, head_dim, block_size, dtype_code(dtype),
+        ctypes.byref(got)))
+    return got.value
+
+
+def prefill_workspace_bytes(num_tokens: int, num_heads: int, num_kv_heads: int, head_dim: int,
+                            block_size: int, dtype: torch.dtype) -> int:
+    """Workspace that ``prefill_attention`` needs for this shape."""
+    got = ctypes.c_uint64(0)
+    check(lib().bs_prefill_attention_workspace_bytes(
+        num_tokens, num_heads, num_kv_heads, head_dim, block_size, dtype_code(dtype),
+        ctypes.byref(got)))
+    return got.value
+
+
 def kernel_launches() -> int:
     """Kernels this package's library has launched (or recorded into a CUDA
     graph) in this process."""
@@ -482,6 +502,8 @@ __all__ = [
     "silu_mul",
     "take_status",
     "kernel_launches",
+    "decode_workspace_bytes",
+    "prefill_workspace_bytes",
     "workspace_for",
     "dtype_code",
     "_lib",

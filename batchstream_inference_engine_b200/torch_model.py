@@ -201,8 +201,9 @@ class TorchModel:
 
     def __init__(self, config: ModelConfig, weights: dict[str, torch.Tensor],
                  device: torch.device | str = "cuda", dtype: torch.dtype = torch.bfloat16,
-                 max_position: int = 32768, decode_graphs: bool = True,
-                 max_graph_batch: int = 256):
+                 max_position: int = 32768, step_graphs: bool = True,
+                 max_graph_batch: int = 256, max_graph_prefill: int = 512,
+                 max_graph_chunks: int = 8):
         self.config = config
         self.device = torch.device(device)
         self.dtype = dtype
@@ -246,13 +247,18 @@ class TorchModel:
                           d2h_bytes=0)
         self._host = None  # pinned staging buffer for per-step row metadata
         self._host_free = None  # event: the last copy out of it has completed
-        # Decode-only steps replay CUDA graphs captured per power-of-two batch
-        # size (rows padded up), on a stream no eager call uses.
-        self.decode_graphs = decode_graphs and self.device.type == "cuda"
+        # Steps replay CUDA graphs captured per padded shape (decode rows, prompt
+        # chunks, prompt tokens), on a stream no eager call uses; steps beyond
+        # max_graph_batch decode rows, max_graph_chunks chunks or
+        # max_graph_prefill prompt tokens run eagerly.
+        self.step_graphs = step_graphs and self.device.type == "cuda"
         self.max_graph_batch = max_graph_batch
-        self._graphs: dict[tuple[int, int], tuple] = {}
+        self.max_graph_prefill = max_graph_prefill
+        self.max_graph_chunks = max_graph_chunks
+        self._graphs: dict[tuple, tuple] = {}
         self._graph_stream = None
         self._graph_pool = None
+        self._graph_ws = None
 
     @classmethod
     def load(cls, model_dir: Path, device="cuda", dtype=torch.bfloat16) -> "TorchModel":
@@ -271,14 +277,16 @@ class TorchModel:
 
     @torch.inference_mode()
     def next_tokens(self, groups: list[tuple[list[int], PagedKVCache]]) -> list[int]:
-        """Greedy next token of each group: argmax of the float last-token
-        logits (first index on ties), reduced on the device.  A step in which
-        every group brings one token replays a captured decode graph."""
-        if (self.decode_graphs and len(groups) <= self.max_graph_batch
-                and all(len(tokens) == 1 for tokens, _ in groups)):
-            return self._graph_step(groups)
+        """Greedy next token of each group: argmax of the last-token logits
+        (first index on ties; bf16 -> fp32 is exact, so the argmax of the
+        model-dtype logits is the reference's argmax of logits.float()),
+        reduced on the device.  Steps within the graph limits replay a
+        captured step graph."""
+        key = self._graph_key([len(tokens) for tokens, _ in groups]) if self.step_graphs else None
+        if key is not None:
+            return self._graph_step(groups, key)
         logits = self.forward_batch(groups)
-        ids = logits.float().argmax(dim=-1).to(torch.int32)
+        ids = logits.argmax(dim=-1).to(torch.int32)
         host = torch.empty(ids.shape, dtype=torch.int32, pin_memory=True)
         host.copy_(ids, non_blocking=True)
         self.stats["d2h_bytes"] += 4 * ids.numel()
@@ -398,100 +406,173 @@ class TorchModel:
             delta = F.linear(ops.silu_mul(F.linear(normed, lw["gate_up_w"])), lw["down_w"])
         return ops.rms_norm(hidden, self.final_norm, eps, add=delta, row_index=last_rows)
 
-    # ---------------------------------------------------------------- decode graphs
+    # ---------------------------------------------------------------- step graphs
 
-    def _decode_forward(self, pool: PagedKVPool, rows, start, pos, ctx, tokens) -> torch.Tensor:
-        """Greedy ids [B] (int32, on the device) of B single-token rows: row r is
-        block-table row rows[r] at position start[r] with context ctx[r] after
-        the step; start[r] < 0 and ctx[r] == 0 mark a padding row.  Launches
-        only (no host synchronisation), so it can be captured."""
+    def _decode_bucket(self, n: int) -> int:
+        """Padded decode rows: powers of two to 32, then multiples of 32."""
+        if n == 0:
+            return 0
+        b = 1
+        while b < min(n, 32):
+            b *= 2
+        if n > 32:
+            b = -(-n // 32) * 32
+        return min(b, self.max_graph_batch)
+
+    def _graph_key(self, lengths: list[int]):
+        """(decode rows, chunk rows, chunk tokens) of the graph that serves a
+        step with these per-row token counts, or None (run eagerly)."""
+        n_dec = 0
+        while n_dec < len(lengths) and lengths[n_dec] == 1:
+            n_dec += 1
+        if n_dec > self.max_graph_batch:
+            return None
+        chunks = lengths[n_dec:]
+        if not chunks:
+            return (self._decode_bucket(n_dec), 0, 0)
+        tok = sum(chunks)
+        if len(chunks) > self.max_graph_chunks or tok > self.max_graph_prefill:
+            return None
+        rows = 1
+        while rows < len(chunks):
+            rows *= 2
+        q = 64
+        while q < tok:
+            q *= 2
+        return (self._decode_bucket(n_dec), rows, q)
+
+    def _graph_forward(self, pool: PagedKVPool, key, inputs: torch.Tensor) -> torch.Tensor:
+        """Greedy ids (int32 [B + P], on the device) of one padded step: B
+        decode rows then P prompt-chunk rows holding up to Q tokens, described
+        by the int32 ``inputs`` (see ``_graph_inputs``).  Launches only (no host
+        synchronisation), so it can be captured."""
         config = self.config
+        B, P, Q = key
+        R, T = B + P, B + Q
         alloc = pool.allocator
-        _, slots = ops.decode_append(None, None, pool.keys[0], pool.values[0],
-                                     alloc.device_tables, start, seq_rows=rows)
+        rows, start, n_new, after, ends, tokens = inputs.split([R, R, R, B, R, T])
+        cu_q, positions, slots, ctx = ops.step_metadata(
+            alloc.device_tables, start, n_new, T, pool.block_size, pool.num_blocks,
+            seq_rows=rows)
+        pre_cu = cu_q[B:] - B if P else None
+        scale = config.head_dim ** -0.5
 
         def attend(q, kp, vp, attended):
-            ops.paged_attention_batched(q, kp, vp, alloc.device_tables, ctx,
-                                        config.head_dim ** -0.5, seq_rows=rows, out=attended,
-                                        lens_ready=True, after_append=True)
+            if B:
+                ops.paged_attention_batched(q[:B], kp, vp, alloc.device_tables, after, scale,
+                                            seq_rows=rows[:B], out=attended[:B], lens_ready=True,
+                                            after_append=True)
+            if P:
+                ops.prefill_attention(q[B:], kp, vp, alloc.device_tables, pre_cu, ctx[B:], scale,
+                                      max_query_len=Q, seq_rows=rows[B:], out=attended[B:])
 
-        last = self._layers(pool, tokens, pos, slots, None, attend)
-        logits = F.linear(last, self.embed)
-        return logits.float().argmax(dim=-1).to(torch.int32)
+        last = self._layers(pool, tokens, positions, slots, ends, attend)
+        return F.linear(last, self.embed).argmax(dim=-1).to(torch.int32)
 
-    def _capture_graphs(self, pool: PagedKVPool) -> None:
-        """Captures every power-of-two batch size up to max_graph_batch for this
-        pool, largest first, so the stream's workspace is sized before the first
-        capture and never moves afterwards."""
+    @staticmethod
+    def _graph_inputs(key, rows, starts, lengths, n_dec, tokens) -> list[int]:
+        """The int32 input vector of a padded step: rows | start | n_new (R
+        each) | context after the step of the decode rows (B) | token index of
+        each row's last token (R) | tokens (T).  Padding rows have start -1
+        (they read and write nothing); padding tokens are 0."""
+        B, P, Q = key
+        pd, pp = B - n_dec, P - (len(rows) - n_dec)
+        lengths_p = lengths[n_dec:]
+        ends, acc = list(range(n_dec)) + [0] * pd, B
+        for n in lengths_p:
+            acc += n
+            ends.append(acc - 1)
+        flat_p = [t for ts in tokens[n_dec:] for t in ts]
+        return (rows[:n_dec] + [0] * pd + rows[n_dec:] + [0] * pp
+                + starts[:n_dec] + [-1] * pd + starts[n_dec:] + [-1] * pp
+                + [1] * B + lengths_p + [0] * pp
+                + [s + 1 for s in starts[:n_dec]] + [0] * pd
+                + ends + [0] * pp
+                + [ts[0] for ts in tokens[:n_dec]] + [0] * pd + flat_p + [0] * (Q - len(flat_p)))
+
+    def _reserve_graph_workspace(self, block_size: int) -> None:
+        """Sizes the graph stream's workspace for the largest graph before the
+        first capture: a captured launch keeps the buffer's address."""
+        c = self.config
+        need = max(
+            ops.decode_workspace_bytes(self.max_graph_batch, c.num_heads, c.num_kv_heads,
+                                       c.head_dim, block_size, self.dtype),
+            ops.prefill_workspace_bytes(self.max_graph_prefill, c.num_heads, c.num_kv_heads,
+                                        c.head_dim, block_size, self.dtype))
+        self._graph_ws = ops.workspace_for(self.device, need)
+
+    def _capture(self, pool: PagedKVPool, key):
         if self._graph_stream is None:
             self._graph_stream = torch.cuda.Stream(self.device)
             self._graph_pool = torch.cuda.graph_pool_handle()
-        sizes = []
-        b = 1
-        while b < self.max_graph_batch:
-            sizes.append(b)
-            b *= 2
-        sizes.append(self.max_graph_batch)
         stream = self._graph_stream
         stream.wait_stream(torch.cuda.current_stream(self.device))
         with torch.cuda.stream(stream):
-            for B in sorted(set(sizes), reverse=True):
-                inputs = torch.zeros((5, B), dtype=torch.int32, device=self.device)
-                inputs[1].fill_(-1)  # all padding while warming up and capturing
-                for _ in range(2):
-                    self._decode_forward(pool, *inputs)
-                stream.synchronize()
-                graph = torch.cuda.CUDAGraph()
-                before = ops.kernel_launches()
-                with torch.cuda.graph(graph, pool=self._graph_pool, stream=stream):
-                    ids = self._decode_forward(pool, *inputs)
-                # This package's kernels in the graph, launched again by each replay.
-                self._graphs[(id(pool), B)] = (inputs, graph, ids, ops.kernel_launches() - before)
+            if self._graph_ws is None:
+                self._reserve_graph_workspace(pool.block_size)
+            B, P, Q = key
+            R = B + P
+            # An all-padding step while warming up and capturing: nothing is
+            # read from or written to the pool.
+            inputs = torch.tensor([0] * R + [-1] * R + [1] * B + [0] * P + [0] * B + [0] * R
+                                  + [0] * (B + Q), dtype=torch.int32, device=self.device)
+            self._graph_forward(pool, key, inputs)
+            stream.synchronize()
+            graph = torch.cuda.CUDAGraph()
+            before = ops.kernel_launches()
+            with torch.cuda.graph(graph, pool=self._graph_pool, stream=stream):
+                ids = self._graph_forward(pool, key, inputs)
+            launches = ops.kernel_launches() - before
+            if ops.workspace_for(self.device, 0).data_ptr() != self._graph_ws.data_ptr():
+                raise RuntimeError("the graph workspace moved during capture")
             ops.take_status(self.device)
         torch.cuda.current_stream(self.device).wait_stream(stream)
+        entry = (inputs, graph, ids, launches)
+        self._graphs[(id(pool),) + key] = entry
+        return entry
 
-    def _graph_step(self, groups) -> list[int]:
+    def _graph_step(self, groups, key) -> list[int]:
         config = self.config
         pool = groups[0][1]._pool
-        if (id(pool), 1) not in self._graphs:
-            self._capture_graphs(pool)
-        for _, cache in groups:
-            cache.reserve(1)
+        entry = self._graphs.get((id(pool),) + key)
+        if entry is None:
+            entry = self._capture(pool, key)
+        inputs, graph, ids, graph_launches = entry
+        for tokens, cache in groups:
+            cache.reserve(len(tokens))
         alloc = pool.allocator
         self.stats["h2d_bytes"] += 16 * alloc.sync_device()
-        R = len(groups)
-        B = 1
-        while B < R:
-            B *= 2
-        B = min(B, self.max_graph_batch)
-        inputs, graph, ids, graph_launches = self._graphs[(id(pool), B)]
+        lengths = [len(tokens) for tokens, _ in groups]
         starts = [cache.length for _, cache in groups]
-        if max(starts) + 1 > self.max_position:
+        if max(s + n for s, n in zip(starts, lengths)) > self.max_position:
             raise RuntimeError(f"positions beyond the rotary table ({self.max_position})")
-        pad = B - R
-        rows = [alloc.row(cache.seq_id) for _, cache in groups] + [0] * pad
-        values = (rows + starts + [-1] * pad + starts + [0] * pad
-                  + [s + 1 for s in starts] + [0] * pad
-                  + [tokens[0] for tokens, _ in groups] + [0] * pad)
-        inputs.view(-1).copy_(self._stage(values))
+        n_dec = 0
+        while n_dec < len(lengths) and lengths[n_dec] == 1:
+            n_dec += 1
+        rows = [alloc.row(cache.seq_id) for _, cache in groups]
+        values = self._graph_inputs(key, rows, starts, lengths, n_dec,
+                                    [tokens for tokens, _ in groups])
+        inputs.copy_(self._stage(values))
         graph.replay()
-        host = torch.empty(R, dtype=torch.int32, pin_memory=True)
-        host.copy_(ids[:R], non_blocking=True)
+        B = key[0]
+        host = torch.empty(ids.numel(), dtype=torch.int32, pin_memory=True)
+        host.copy_(ids, non_blocking=True)
         torch.cuda.current_stream(self.device).synchronize()
         with torch.cuda.stream(self._graph_stream):
             ops.take_status(self.device)  # the graphs' kernels report here
         ops.take_status(self.device)
-        for _, cache in groups:
-            cache.advance(1)
+        for tokens, cache in groups:
+            cache.advance(len(tokens))
         st = self.stats
         st["steps"] += 1
-        st["tokens"] += R
-        st["rows"] += R
+        st["tokens"] += sum(lengths)
+        st["rows"] += len(groups)
         st["attn_flops"] += config.num_layers * 4 * config.num_heads * config.head_dim * sum(
-            s + 1 for s in starts)
+            n * s + n * (n + 1) // 2 for s, n in zip(starts, lengths))
         st["launches"] += graph_launches
-        st["d2h_bytes"] += 4 * R
-        return host.tolist()
+        st["d2h_bytes"] += 4 * ids.numel()
+        out = host.tolist()
+        return out[:n_dec] + out[B: B + len(groups) - n_dec]
 
 
 __all__ = ["ModelConfig", "PagedKVPool", "PagedKVCache", "TorchModel", "QWEN25_05B",

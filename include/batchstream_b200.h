@@ -231,7 +231,10 @@ int bs_decode_append(const int32_t* seq_rows, const int32_t* start_pos, int64_t 
  * on the host in TorchModel._hidden_states, src/server/torch_model.py:231-241,
  * and per token through BlockAllocator.locate).  Writes cu_q[num_rows + 1],
  * positions[num_tokens], slot_mapping[num_tokens] and
- * context_lens[num_rows] = start_pos + n_new.  num_tokens = sum(n_new).
+ * context_lens[num_rows] = start_pos + n_new.  num_tokens is normally
+ * sum(n_new); tokens past the last row, and the tokens of a padding row
+ * (start_pos < 0, context length 0), get position 0 and slot -1, so a
+ * fixed-size (graph-captured) step can carry padding.
  */
 int bs_step_metadata(const int32_t* seq_rows, const int32_t* start_pos, const int32_t* n_new,
                      int64_t num_rows, const int32_t* block_tables, int64_t table_stride,

@@ -79,6 +79,37 @@ def test_step_metadata_matches_locate():
     assert ops.take_status() == 0
 
 
+def test_step_metadata_padding_rows_and_tokens():
+    # A fixed-size step: real rows interleaved with padding rows (start < 0),
+    # and more tokens than the rows hold.  Real rows are unaffected; padding
+    # tokens get position 0 and slot -1, padding rows context length 0.
+    alloc, lengths = grown_allocator(seed=3)
+    seqs = list(lengths)[:5]
+    start = [lengths[s] - 1 for s in seqs]
+    n_new = [1] * len(seqs)
+    rows = [alloc.row(s) for s in seqs]
+    # Insert padding: one decode-style padding row (1 token) and one empty row.
+    start_p = start[:2] + [-1] + start[2:] + [-1]
+    n_p = n_new[:2] + [1] + n_new[2:] + [0]
+    rows_p = rows[:2] + [0] + rows[2:] + [0]
+    T = sum(n_p) + 7
+    cu, pos, slots, ctx = ops.step_metadata(
+        alloc.device_tables, torch.tensor(start_p, dtype=torch.int32, device=DEV),
+        torch.tensor(n_p, dtype=torch.int32, device=DEV), T, 16, alloc.num_blocks,
+        seq_rows=torch.tensor(rows_p, dtype=torch.int32, device=DEV))
+    assert ops.take_status() == 0
+    want_pos, want_slots = oracle.slot_mapping([alloc.block_table(s) for s in seqs], start, n_new,
+                                               16)
+    pos, slots = pos.cpu().tolist(), slots.cpu().tolist()
+    real = [0, 1, 3, 4, 5]  # token index of each real row
+    assert [pos[t] for t in real] == want_pos.tolist()
+    assert [slots[t] for t in real] == want_slots.tolist()
+    assert pos[2] == 0 and slots[2] == -1
+    assert pos[6:] == [0] * 7 and slots[6:] == [-1] * 7
+    assert ctx.cpu().tolist() == [s + 1 for s in start[:2]] + [0] + [s + 1 for s in start[2:]] + [0]
+    assert cu.cpu().tolist() == [0, 1, 2, 3, 4, 5, 6, 6]
+
+
 @pytest.mark.parametrize("in_dtype", [torch.float32, torch.bfloat16])
 @pytest.mark.parametrize("pool_dtype", [torch.float32, torch.bfloat16])
 @pytest.mark.parametrize("head_dim", [64, 4])

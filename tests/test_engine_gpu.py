@@ -10,9 +10,10 @@ N(0, 0.02), RMSNorm 1), max 8 concurrent, 256 blocks of 16, prefill chunk 64.
 * bf16: free-running greedy decoding in bf16 flips on near-ties (the
   reference's own bf16 run leaves its fp32 run within 0-88 tokens), so bf16 is
   held to the reference's fp32 logits teacher-forced along the fp32 token
-  stream: logits at the reference's top-16 ids within 2e-2 of the largest, and
-  every greedy pick a near-tie of the reference's best.  fp32 is held to 1e-3
-  and the same pick on the same test.
+  stream: logits at the reference's top-16 ids within the reference bf16
+  model's own error envelope (2.19e-2 of the largest, + 2**-8), on average
+  within twice its mean error, and every greedy pick a near-tie of the
+  reference's best.  fp32 is held to 1e-3 and the same pick on the same test.
 """
 
 from pathlib import Path
@@ -52,15 +53,17 @@ def weights():
     return random_weights()
 
 
-def run_engine(weights, dtype):
+def run_engine(weights, dtype, step_graphs=True):
     prev = torch.backends.cuda.matmul.allow_tf32
     torch.backends.cuda.matmul.allow_tf32 = False
     try:
-        model = TorchModel(QWEN25_05B, weights, device=DEV, dtype=dtype)
+        model = TorchModel(QWEN25_05B, weights, device=DEV, dtype=dtype, step_graphs=step_graphs)
         backend = PagedBackend(model, NUM_BLOCKS, BLOCK_SIZE, PREFILL_CHUNK)
         requests = serve(backend, engine_workload(), MAX_CONCURRENT,
                          BlockBudget(NUM_BLOCKS, BLOCK_SIZE))
         assert backend.blocks_in_use == 0
+        if step_graphs:  # every step of this workload fits a step graph
+            assert model.stats["steps"] > 0 and len(model._graphs) > 0
         return [r.tokens for r in requests], requests
     finally:
         torch.backends.cuda.matmul.allow_tf32 = prev
@@ -72,8 +75,9 @@ def test_workload_matches_the_fixture(golden):
     assert [m for _, m in specs] == golden["max_tokens"]
 
 
-def test_fp32_greedy_tokens_match_the_reference(golden, weights):
-    tokens, requests = run_engine(weights, torch.float32)
+@pytest.mark.parametrize("step_graphs", [True, False], ids=["graphs", "eager"])
+def test_fp32_greedy_tokens_match_the_reference(golden, weights, step_graphs):
+    tokens, requests = run_engine(weights, torch.float32, step_graphs)
     assert not any(r.failed for r in requests)
     for i, (ours, ref) in enumerate(zip(tokens, golden["fp32"])):
         n = min(32, len(ref))
@@ -126,19 +130,26 @@ def teacher_forced(weights, dtype, golden):
 def test_teacher_forced_logits_against_the_reference_fp32(golden, weights, dtype, rel):
     """At every position: logits at the reference's top-16 ids within `rel` of
     the largest, and the greedy choice a near-tie (within 2 * rel) of the
-    reference's best (for fp32: the same token).  For bf16, `rel` at a position
-    is 2e-2 or, where the reference's own bf16 model is already further than
-    that from its fp32 logits (up to 2.19e-2 here), that distance plus 2**-8."""
+    reference's best (for fp32: the same token).
+
+    For bf16 the error at a position is rounding noise accumulated over 24
+    layers, and the reference's own bf16 model shows how large it gets on this
+    workload: up to 2.19e-2 of the largest logit.  So bf16 is held at every
+    position to max(2e-2, that envelope + 2**-8), and on average to at most
+    twice the reference bf16 model's mean error (a systematic error fails)."""
     logits, ids, values = teacher_forced(weights, dtype, golden)
     ref_bf16 = np.load(GOLDEN)["ref_bf16_logit_err"]
+    bound = rel if dtype == torch.float32 else max(rel, float(ref_bf16.max()) + 2.0 ** -8)
+    errors = np.zeros(ref_bf16.shape)
     for n, seq in enumerate(logits):
         for step in range(ids.shape[1]):
             ref_ids = torch.from_numpy(ids[n, step]).long()
             ref = torch.from_numpy(values[n, step])
-            bound = rel if dtype == torch.float32 else max(rel, ref_bf16[n, step] + 2.0 ** -8)
-            tol = bound * ref.abs().max().item()
+            scale = ref.abs().max().item()
+            tol = bound * scale
             ours = seq[step][ref_ids]
-            assert (ours - ref).abs().max().item() <= tol, (n, step)
+            errors[n, step] = (ours - ref).abs().max().item() / scale
+            assert errors[n, step] <= bound, (n, step, errors[n, step], bound)
             pick = int(seq[step].argmax())
             if dtype == torch.float32:
                 assert pick == int(ref_ids[0]), (n, step)
@@ -146,3 +157,7 @@ def test_teacher_forced_logits_against_the_reference_fp32(golden, weights, dtype
                 hit = (ref_ids == pick).nonzero()
                 assert hit.numel() == 1, (n, step, pick)
                 assert ref[hit[0, 0]].item() >= ref[0].item() - 2 * tol, (n, step)
+    print(f"{dtype}: relative logit error max {errors.max():.4f} mean {errors.mean():.4f}; "
+          f"reference bf16 model max {ref_bf16.max():.4f} mean {ref_bf16.mean():.4f}")
+    if dtype == torch.bfloat16:
+        assert errors.mean() <= 2 * ref_bf16.mean(), (errors.mean(), ref_bf16.mean())

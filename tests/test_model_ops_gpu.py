@@ -45,9 +45,10 @@ def norm_bound(out, ref, dtype):
 
 
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
-def test_rms_norm_with_residual_add_in_place(dtype):
+@pytest.mark.parametrize("hidden", [896, 100], ids=["vector", "scalar"])
+def test_rms_norm_with_residual_add_in_place(dtype, hidden):
     g = torch.Generator(device=DEV).manual_seed(0)
-    T, hidden = 37, 896
+    T = 37
     x = torch.randn(T, hidden, generator=g, device=DEV).to(dtype)
     add = torch.randn(T, hidden, generator=g, device=DEV).to(dtype) * 3
     w = (1 + 0.1 * torch.randn(hidden, generator=g, device=DEV)).to(dtype)
@@ -150,9 +151,10 @@ def test_rope_append_reports_bad_positions_and_slots():
 
 
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
-def test_silu_mul_matches_the_torch_ops(dtype):
+@pytest.mark.parametrize("inter", [4864, 37], ids=["vector", "scalar"])
+def test_silu_mul_matches_the_torch_ops(dtype, inter):
     g = torch.Generator(device=DEV).manual_seed(3)
-    T, inter = 53, 4864
+    T = 53
     gate_up = (torch.randn(T, 2 * inter, generator=g, device=DEV) * 4).to(dtype)
     gate, up = gate_up.split(inter, dim=-1)
     ref = F.silu(gate) * up
