@@ -217,7 +217,7 @@ __global__ void __launch_bounds__(256)
 // replaces the metadata + slot-write pair for decode steps and lets the next
 // kernel launch at once.
 template <typename Tin, typename Tpool, bool VEC>
-__global__ void __launch_bounds__(256)
+__global__ void __launch_bounds__(64)
     decode_append_kernel(const int32_t* __restrict__ seq_rows, const int32_t* __restrict__ start_pos,
                          int32_t R, const int32_t* __restrict__ block_tables, int64_t bt_stride,
                          int32_t bt_rows, int32_t max_blocks, int32_t block_size,
@@ -279,7 +279,9 @@ int launch_decode_append_t(const int32_t* seq_rows, const int32_t* start_pos, in
                            void* vp, int64_t pool_slots, bool vec, int32_t* ctx, int32_t* slots,
                            uint32_t* status, cudaStream_t stream) {
   if (R == 0) return 0;
-  cudaLaunchConfig_t cfg = pdl_config((R + 7) / 8, 256, stream);
+  // Two rows (warps) per CTA: small CTAs fit beside the decode CTAs that launch
+  // behind this kernel, so none of those waits for a slot.
+  cudaLaunchConfig_t cfg = pdl_config((R + 1) / 2, 64, stream);
   cudaLaunchAttribute attr[1];
   pdl_attr(cfg, attr);
   auto kernel = vec ? decode_append_kernel<Tin, Tpool, true> : decode_append_kernel<Tin, Tpool, false>;

@@ -77,16 +77,34 @@ __device__ __forceinline__ uint64_t global_timer_ns() {
   return t;
 }
 
+// try_wait with a suspend-time hint: a thread whose phase is not complete
+// sleeps until it completes (or `ns` nanoseconds pass) instead of polling, so
+// waiting warps leave the issue slots and the shared-memory pipe to the warps
+// that compute.
+__device__ __forceinline__ bool mbar_try_wait_suspend(uint64_t* bar, uint32_t parity,
+                                                      uint32_t ns) {
+  uint32_t done;
+  asm volatile(
+      "{\n .reg .pred p;\n"
+      " mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n"
+      " selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(done)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(ns)
+      : "memory");
+  return done != 0;
+}
+
 // Bounded wait: true when the phase with `parity` completed, false once about
 // kWaitLimitNs of wall time (or kSpinLimit polls) went by without it.
 constexpr uint64_t kWaitLimitNs = 2000000000ull;
+constexpr uint32_t kSuspendNs = 20000;
 
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t start = global_timer_ns();
   for (uint32_t i = 1; i < kSpinLimit; ++i) {
-    if (mbar_try_wait(bar, parity)) return true;
-    if ((i & 255u) == 0 && global_timer_ns() - start > kWaitLimitNs) return false;
+    if (mbar_try_wait_suspend(bar, parity, kSuspendNs)) return true;
+    if (global_timer_ns() - start > kWaitLimitNs) return false;
   }
   return false;
 }

@@ -80,11 +80,13 @@ __device__ __forceinline__ int32_t units_of(const DecodeArgs& a, int32_t raw_len
   return (len + a.block_size - 1) / a.block_size;
 }
 
-// Units of sequence i after validation; also returns the clamped length.
-__device__ __forceinline__ int32_t seq_units(const DecodeArgs& a, int32_t i, int32_t& len,
-                                             int32_t& row, bool report) {
-  len = __ldg(a.context_lens + i);
-  row = a.seq_rows != nullptr ? __ldg(a.seq_rows + i) : i;
+// Units of a sequence with raw length `raw_len` and table row `raw_row` after
+// validation; also returns the clamped length.
+__device__ __forceinline__ int32_t seq_units_raw(const DecodeArgs& a, int32_t raw_len,
+                                                 int32_t raw_row, int32_t& len, int32_t& row,
+                                                 bool report) {
+  len = raw_len;
+  row = raw_row;
   if (len == 0) return 0;  // padding row: nothing read, its output row left as is
   if (row < 0 || row >= a.bt_rows) {
     if (report) set_status(a.status, kStatusBadRow);
@@ -98,6 +100,13 @@ __device__ __forceinline__ int32_t seq_units(const DecodeArgs& a, int32_t i, int
     return 0;
   }
   return (len + a.block_size - 1) / a.block_size;
+}
+
+// Units of sequence i after validation; also returns the clamped length.
+__device__ __forceinline__ int32_t seq_units(const DecodeArgs& a, int32_t i, int32_t& len,
+                                             int32_t& row, bool report) {
+  return seq_units_raw(a, __ldg(a.context_lens + i),
+                       a.seq_rows != nullptr ? __ldg(a.seq_rows + i) : i, len, row, report);
 }
 
 struct Span {
@@ -312,6 +321,8 @@ __device__ void emit_portion(const DecodeArgs& a, const Span& sp, const Portion&
 struct WarpStarts {
   int32_t seq[8];
   int64_t prefix[8];
+  // Raw length and table row of each warp's first sequence and of the one after.
+  int32_t len[8], row[8], nlen[8], nrow[8];
 };
 
 // Like compute_span, then splits the CTA span into NW contiguous warp spans and
@@ -361,6 +372,97 @@ __device__ __forceinline__ Span compute_warp_spans(const DecodeArgs& a, ScanSmem
     const int64_t last_target = sp.r0 + (sp.r1 - sp.r0) * (NW - 1) / NW;
     if (carry * Hkv > last_target) break;
   }
+  if (tid < NW && ws.seq[tid] >= 0) {
+    const int32_t i = ws.seq[tid];
+    ws.len[tid] = __ldg(a.context_lens + i);
+    ws.row[tid] = a.seq_rows != nullptr ? __ldg(a.seq_rows + i) : i;
+    ws.nlen[tid] = i + 1 < B ? __ldg(a.context_lens + i + 1) : 0;
+    ws.nrow[tid] = i + 1 < B ? (a.seq_rows != nullptr ? __ldg(a.seq_rows + i + 1) : i + 1) : 0;
+  }
+  __syncthreads();
+  sp.seq = ws.seq[0];
+  sp.prefix = ws.prefix[0];
+  if (sp.seq < 0) sp.r1 = sp.r0;  // cannot happen when r0 < W; never walk from nowhere
+  return sp;
+}
+
+// compute_warp_spans with one round of global loads: the raw lengths and table
+// rows of all `B` sequences are staged in `scratch` (2 * B int32 of shared
+// memory that nothing else uses until this returns), and both passes (total,
+// then the scan for the warp starts) run from there.  All threads call it.
+template <int NW>
+__device__ __forceinline__ Span compute_warp_spans_smem(const DecodeArgs& a, ScanSmem& sm,
+                                                        WarpStarts& ws, int32_t* scratch) {
+  static_assert(NW <= 8, "at most 8 warp spans");
+  const int tid = threadIdx.x, nthr = blockDim.x, lane = tid & 31, warp = tid >> 5;
+  const int nwarps = (nthr + 31) >> 5;
+  const int64_t C = gridDim.x, c = blockIdx.x;
+  const int32_t B = a.num_seqs;
+  const int64_t Hkv = a.num_kv_heads;
+  int32_t* lens = scratch;
+  int32_t* rows = scratch + B;
+  int64_t local = 0;
+  for (int32_t i = tid; i < B; i += nthr) {
+    const int32_t len = __ldg(a.context_lens + i);
+    const int32_t row = a.seq_rows != nullptr ? __ldg(a.seq_rows + i) : i;
+    lens[i] = len;
+    rows[i] = row;
+    int32_t l2, r2;
+    local += seq_units_raw(a, len, row, l2, r2, c == 0);  // CTA 0 reports bad input once
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) local += __shfl_xor_sync(0xffffffffu, local, o);
+  if (lane == 0) sm.warp_tot[warp] = local;
+  if (tid < NW) ws.seq[tid] = -1;
+  __syncthreads();
+  int64_t total = 0;
+  for (int w = 0; w < nwarps; ++w) total += sm.warp_tot[w];
+  Span sp;
+  sp.W = total * Hkv;
+  sp.q = sp.W / C;
+  sp.rem = sp.W % C;
+  sp.r0 = span_begin(c, sp.q, sp.rem);
+  sp.r1 = sp.r0 + sp.q + (c < sp.rem ? 1 : 0);
+  sp.seq = -1;
+  sp.prefix = 0;
+  __syncthreads();  // warp_tot reuse below
+  if (sp.r0 >= sp.r1) return sp;
+  const int64_t last_target = sp.r0 + (sp.r1 - sp.r0) * (NW - 1) / NW;
+  int64_t carry = 0;
+  for (int32_t base = 0; base < B; base += nthr) {
+    const int32_t i = base + tid;
+    int64_t nb = 0;
+    if (i < B) {
+      int32_t len, row;
+      nb = seq_units_raw(a, lens[i], rows[i], len, row, false);
+    }
+    const int64_t incl = warp_inclusive_scan(nb);
+    if (lane == 31) sm.warp_tot[warp] = incl;
+    __syncthreads();
+    int64_t before = carry, chunk_total = 0;
+    for (int w = 0; w < nwarps; ++w) {
+      if (w < warp) before += sm.warp_tot[w];
+      chunk_total += sm.warp_tot[w];
+    }
+    const int64_t excl = before + incl - nb;
+    if (nb > 0) {
+#pragma unroll
+      for (int k = 0; k < NW; ++k) {
+        const int64_t target = sp.r0 + (sp.r1 - sp.r0) * k / NW;
+        if (excl * Hkv <= target && target < (excl + nb) * Hkv) {
+          ws.seq[k] = i;
+          ws.prefix[k] = excl;
+          ws.len[k] = lens[i];
+          ws.row[k] = rows[i];
+          ws.nlen[k] = i + 1 < B ? lens[i + 1] : 0;
+          ws.nrow[k] = i + 1 < B ? rows[i + 1] : 0;
+        }
+      }
+    }
+    carry += chunk_total;
+    __syncthreads();  // warp_tot reuse; the starts are visible after the last one
+    if (carry * Hkv > last_target) break;
+  }
   sp.seq = ws.seq[0];
   sp.prefix = ws.prefix[0];
   if (sp.seq < 0) sp.r1 = sp.r0;  // cannot happen when r0 < W; never walk from nowhere
@@ -380,6 +482,26 @@ __device__ __forceinline__ void warp_store_record(const DecodeArgs& a, const Spa
   for (int r = lane; r < G; r += 32) {
     rec[G * D + r] = m[r];
     rec[G * D + G + r] = l[r];
+  }
+}
+
+// warp_store_record for at most ROWS rows of DIM elements (compile-time bounds,
+// so the copies issue back to back).
+template <int ROWS, int DIM>
+__device__ __forceinline__ void warp_store_record_fixed(const DecodeArgs& a, const Span& sp,
+                                                        int64_t seg_unit, const float* o,
+                                                        const float* m, const float* l,
+                                                        int lane) {
+  const int G = a.groups;
+  float* rec = a.partials + record_index(blockIdx.x, seg_unit, sp.q, sp.rem) * a.rec_stride;
+#pragma unroll
+  for (int j = 0; j < ROWS * DIM / 32; ++j) {
+    const int e = lane + 32 * j;
+    if (e < G * DIM) rec[e] = o[e];
+  }
+  if (lane < G) {
+    rec[G * DIM + lane] = m[lane];
+    rec[G * DIM + G + lane] = l[lane];
   }
 }
 
@@ -418,10 +540,24 @@ __device__ void cta_merge_records(const DecodeArgs& a, const Span& sp, int32_t s
   float* wl = scratch + n * G;  // [n][G]: record sums
   float* rowM = wl + n * G;     // [G]
   float* rowInvL = rowM + G;    // [G]
+  auto record = [&](int c) {
+    return a.partials + record_index(c_first + c, seg_unit, sp.q, sp.rem) * a.rec_stride;
+  };
+  // Up to kBatch records per round: their loads are independent and issue back
+  // to back.  The first round of each thread's first element group goes out
+  // with the maxima and sums below, so n <= kBatch costs one L2 round trip.
+  constexpr int kBatch = 8;
+  const int E4 = G * D / 4;
+  float4 v[kBatch];
+  if (tid < E4) {
+#pragma unroll
+    for (int u = 0; u < kBatch; ++u) {
+      if (u < n) v[u] = __ldcg(reinterpret_cast<const float4*>(record(u)) + tid);
+    }
+  }
   for (int idx = tid; idx < n * G; idx += nthr) {
     const int c = idx / G, r = idx - c * G;
-    const float* rr =
-        a.partials + record_index(c_first + c, seg_unit, sp.q, sp.rem) * a.rec_stride;
+    const float* rr = record(c);
     wm[idx] = __ldcg(rr + G * D + r);
     wl[idx] = __ldcg(rr + G * D + G + r);
   }
@@ -442,36 +578,26 @@ __device__ void cta_merge_records(const DecodeArgs& a, const Span& sp, int32_t s
   __syncthreads();
   OutT* out = static_cast<OutT*>(a.out) + static_cast<int64_t>(seq) * a.o_stride_seq +
               static_cast<int64_t>(kvh) * G * D;
-  for (int e4 = tid; e4 < G * D / 4; e4 += nthr) {
+  for (int e4 = tid; e4 < E4; e4 += nthr) {
     const int r = (e4 * 4) / D;
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-    int c = 0;
-    for (; c + 4 <= n; c += 4) {
-      float4 v[4];
+    for (int c0 = 0; c0 < n; c0 += kBatch) {
+      if (e4 != tid || c0 != 0) {  // else: prefetched above
 #pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const float* rr =
-            a.partials + record_index(c_first + c + u, seg_unit, sp.q, sp.rem) * a.rec_stride;
-        v[u] = __ldcg(reinterpret_cast<const float4*>(rr) + e4);
+        for (int u = 0; u < kBatch; ++u) {
+          if (c0 + u < n) v[u] = __ldcg(reinterpret_cast<const float4*>(record(c0 + u)) + e4);
+        }
       }
 #pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const float w = wm[(c + u) * G + r];
-        acc.x += w * v[u].x;
-        acc.y += w * v[u].y;
-        acc.z += w * v[u].z;
-        acc.w += w * v[u].w;
+      for (int u = 0; u < kBatch; ++u) {
+        if (c0 + u < n) {
+          const float w = wm[(c0 + u) * G + r];
+          acc.x += w * v[u].x;
+          acc.y += w * v[u].y;
+          acc.z += w * v[u].z;
+          acc.w += w * v[u].w;
+        }
       }
-    }
-    for (; c < n; ++c) {
-      const float* rr =
-          a.partials + record_index(c_first + c, seg_unit, sp.q, sp.rem) * a.rec_stride;
-      const float4 v = __ldcg(reinterpret_cast<const float4*>(rr) + e4);
-      const float w = wm[c * G + r];
-      acc.x += w * v.x;
-      acc.y += w * v.y;
-      acc.z += w * v.z;
-      acc.w += w * v.w;
     }
     const float inv = rowInvL[r];
     store_out<OutT>(out + 4 * e4 + 0, acc.x * inv);

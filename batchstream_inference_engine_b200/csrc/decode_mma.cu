@@ -44,7 +44,11 @@ template <int D, bool G16>
 struct Cfg {
   static constexpr int W = 4;                  // warps per CTA
   static constexpr int S = (D == 64) ? 3 : 2;  // stages per warp
-  static constexpr int MIN_CTAS = (D == 64) ? 3 : 2;  // resident CTAs per SM (register cap)
+  static constexpr int MIN_CTAS = (D == 64) ? 3 : 2;  // resident CTAs per SM
+  // Registers per thread: MIN_CTAS CTAs leave room on the SM for a small CTA of
+  // the kernel just ahead (it runs on during the programmatic launch), so no
+  // decode CTA waits for it to exit.
+  static constexpr int MAX_REGS = (D == 64) ? 160 : 232;
   static constexpr int HALVES = D / 64;
   static constexpr int GROWS = G16 ? 16 : 8;
   static constexpr int BLOCK_BYTES = kBS * D * 2;  // one block of one kv head
@@ -60,7 +64,7 @@ struct Cfg {
 };
 
 template <int D, bool G16>
-__global__ void __launch_bounds__(Cfg<D, G16>::W * 32, Cfg<D, G16>::MIN_CTAS)
+__global__ void __maxnreg__((Cfg<D, G16>::MAX_REGS))
     decode_mma_kernel(const __grid_constant__ CUtensorMap kmap,
                       const __grid_constant__ CUtensorMap vmap, const DecodeArgs a) {
   using C = Cfg<D, G16>;
@@ -105,7 +109,13 @@ __global__ void __launch_bounds__(Cfg<D, G16>::W * 32, Cfg<D, G16>::MIN_CTAS)
   // so do the first loads of blocks that kernel cannot have written.
   const bool early_loads = a.lens_ready && a.after_append;
   if (!a.lens_ready) pdl_wait();
-  const Span sp = compute_warp_spans<W>(a, scan, starts);  // syncs the inits
+  // The stages are free until the first copy: they hold the lengths and rows
+  // for the span scan when they fit (one round of global loads).
+  constexpr int kScratchInts = W * S * C::STAGE_BYTES / 4;
+  const Span sp =
+      2 * a.num_seqs <= kScratchInts
+          ? compute_warp_spans_smem<W>(a, scan, starts, reinterpret_cast<int32_t*>(smem))
+          : compute_warp_spans<W>(a, scan, starts);  // both sync the inits
   if (a.lens_ready && !early_loads) pdl_wait();  // query, pools from here on
   if (sp.r0 >= sp.r1) {
     if (a.tasks != nullptr && tid == 0) a.tasks[blockIdx.x].valid = 0;
@@ -130,14 +140,12 @@ __global__ void __launch_bounds__(Cfg<D, G16>::W * 32, Cfg<D, G16>::MIN_CTAS)
   int32_t win_row = -1, win0 = 0, win_val = 0;
   int64_t cu = wr0;
   if (ntiles > 0) {
-    cnb = seq_units(a, ci, clen, crow, false);
+    cnb = units_of(a, starts.len[warp], starts.row[warp], clen, crow);
     const int64_t rel = wr0 - cprefix * Hkv;
     ch = static_cast<int32_t>(rel / cnb);
     cb = static_cast<int32_t>(rel % cnb);
-    if (ci + 1 < a.num_seqs) {
-      nxt_len = __ldg(a.context_lens + ci + 1);
-      nxt_row = a.seq_rows != nullptr ? __ldg(a.seq_rows + ci + 1) : ci + 1;
-    }
+    nxt_len = starts.nlen[warp];
+    nxt_row = starts.nrow[warp];
   }
 
   auto issue = [&](int stage) {
@@ -450,12 +458,15 @@ __global__ void __launch_bounds__(Cfg<D, G16>::W * 32, Cfg<D, G16>::MIN_CTAS)
         mine[G * D + G + lane] = mine[G * D + G + lane] * fa + other[G * D + G + lane] * fb;
         mine[G * D + lane] = M;
       }
-      for (int j = 0; j < G * D / 32; ++j) {
+      // Compile-time bounds (rows padded to GROWS): the loads of all elements
+      // issue back to back instead of one dependent step at a time.
+#pragma unroll
+      for (int j = 0; j < C::GROWS * D / 32; ++j) {
         const int r = (32 * j) / D;
         const float a0 = __shfl_sync(0xffffffffu, fa, r);
         const float b0 = __shfl_sync(0xffffffffu, fb, r);
         const int e = lane + 32 * j;
-        mine[e] = mine[e] * a0 + other[e] * b0;
+        if (r < G) mine[e] = mine[e] * a0 + other[e] * b0;
       }
       __syncwarp();
       if (k2 == 1) break;  // the chain starts in that warp
@@ -466,13 +477,19 @@ __global__ void __launch_bounds__(Cfg<D, G16>::W * 32, Cfg<D, G16>::MIN_CTAS)
       __nv_bfloat16* out = static_cast<__nv_bfloat16*>(a.out) +
                            static_cast<int64_t>(seq) * a.o_stride_seq +
                            static_cast<int64_t>(kvh) * G * D;
-      for (int e = lane; e < G * D; e += 32) {
-        out[e] = __float2bfloat16_rn(mine[e] / mine[G * D + G + e / D]);
+      const float inv_l = lane < G ? 1.f / mine[G * D + G + lane] : 0.f;
+#pragma unroll
+      for (int j = 0; j < C::GROWS * D / 32; ++j) {
+        const int r = (32 * j) / D;
+        const float inv = __shfl_sync(0xffffffffu, inv_l, r);
+        const int e = lane + 32 * j;
+        if (r < G) out[e] = __float2bfloat16_rn(mine[e] * inv);
       }
     } else if (a.tasks != nullptr) {
       // Cut across CTAs: leave this CTA's record; the segment is merged after
       // the kernel, listed by the CTA that holds its last unit.
-      warp_store_record(a, sp, seg_unit, mine, mine + G * D, mine + G * D + G, lane);
+      warp_store_record_fixed<C::GROWS, D>(a, sp, seg_unit, mine, mine + G * D,
+                                           mine + G * D + G, lane);
       if (lane == 0 && seg_unit < sp.r0 && seg_unit + nb <= sp.r1) {
         task.seg_unit = seg_unit;
         task.q = sp.q;
@@ -534,7 +551,8 @@ int launch_one(const DecodeArgs& a, const CUtensorMap& kmap, const CUtensorMap& 
 
 // Merges, after the decode kernel, the cut segments its CTAs listed: one CTA
 // per decode CTA, all threads on the records of one segment.
-__global__ void __launch_bounds__(128) decode_merge_kernel(const DecodeArgs a) {
+// Three CTAs per SM: as many as the decode kernel's grid holds, all in one wave.
+__global__ void __launch_bounds__(128, 3) decode_merge_kernel(const DecodeArgs a) {
   extern __shared__ float merge_scratch[];
   pdl_wait();
   const MergeTask t = a.tasks[blockIdx.x];
