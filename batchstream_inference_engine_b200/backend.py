@@ -52,8 +52,17 @@ class QwenIds:
 class _Sequence:
     cache: PagedKVCache
     pending: deque
-    next_token: int | None = None
+    next_token: int | None = None  # the input of the next step, as an id or a token reference
     finished: bool = False
+    feeds: object = None  # the launched step whose output the reference in next_token names
+
+
+@dataclass
+class LaunchedStep:
+    """A step on the device: ``PagedBackend.finish`` turns it into outputs."""
+
+    ids: object  # PendingTokens
+    rows: list  # (seq_id, _Sequence, output row or None) per batch row
 
 
 class PagedBackend:
@@ -98,15 +107,50 @@ class PagedBackend:
         return seq_id
 
     def step(self) -> dict[int, StepOutput]:
+        launched = self.launch()
+        return self.finish(launched) if launched is not None else {}
+
+    def launch(self) -> LaunchedStep | None:
+        """Composes and launches one step without waiting for it (the batch of
+        ``step``).  A generating sequence whose last token has not reached the
+        host yet feeds it by reference from the device, so the next step can be
+        composed while this one runs; ``finish`` returns this step's outputs.
+        A sequence that ends on an end-of-generation token revealed only by
+        ``finish`` of the previous step still runs in this one: that row's
+        output is dropped (``finish`` skips finished sequences)."""
         batch = self._generating_inputs() + self._prefill_inputs()
         if not batch:
-            return {}
-        tokens = self._model.next_tokens([(toks, self._sequences[s].cache) for s, toks in batch])
-        outputs = {}
+            return None
+        pending = self._model.launch_tokens(
+            [(toks, self._sequences[s].cache) for s, toks in batch])
+        rows = []
         for row, (seq_id, _) in enumerate(batch):
             sequence = self._sequences[seq_id]
-            if not sequence.pending:
-                outputs[seq_id] = self._next_output(sequence, tokens[row])
+            if sequence.pending:
+                rows.append((seq_id, sequence, None))
+            else:
+                rows.append((seq_id, sequence, row))
+        launched = LaunchedStep(pending, rows)
+        for seq_id, sequence, row in rows:
+            if row is not None:
+                sequence.next_token = pending.ref(row)  # resolved on the device
+                sequence.feeds = launched
+        return launched
+
+    def finish(self, launched: LaunchedStep) -> dict[int, StepOutput]:
+        """Waits for a launched step: {seq_id: StepOutput} for every sequence
+        whose prompt was fully consumed and that had not finished before."""
+        tokens = launched.ids.result()
+        outputs = {}
+        for seq_id, sequence, row in launched.rows:
+            if row is None or sequence.finished:
+                continue
+            token = tokens[row]
+            if sequence.feeds is launched:
+                sequence.next_token = token  # not relaunched yet: feed the id itself
+                sequence.feeds = None
+            sequence.finished = self._vocab.is_end_of_generation(token)
+            outputs[seq_id] = StepOutput(token, sequence.finished)
         return outputs
 
     def release_sequence(self, seq_id: int) -> None:
@@ -131,8 +175,3 @@ class PagedBackend:
                 inputs.append((seq_id, [sequence.pending.popleft() for _ in range(take)]))
                 remaining -= take
         return inputs
-
-    def _next_output(self, sequence: _Sequence, token: int) -> StepOutput:
-        sequence.next_token = token
-        sequence.finished = self._vocab.is_end_of_generation(token)
-        return StepOutput(token, sequence.finished)

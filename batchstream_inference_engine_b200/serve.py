@@ -50,6 +50,8 @@ class Request:
     tokens: list[int] = field(default_factory=list)
     failed: bool = False
     done: bool = False
+    issued: int = 0  # tokens launched (pipelined loop)
+    retired: bool = False  # its sequence was released with its last tokens in flight
 
     @property
     def kv_tokens(self) -> int:
@@ -58,10 +60,20 @@ class Request:
 
 class OfflineScheduler:
     """One turn of the loop per ``step()``: admit, run one backend step, record
-    and complete.  ``idle`` once every request is done."""
+    and complete.  ``idle`` once every request is done.
 
-    def __init__(self, backend, specs, max_concurrent: int, budget: BlockBudget):
+    ``pipelined``: each turn launches the next step before it reads the
+    previous one, so the host composes step t + 1 while step t runs (the
+    backend feeds each generating sequence's last token by reference on the
+    device).  Same tokens as the plain loop: a request that reaches max_tokens
+    is not launched again, and the one extra row of a sequence that ended on an
+    end-of-generation token is dropped."""
+
+    def __init__(self, backend, specs, max_concurrent: int, budget: BlockBudget,
+                 pipelined: bool = False):
         self.backend = backend
+        self.pipelined = pipelined
+        self._inflight = None
         self.max_concurrent = max_concurrent
         self.budget = budget
         self.requests = [Request(list(p), int(m)) for p, m in specs]
@@ -73,13 +85,21 @@ class OfflineScheduler:
 
     @property
     def idle(self) -> bool:
-        return not self.waiting and not self.active
+        return not self.waiting and not self.active and self._inflight is None
 
     def _complete(self, seq_id: int, request: Request) -> None:
         del self.active[seq_id]
         self.budget.release(request.kv_tokens)
-        self.backend.release_sequence(seq_id)
+        if not request.retired:
+            self.backend.release_sequence(seq_id)
         request.done = True
+
+    def _fail_all(self) -> dict[int, int]:
+        self._inflight = None
+        for seq_id, request in list(self.active.items()):
+            request.failed = True
+            self._complete(seq_id, request)
+        return {}
 
     def step(self) -> dict[int, int]:
         """Returns {seq_id: token} of the step (empty when idle)."""
@@ -91,13 +111,12 @@ class OfflineScheduler:
             if self.waiting:
                 raise RuntimeError("the budget cannot admit the next request")
             return {}
+        if self.pipelined:
+            return self._step_pipelined()
         try:
             outputs = self.backend.step()
         except RuntimeError:
-            for seq_id, request in list(self.active.items()):
-                request.failed = True
-                self._complete(seq_id, request)
-            return {}
+            return self._fail_all()
         for seq_id, output in outputs.items():
             request = self.active[seq_id]
             request.tokens.append(output.token)
@@ -105,12 +124,42 @@ class OfflineScheduler:
                 self._complete(seq_id, request)
         return {seq_id: output.token for seq_id, output in outputs.items()}
 
+    def _step_pipelined(self) -> dict[int, int]:
+        try:
+            launched = self.backend.launch()
+            outputs = self.backend.finish(self._inflight) if self._inflight is not None else {}
+        except RuntimeError:
+            return self._fail_all()
+        self._inflight = launched
+        if launched is not None:
+            for seq_id, _, row in launched.rows:
+                request = self.active.get(seq_id)
+                if row is None or request is None or request.retired:
+                    continue
+                request.issued += 1
+                if request.issued >= request.max_tokens:
+                    # Its last token is in flight: no further rows.  The blocks
+                    # may be reused by later steps, which run after this one.
+                    self.backend.release_sequence(seq_id)
+                    request.retired = True
+        recorded = {}
+        for seq_id, output in outputs.items():
+            request = self.active.get(seq_id)
+            if request is None:
+                continue  # ended on an end-of-generation token one step earlier
+            request.tokens.append(output.token)
+            recorded[seq_id] = output.token
+            if output.finished or len(request.tokens) >= request.max_tokens:
+                self._complete(seq_id, request)
+        return recorded
 
-def serve(backend, specs, max_concurrent: int, budget: BlockBudget, on_step=None) -> list[Request]:
+
+def serve(backend, specs, max_concurrent: int, budget: BlockBudget, on_step=None,
+          pipelined: bool = False) -> list[Request]:
     """Runs every (prompt_tokens, max_tokens) in ``specs`` to completion and
     returns the requests in submission order.  ``on_step(tokens)`` is called
     after each backend step with its {seq_id: token}."""
-    scheduler = OfflineScheduler(backend, specs, max_concurrent, budget)
+    scheduler = OfflineScheduler(backend, specs, max_concurrent, budget, pipelined=pipelined)
     while not scheduler.idle:
         tokens = scheduler.step()
         if on_step is not None:

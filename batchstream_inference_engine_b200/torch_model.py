@@ -162,6 +162,11 @@ class PagedKVPool:
         self.allocator = BlockAllocator(num_blocks, block_size, max_seqs=max_seqs,
                                         max_blocks_per_seq=max_blocks_per_seq or num_blocks,
                                         device=self.device)
+        # Greedy token ids of the last step run on this pool, in that step's row
+        # layout: a step may take a row's input token from here (a token
+        # reference) before the host has read it.  Rows: every live sequence,
+        # plus the padding of a graph-captured step.
+        self.last_ids = torch.zeros(max_seqs + 64, dtype=torch.int32, device=self.device)
 
     @property
     def free_blocks(self) -> int:
@@ -192,6 +197,34 @@ class PagedKVCache:
 
     def advance(self, count: int) -> None:
         self.length += count
+
+
+class PendingTokens:
+    """The greedy token ids of a launched step: ``result()`` waits for the step
+    and returns one id per group; ``ref(i)`` is the token reference (a negative
+    input token) through which the next step can take group i's id on the
+    device before the host has it."""
+
+    def __init__(self, model: "TorchModel", host: torch.Tensor, status: torch.Tensor, event,
+                 index: list[int]):
+        self._model = model
+        self._host = host
+        self._status = status  # the status words of the step's workspaces, copied after it
+        self._event = event
+        self._index = index
+        self._values = None
+
+    def ref(self, i: int) -> int:
+        return -1 - self._index[i]
+
+    def result(self) -> list[int]:
+        if self._values is None:
+            self._event.synchronize()
+            if bool(self._status.any()):
+                self._model._raise_status()
+            vals = self._host.tolist()
+            self._values = [vals[j] for j in self._index]
+        return self._values
 
 
 class TorchModel:
@@ -259,6 +292,8 @@ class TorchModel:
         self._graph_stream = None
         self._graph_pool = None
         self._graph_ws = None
+        self._hosts = None  # pinned buffers for pending token ids
+        self._host_turn = 0
 
     @classmethod
     def load(cls, model_dir: Path, device="cuda", dtype=torch.bfloat16) -> "TorchModel":
@@ -282,17 +317,54 @@ class TorchModel:
         model-dtype logits is the reference's argmax of logits.float()),
         reduced on the device.  Steps within the graph limits replay a
         captured step graph."""
+        return self.launch_tokens(groups).result()
+
+    @torch.inference_mode()
+    def launch_tokens(self, groups: list[tuple[list[int], PagedKVCache]]) -> PendingTokens:
+        """``next_tokens`` without waiting: launches the step and returns its
+        pending ids.  An input token t < 0 of a group is a token reference: the
+        id of row -1 - t of the last step launched on this pool (see
+        ``PendingTokens.ref``)."""
         key = self._graph_key([len(tokens) for tokens, _ in groups]) if self.step_graphs else None
         if key is not None:
             return self._graph_step(groups, key)
+        pool = groups[0][1]._pool
         logits = self.forward_batch(groups)
         ids = logits.argmax(dim=-1).to(torch.int32)
-        host = torch.empty(ids.shape, dtype=torch.int32, pin_memory=True)
+        pool.last_ids[: ids.numel()].copy_(ids)
+        return self._pending(ids, list(range(len(groups))))
+
+    def _pending(self, ids: torch.Tensor, index: list[int]) -> PendingTokens:
+        """Copies `ids` to one of a few pinned buffers and records the event the
+        host waits on; at most len(self._hosts) - 1 steps may be pending."""
+        n = ids.numel()
+        if self._hosts is None or self._hosts[0].numel() < n + 2:
+            self._hosts = [torch.empty(max(n + 2, 1024), dtype=torch.int32, pin_memory=True)
+                           for _ in range(3)]
+        buf = self._hosts[self._host_turn]
+        self._host_turn = (self._host_turn + 1) % len(self._hosts)
+        host, status = buf[:n], buf[n: n + 2]
         host.copy_(ids, non_blocking=True)
-        self.stats["d2h_bytes"] += 4 * ids.numel()
-        torch.cuda.current_stream(self.device).synchronize()
+        # Kernels report bad input in the status word of their stream's
+        # workspace (eager calls: this stream; graph replays: the capture
+        # stream's): copied after the step, read with the ids.
+        status[0].copy_(ops.workspace_for(self.device, 0)[:4].view(torch.int32)[0],
+                        non_blocking=True)
+        if self._graph_ws is not None:
+            status[1].copy_(self._graph_ws[:4].view(torch.int32)[0], non_blocking=True)
+        else:
+            status[1].fill_(0)
+        self.stats["d2h_bytes"] += 4 * n
+        event = torch.cuda.Event()
+        event.record(torch.cuda.current_stream(self.device))
+        return PendingTokens(self, host, status, event, index)
+
+    def _raise_status(self) -> None:
+        """Takes (and clears) both status words, raising for the set bits."""
         ops.take_status(self.device)
-        return host.tolist()
+        if self._graph_stream is not None:
+            with torch.cuda.stream(self._graph_stream):
+                ops.take_status(self.device)
 
     # ---------------------------------------------------------------- step
 
@@ -366,7 +438,7 @@ class TorchModel:
                                       max_query_len=max_chunk, seq_rows=rows_d[n_dec:],
                                       out=attended[n_dec:])
 
-        last = self._layers(pool, tokens_d, positions, slots, ends_d, attend)
+        last = self._layers(pool, self._resolve(pool, tokens_d), positions, slots, ends_d, attend)
         for (tokens, cache) in groups:
             cache.advance(len(tokens))
         st = self.stats
@@ -377,6 +449,13 @@ class TorchModel:
             n * s + n * (n + 1) // 2 for s, n in zip(starts, lengths))
         st["launches"] += ops.kernel_launches() - launches
         return last
+
+    @staticmethod
+    def _resolve(pool: PagedKVPool, tokens: torch.Tensor) -> torch.Tensor:
+        """Token references (t < 0: row -1 - t of the pool's last ids) replaced by
+        their ids, on the device."""
+        src = (-1 - tokens).clamp_(min=0).long()
+        return torch.where(tokens < 0, pool.last_ids.index_select(0, src), tokens)
 
     def _layers(self, pool: PagedKVPool, tokens, positions, slots, last_rows, attend):
         """The decoder stack over T tokens (torch_model.py:233-248, 250-287) with
@@ -466,8 +545,10 @@ class TorchModel:
                 ops.prefill_attention(q[B:], kp, vp, alloc.device_tables, pre_cu, ctx[B:], scale,
                                       max_query_len=Q, seq_rows=rows[B:], out=attended[B:])
 
-        last = self._layers(pool, tokens, positions, slots, ends, attend)
-        return F.linear(last, self.embed).argmax(dim=-1).to(torch.int32)
+        last = self._layers(pool, self._resolve(pool, tokens), positions, slots, ends, attend)
+        ids = F.linear(last, self.embed).argmax(dim=-1).to(torch.int32)
+        pool.last_ids[:R].copy_(ids)
+        return ids
 
     @staticmethod
     def _graph_inputs(key, rows, starts, lengths, n_dec, tokens) -> list[int]:
@@ -516,7 +597,11 @@ class TorchModel:
             # read from or written to the pool.
             inputs = torch.tensor([0] * R + [-1] * R + [1] * B + [0] * P + [0] * B + [0] * R
                                   + [0] * (B + Q), dtype=torch.int32, device=self.device)
+            # The warm-up run writes its (padding) ids over the pool's last ids,
+            # which the step about to replay may still read by reference.
+            saved = pool.last_ids.clone()
             self._graph_forward(pool, key, inputs)
+            pool.last_ids.copy_(saved)
             stream.synchronize()
             graph = torch.cuda.CUDAGraph()
             before = ops.kernel_launches()
@@ -531,7 +616,7 @@ class TorchModel:
         self._graphs[(id(pool),) + key] = entry
         return entry
 
-    def _graph_step(self, groups, key) -> list[int]:
+    def _graph_step(self, groups, key) -> PendingTokens:
         config = self.config
         pool = groups[0][1]._pool
         entry = self._graphs.get((id(pool),) + key)
@@ -555,12 +640,6 @@ class TorchModel:
         inputs.copy_(self._stage(values))
         graph.replay()
         B = key[0]
-        host = torch.empty(ids.numel(), dtype=torch.int32, pin_memory=True)
-        host.copy_(ids, non_blocking=True)
-        torch.cuda.current_stream(self.device).synchronize()
-        with torch.cuda.stream(self._graph_stream):
-            ops.take_status(self.device)  # the graphs' kernels report here
-        ops.take_status(self.device)
         for tokens, cache in groups:
             cache.advance(len(tokens))
         st = self.stats
@@ -570,9 +649,8 @@ class TorchModel:
         st["attn_flops"] += config.num_layers * 4 * config.num_heads * config.head_dim * sum(
             n * s + n * (n + 1) // 2 for s, n in zip(starts, lengths))
         st["launches"] += graph_launches
-        st["d2h_bytes"] += 4 * ids.numel()
-        out = host.tolist()
-        return out[:n_dec] + out[B: B + len(groups) - n_dec]
+        index = list(range(n_dec)) + list(range(B, B + len(groups) - n_dec))
+        return self._pending(ids, index)
 
 
 __all__ = ["ModelConfig", "PagedKVPool", "PagedKVCache", "TorchModel", "QWEN25_05B",

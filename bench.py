@@ -880,8 +880,9 @@ def run_engine(args):
     model = TorchModel(QWEN25_05B, random_weights(), device=dev, dtype=torch.bfloat16)
     blocks = ENGINE_CONCURRENT * -(-(ENGINE_PROMPT[1] + ENGINE_MAX_TOKENS[1]) // BLOCK)
     backend = PagedBackend(model, blocks, BLOCK, ENGINE_PREFILL, max_seqs=ENGINE_CONCURRENT)
+    # Pipelined: the host composes step t + 1 while step t runs.
     sched = OfflineScheduler(backend, engine_specs(world, rank), ENGINE_CONCURRENT,
-                             BlockBudget(blocks, BLOCK))
+                             BlockBudget(blocks, BLOCK), pipelined=True)
     gather = TokenGather(ENGINE_CONCURRENT, dev)
 
     def tokens_in(result):

@@ -130,6 +130,24 @@ class ReferenceModelStep:
     def next_tokens(self, groups) -> list[int]:
         return self.forward_batch(groups).float().argmax(dim=-1).tolist()
 
+    def launch_tokens(self, groups) -> "_Done":
+        """The backend's launch interface, computed at once (the CPU backend
+        runs the plain loop: every input token is an id, never a reference)."""
+        if any(t < 0 for tokens, _ in groups for t in tokens):
+            raise ValueError("the reference model step takes token ids only")
+        return _Done(self.next_tokens(groups))
+
+
+class _Done:
+    def __init__(self, values: list[int]):
+        self._values = values
+
+    def ref(self, i: int) -> int:
+        return -1 - i
+
+    def result(self) -> list[int]:
+        return self._values
+
 
 def cpu_backend(weights, dtype, config, num_blocks: int, block_size: int, prefill_chunk: int,
                 max_seqs: int = 256):

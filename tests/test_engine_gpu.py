@@ -53,14 +53,14 @@ def weights():
     return random_weights()
 
 
-def run_engine(weights, dtype, step_graphs=True):
+def run_engine(weights, dtype, step_graphs=True, pipelined=False):
     prev = torch.backends.cuda.matmul.allow_tf32
     torch.backends.cuda.matmul.allow_tf32 = False
     try:
         model = TorchModel(QWEN25_05B, weights, device=DEV, dtype=dtype, step_graphs=step_graphs)
         backend = PagedBackend(model, NUM_BLOCKS, BLOCK_SIZE, PREFILL_CHUNK)
         requests = serve(backend, engine_workload(), MAX_CONCURRENT,
-                         BlockBudget(NUM_BLOCKS, BLOCK_SIZE))
+                         BlockBudget(NUM_BLOCKS, BLOCK_SIZE), pipelined=pipelined)
         assert backend.blocks_in_use == 0
         if step_graphs:  # every step of this workload fits a step graph
             assert model.stats["steps"] > 0 and len(model._graphs) > 0
@@ -75,9 +75,10 @@ def test_workload_matches_the_fixture(golden):
     assert [m for _, m in specs] == golden["max_tokens"]
 
 
-@pytest.mark.parametrize("step_graphs", [True, False], ids=["graphs", "eager"])
-def test_fp32_greedy_tokens_match_the_reference(golden, weights, step_graphs):
-    tokens, requests = run_engine(weights, torch.float32, step_graphs)
+@pytest.mark.parametrize("step_graphs,pipelined", [(True, True), (True, False), (False, False)],
+                         ids=["graphs-pipelined", "graphs", "eager"])
+def test_fp32_greedy_tokens_match_the_reference(golden, weights, step_graphs, pipelined):
+    tokens, requests = run_engine(weights, torch.float32, step_graphs, pipelined)
     assert not any(r.failed for r in requests)
     for i, (ours, ref) in enumerate(zip(tokens, golden["fp32"])):
         n = min(32, len(ref))
@@ -93,7 +94,7 @@ def first_divergence(a, b):
 
 
 def test_bf16_engine_runs_the_workload_to_completion(golden, weights):
-    tokens, requests = run_engine(weights, torch.bfloat16)
+    tokens, requests = run_engine(weights, torch.bfloat16, pipelined=True)
     assert not any(r.failed for r in requests)
     # Every sequence runs to its own max_tokens, as in the reference's bf16 run.
     assert [len(t) for t in tokens] == [len(t) for t in golden["bf16"]]

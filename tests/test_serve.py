@@ -24,15 +24,32 @@ class FakeModel:
         self.max_position = 4096
         self.steps = []
         self.eog_at = eog_at or {}
+        self.last = []  # ids of the last step, by row (what token references name)
 
     def next_tokens(self, groups):
-        self.steps.append([(cache.seq_id, list(tokens)) for tokens, cache in groups])
+        return self.launch_tokens(groups).result()
+
+    def launch_tokens(self, groups):
+        resolved = [[self.last[-1 - t] if t < 0 else t for t in tokens] for tokens, _ in groups]
+        self.steps.append([(cache.seq_id, toks) for toks, (_, cache) in zip(resolved, groups)])
         out = []
         for tokens, cache in groups:
             cache.reserve(len(tokens))
             cache.advance(len(tokens))
             out.append(self.eog_at.get((cache.seq_id, cache.length), 1000 + cache.length))
-        return out
+        self.last = out
+        return FakePending(out)
+
+
+class FakePending:
+    def __init__(self, values):
+        self.values = values
+
+    def ref(self, i):
+        return -1 - i
+
+    def result(self):
+        return self.values
 
 
 def make_backend(model=None, num_blocks=64, prefill_chunk=8):
@@ -103,13 +120,49 @@ def test_serve_holds_the_head_until_the_budget_fits():
     assert all(len(step) == 1 for step in model.steps)
 
 
-def test_serve_fails_every_active_request_on_a_step_error():
-    class Broken(FakeModel):
-        def next_tokens(self, groups):
-            raise RuntimeError("device-side status")
+@pytest.mark.parametrize("num_blocks", [64, 6])
+def test_pipelined_loop_gives_the_same_tokens(num_blocks):
+    # Ends by end-of-generation tokens and by max_tokens, admissions gated by
+    # the concurrency limit and (with 6 blocks) by the budget.
+    specs = [([1] * 5, 6), ([2] * 20, 3), ([3] * 2, 8), ([4] * 9, 5), ([5] * 3, 7), ([6], 4)]
+    eog = {(0, 8): 151645, (2, 4): 151643, (4, 5): 151645}
+    runs = []
+    for pipelined in (False, True):
+        model = FakeModel(eog_at=eog)
+        b = make_backend(model, num_blocks=num_blocks, prefill_chunk=8)
+        requests = serve(b, specs, max_concurrent=3, budget=BlockBudget(num_blocks, 16),
+                         pipelined=pipelined)
+        assert all(r.done and not r.failed for r in requests)
+        assert b.blocks_in_use == 0
+        runs.append([r.tokens for r in requests])
+    assert runs[0] == runs[1]
+    assert runs[0][0][-1] == 151645 and len(runs[0][0]) < 6  # stopped early
+    assert [len(t) for t in runs[0]][1] == 3  # stopped at max_tokens
 
-    b = make_backend(Broken())
-    requests = serve(b, [([1, 2], 4), ([3], 4)], max_concurrent=8, budget=BlockBudget(64, 16))
+
+class BrokenAtLaunch(FakeModel):
+    def launch_tokens(self, groups):
+        raise RuntimeError("launch failed")
+
+
+class BrokenAtResult(FakeModel):
+    """Fails when a step's ids are read (a device-side status bit)."""
+
+    def launch_tokens(self, groups):
+        pending = super().launch_tokens(groups)
+
+        def result():
+            raise RuntimeError("device-side status")
+        pending.result = result
+        return pending
+
+
+@pytest.mark.parametrize("model", [BrokenAtLaunch, BrokenAtResult])
+@pytest.mark.parametrize("pipelined", [False, True])
+def test_serve_fails_every_active_request_on_a_step_error(model, pipelined):
+    b = make_backend(model())
+    requests = serve(b, [([1, 2], 4), ([3], 4)], max_concurrent=8, budget=BlockBudget(64, 16),
+                     pipelined=pipelined)
     assert all(r.failed and r.done for r in requests)
     assert b.blocks_in_use == 0
 
