@@ -70,7 +70,7 @@ _SIGNATURES = {
         ctypes.c_int,
     ),
     "bs_prefill_attention_workspace_bytes": (
-        [_i64, _i64, _i64, _i64, _i64, _i32, ctypes.POINTER(_u64)], ctypes.c_int,
+        [_i64, _i64, _i64, _i64, _i64, _i64, _i64, _i32, ctypes.POINTER(_u64)], ctypes.c_int,
     ),
     "bs_reshape_and_cache": (
         [_p, _p, _i64, _i64, _i32, _p, _i64, _p, _p, _i32, _i64, _i64, _i64, _i64, _p, _p],

@@ -7,6 +7,7 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <atomic>
 #include <cmath>
 #include <cstdarg>
@@ -170,6 +171,26 @@ WsLayout ws_layout(int64_t segments, int64_t staging_ints, int64_t grid, int64_t
   w.tasks = w.partials + round_up(2 * grid * rec_stride * 4, 256);
   w.total = w.tasks + round_up(grid * static_cast<int64_t>(sizeof(bsb::MergeTask)), 256);
   return w;
+}
+
+// Split-KV factor of the tensor-core prefill: up to one CTA per SM.  A second
+// CTA on an SM adds no throughput (measured: the SM's softmax and operand
+// traffic are the bound, not one CTA's chain of waits), so only batches with
+// fewer query tiles than SMs are split.
+int prefill_splits(int64_t items, int sms) {
+  if (items <= 0) return 1;
+  const int64_t want = (static_cast<int64_t>(sms) + items - 1) / items;
+  return static_cast<int>(std::min<int64_t>(std::max<int64_t>(want, 1), bsb::kMaxPrefillSplits));
+}
+
+// Workspace bytes of the prefill records (split > 1): they start where the
+// decode's scratch does, past the status word and the segment counters (which
+// stay zero between calls).
+int64_t prefill_split_offset() { return ws_layout(0, 0, 0, 0).staging; }
+int64_t prefill_split_bytes(int64_t items, int splits) {
+  if (splits <= 1) return 256;
+  return prefill_split_offset() +
+         items * splits * (bsb::kPrefillRecordO + bsb::kPrefillRecordML) * 4;
 }
 
 // ------------------------------------------------------------------ tensor maps
@@ -555,11 +576,12 @@ int bs_paged_attention_batched(const void* query, int64_t query_seq_stride, cons
                        reinterpret_cast<bsb::MergeTask*>(ws + w.tasks));
 }
 
-int bs_prefill_attention_workspace_bytes(int64_t num_tokens, int64_t num_heads,
+int bs_prefill_attention_workspace_bytes(int64_t num_tokens, int64_t num_rows,
+                                         int64_t max_query_len, int64_t num_heads,
                                          int64_t num_kv_heads, int64_t head_dim,
                                          int64_t block_size, int32_t dtype, uint64_t* bytes_out) {
   BS_CHECK(bytes_out != nullptr, "bytes_out is null");
-  BS_CHECK(num_tokens >= 0, "num_tokens must be non-negative");
+  BS_CHECK(num_tokens >= 0 && num_rows >= 0 && max_query_len >= 0, "counts must be non-negative");
   BS_CHECK(num_kv_heads > 0 && num_heads % num_kv_heads == 0, "heads must equal kv_heads * groups");
   const int64_t groups = num_heads / num_kv_heads;
   int grid = 0;
@@ -569,7 +591,13 @@ int bs_prefill_attention_workspace_bytes(int64_t num_tokens, int64_t num_heads,
   // The per-token path stages token lengths and rows, then runs the decode.
   const WsLayout w = ws_layout(num_tokens * num_kv_heads, 2 * num_tokens, grid,
                                record_stride(groups, head_dim));
-  *bytes_out = static_cast<uint64_t>(w.total);
+  int64_t need = w.total;
+  // The tensor-core path: split-KV records after the decode's counters.
+  DeviceInfo* d = nullptr;
+  if (int rc = current_device_info(&d)) return rc;
+  const int64_t items = num_rows * num_heads * ((max_query_len + 127) / 128);
+  need = std::max(need, prefill_split_bytes(items, prefill_splits(items, d->sms)));
+  *bytes_out = static_cast<uint64_t>(need);
   return BS_OK;
 }
 
@@ -649,11 +677,24 @@ int bs_prefill_attention(const void* query, int64_t query_token_stride, const in
       p.exact_scale = std::frexp(static_cast<double>(p.scale), &e) == 0.5 ? 1 : 0;
     }
     p.status = reinterpret_cast<uint32_t*>(ws);
-    const int64_t grid = num_rows * num_heads * p.qtiles;
+    const int64_t items = num_rows * num_heads * p.qtiles;
+    DeviceInfo* d = nullptr;
+    if ((rc = current_device_info(&d))) return rc;
+    p.splits = prefill_splits(items, d->sms);
+    if (static_cast<int64_t>(workspace_bytes) < prefill_split_bytes(items, p.splits)) p.splits = 1;
+    float* records = reinterpret_cast<float*>(ws + prefill_split_offset());
+    p.part_o = records;
+    p.part_ml = records + items * p.splits * bsb::kPrefillRecordO;
+    const int64_t grid = items * p.splits;
     if (grid > kInt32Max) return fail(BS_ERR_UNSUPPORTED, "too many query tiles");
     rc = bsb::launch_prefill_tc(p, qmap, kmap, vmap, static_cast<int>(grid), st);
     if (rc != 0) return cuda_fail(static_cast<cudaError_t>(rc), "prefill kernel launch");
     count_launches(1);
+    if (p.splits > 1) {
+      rc = bsb::launch_prefill_merge(p, static_cast<int>(items), st);
+      if (rc != 0) return cuda_fail(static_cast<cudaError_t>(rc), "prefill merge launch");
+      count_launches(1);
+    }
     return BS_OK;
   }
   // Per-token path: token i of a chunk is a decode query over its causal length.

@@ -152,15 +152,20 @@ __device__ __forceinline__ uint32_t swz128(int r, int c) {
   return r * 128 + ((((c >> 3) ^ (r & 7))) << 4) + (c & 7) * 2;
 }
 
-// Query tile index of CTA b: tiles with the most keys first (the last query
-// tile of every chunk, then the one before, ...), heads innermost.
-__device__ __forceinline__ void cta_work(const PrefillArgs& a, int b, int& r, int& h, int& t0) {
+// Work item (chunk r, head h, query tile at t0) of CTA b and its key range
+// split sp: tiles with the most keys first (the last query tile of every
+// chunk, then the one before, ...), heads inside, splits innermost.
+__device__ __forceinline__ int cta_work(const PrefillArgs& a, int b, int& r, int& h, int& t0,
+                                        int& sp) {
+  sp = b % a.splits;
+  const int item = b / a.splits;
   const int H = a.num_heads;
-  h = b % H;
-  const int item = b / H;                 // 0 .. num_rows * qtiles - 1
-  const int t = a.qtiles - 1 - item / a.num_rows;
-  r = item % a.num_rows;
+  h = item % H;
+  const int rt = item / H;  // 0 .. num_rows * qtiles - 1
+  const int t = a.qtiles - 1 - rt / a.num_rows;
+  r = rt % a.num_rows;
   t0 = t * kRows;
+  return item;
 }
 
 __global__ void __launch_bounds__(kThreads, 2)
@@ -187,8 +192,8 @@ __global__ void __launch_bounds__(kThreads, 2)
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   pdl_wait();
 
-  int r, h, t0;
-  cta_work(a, blockIdx.x, r, h, t0);
+  int r, h, t0, sp;
+  const int item = cta_work(a, blockIdx.x, r, h, t0, sp);
   const int tok0 = __ldg(a.cu_q + r);
   const int n = __ldg(a.cu_q + r + 1) - tok0;
   if (t0 == 0 && h == 0 && tid == 0 && n > a.qtiles * kRows) set_status(a.status, kStatusBadLength);
@@ -203,7 +208,12 @@ __global__ void __launch_bounds__(kThreads, 2)
     return;
   }
   const int kv_end = min(ctx, prior + t0 + kRows);  // keys the tile's last row can see
-  const int ntiles = (kv_end + kKeys - 1) / kKeys;
+  const int all_tiles = (kv_end + kKeys - 1) / kKeys;
+  // This CTA's key tiles [j_lo, j_lo + ntiles) of the query tile's range.
+  const int nsplit = prefill_tile_splits(all_tiles, a.splits);
+  if (sp >= nsplit) return;
+  const int j_lo = sp * all_tiles / nsplit;
+  const int ntiles = (sp + 1) * all_tiles / nsplit - j_lo;
   const int kvh = h / a.groups;
   const int32_t* table = a.block_tables + static_cast<int64_t>(row_tab) * a.bt_stride;
 
@@ -252,8 +262,8 @@ __global__ void __launch_bounds__(kThreads, 2)
       const int e = w * 32 + lane;
       return (e < a.max_blocks && e * 16 < kv_end) ? __ldg(table + e) : 0;
     };
-    int32_t win_cur = fetch(0), win_next = fetch(1);
-    int win = 0;
+    int win = (j_lo * 4) / 32;
+    int32_t win_cur = fetch(win), win_next = fetch(win + 1);
     if (lane == 0) {
       mbar_arrive_expect_tx(&q_full, kQBytes);
       tma_load_3d(sQ, &qmap, &q_full, 0, h, tok0 + t0);
@@ -290,12 +300,12 @@ __global__ void __launch_bounds__(kThreads, 2)
           ok = wait_all(&k_empty[st], ((i - kKStages) / kKStages) & 1);
           if (!ok) break;
         }
-        if ((i * 4) / 32 != win) {
+        if (((j_lo + i) * 4) / 32 != win) {
           win_cur = win_next;
           ++win;
           win_next = fetch(win + 1);
         }
-        const int32_t blk = block_of(i, win_cur);
+        const int32_t blk = block_of(j_lo + i, win_cur);
         load(&kmap, sK(st), &k_full[st], blk);
         k_loads = i + 1;
         if (i & 1) hold_odd = blk; else hold_even = blk;
@@ -411,7 +421,7 @@ __global__ void __launch_bounds__(kThreads, 2)
                               __uint_as_float(sp[i] & 0xFFFF0000u) * a.scale);
         }
       }
-      const int key0 = j * kKeys;
+      const int key0 = (j_lo + j) * kKeys;
       // Tiles wholly at or before the first row's position need no mask;
       // masked keys become bf16 -inf.
       if (key0 + kKeys - 1 > prior + t0) {
@@ -428,7 +438,9 @@ __global__ void __launch_bounds__(kThreads, 2)
       const uint32_t m2 = max_bf16x2(max_bf16x2(mp[0], mp[1]), max_bf16x2(mp[2], mp[3]));
       const float m_tile = fmaxf(__uint_as_float(m2 << 16), __uint_as_float(m2 & 0xFFFF0000u));
       const float m_tile_z = m_tile * zscale;
-      // Key 0 is visible to every row, so m_used is finite from tile 0 on.
+      // Key 0 is visible to every row, so m_used is finite from the first tile
+      // on when the range starts at key 0; a later range's first tiles may hide
+      // every key from some rows (m_used -inf until one shows, P 0 meanwhile).
       const bool grow = m_tile_z > m_used + kRescaleSlack;
       if (j == 0) {
         m_used = m_tile_z;
@@ -458,7 +470,8 @@ __global__ void __launch_bounds__(kThreads, 2)
       // Sums kept in 8 partials (key index mod 8), two per packed register.
       float2 ps[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f),
                       make_float2(0.f, 0.f)};
-      const float2 zs = make_float2(zscale, zscale), mm = make_float2(-m_used, -m_used);
+      const float m_base = m_used == -INFINITY ? 0.f : m_used;  // no -inf - -inf
+      const float2 zs = make_float2(zscale, zscale), mm = make_float2(-m_base, -m_base);
       uint8_t* prow = sP(j & 1);
 #pragma unroll
       for (int ch = 0; ch < kKeys / 8; ++ch) {
@@ -494,7 +507,25 @@ __global__ void __launch_bounds__(kThreads, 2)
       mbar_arrive(&p_full[j & 1]);
     }
     if (ok) ok = wait_all(&o_last, 0);
-    if (ok) {
+    if (ok && nsplit > 1) {
+      tc_fence_after();
+      // One record per CTA: unnormalised O, then (max, sum) of the row.
+      const int64_t rec = static_cast<int64_t>(item) * a.splits + sp;
+      float* orow = a.part_o + (rec * kRows + row) * kD;
+#pragma unroll
+      for (int c0 = 0; c0 < kD; c0 += 32) {
+        uint32_t v[32];
+        tmem_ld32(tmem + kTmemO + lane_base + c0, v);
+        tmem_wait_ld();
+#pragma unroll
+        for (int c = 0; c < 32; c += 4) {
+          *reinterpret_cast<float4*>(orow + c0 + c) =
+              make_float4(__uint_as_float(v[c]), __uint_as_float(v[c + 1]),
+                          __uint_as_float(v[c + 2]), __uint_as_float(v[c + 3]));
+        }
+      }
+      *reinterpret_cast<float2*>(a.part_ml + (rec * kRows + row) * 2) = make_float2(m_used, l_run);
+    } else if (ok) {
       tc_fence_after();
       // Every lane reads its TMEM row (warp-collective); rows past the chunk
       // are not stored.
@@ -533,9 +564,89 @@ __global__ void __launch_bounds__(kThreads, 2)
   }
 }
 
+// Merges the split records of one work item per CTA, one query row per
+// thread: out = sum_s 2^(m_s - M) O_s / sum_s 2^(m_s - M) l_s in bf16.  Items
+// whose key range was not split were written by the prefill kernel itself.
+__global__ void __launch_bounds__(kRows) prefill_merge_kernel(const PrefillArgs a) {
+  pdl_wait();
+  int r, h, t0, sp;
+  const int item = cta_work(a, blockIdx.x * a.splits, r, h, t0, sp);
+  const int tok0 = __ldg(a.cu_q + r);
+  const int n = __ldg(a.cu_q + r + 1) - tok0;
+  const int row = threadIdx.x;
+  if (t0 >= n || t0 + row >= n) return;
+  const int ctx = __ldg(a.context_lens + r);
+  const int prior = ctx - n;
+  const int row_tab = a.seq_rows != nullptr ? __ldg(a.seq_rows + r) : r;
+  if (prior < 0 || row_tab < 0 || row_tab >= a.bt_rows || ctx > a.max_blocks * 16) return;
+  const int kv_end = min(ctx, prior + t0 + kRows);
+  const int nsplit = prefill_tile_splits((kv_end + kKeys - 1) / kKeys, a.splits);
+  if (nsplit <= 1) return;
+  const int64_t rec0 = static_cast<int64_t>(item) * a.splits;
+  float m[kMaxPrefillSplits], w[kMaxPrefillSplits];
+  float M = -INFINITY;
+#pragma unroll
+  for (int s = 0; s < kMaxPrefillSplits; ++s) {
+    m[s] = -INFINITY;
+    w[s] = 0.f;
+    if (s < nsplit) {
+      const float2 ml =
+          *reinterpret_cast<const float2*>(a.part_ml + ((rec0 + s) * kRows + row) * 2);
+      m[s] = ml.x;
+      w[s] = ml.y;
+      M = fmaxf(M, ml.x);
+    }
+  }
+  float L = 0.f;
+#pragma unroll
+  for (int s = 0; s < kMaxPrefillSplits; ++s) {
+    // A range none of whose keys this row sees has max -inf: weight 0, and its
+    // O (all zero) is not read.
+    const float f = m[s] == -INFINITY ? 0.f : fast_exp2(m[s] - M);
+    L += f * w[s];
+    w[s] = f;
+  }
+  const float inv = 1.f / L;
+  __nv_bfloat16* dst = static_cast<__nv_bfloat16*>(a.out) +
+                       static_cast<int64_t>(tok0 + t0 + row) * a.o_stride_tok +
+                       static_cast<int64_t>(h) * kD;
+#pragma unroll 4
+  for (int c = 0; c < kD; c += 8) {
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int s = 0; s < kMaxPrefillSplits; ++s) {
+      if (w[s] == 0.f) continue;  // also every s >= nsplit
+      const float* o = a.part_o + ((rec0 + s) * kRows + row) * kD + c;
+      const float4 x = *reinterpret_cast<const float4*>(o);
+      const float4 y = *reinterpret_cast<const float4*>(o + 4);
+      acc[0] += w[s] * x.x; acc[1] += w[s] * x.y; acc[2] += w[s] * x.z; acc[3] += w[s] * x.w;
+      acc[4] += w[s] * y.x; acc[5] += w[s] * y.y; acc[6] += w[s] * y.z; acc[7] += w[s] * y.w;
+    }
+    uint4 out;
+    out.x = pack_bf16x2(acc[0] * inv, acc[1] * inv);
+    out.y = pack_bf16x2(acc[2] * inv, acc[3] * inv);
+    out.z = pack_bf16x2(acc[4] * inv, acc[5] * inv);
+    out.w = pack_bf16x2(acc[6] * inv, acc[7] * inv);
+    *reinterpret_cast<uint4*>(dst + c) = out;
+  }
+}
+
 }  // namespace
 
 int prefill_smem_bytes() { return kSmemBytes; }
+
+int launch_prefill_merge(const PrefillArgs& a, int items, cudaStream_t stream) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(items);
+  cfg.blockDim = dim3(kRows);
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return static_cast<int>(cudaLaunchKernelEx(&cfg, prefill_merge_kernel, a));
+}
 
 int launch_prefill_tc(const PrefillArgs& a, const CUtensorMap& qmap, const CUtensorMap& kmap,
                       const CUtensorMap& vmap, int grid, cudaStream_t stream) {

@@ -22,9 +22,29 @@ struct PrefillArgs {
   // bf16(q.k) * scale exactly and the second rounding is skipped.
   int32_t exact_scale;
   uint32_t* status;
+  // Split-KV: each query tile's key tiles are cut into up to `splits` ranges
+  // of at least kMinSplitTiles tiles, one CTA each; with more than one, every
+  // CTA writes its unnormalised O [128][64] (part_o) and per-row (max, sum)
+  // (part_ml, max in base-2 units) for prefill_merge_kernel, else the output.
+  int32_t splits;
+  float* part_o;
+  float* part_ml;
 };
 
+constexpr int kMinSplitTiles = 4;
+constexpr int kMaxPrefillSplits = 4;
+
+// Ranges a query tile with `ntiles` key tiles is cut into.
+__host__ __device__ __forceinline__ int prefill_tile_splits(int ntiles, int splits) {
+  const int by_size = (ntiles + kMinSplitTiles - 1) / kMinSplitTiles;
+  return by_size < splits ? (by_size > 0 ? by_size : 1) : splits;
+}
+
 int prefill_smem_bytes();
+// Record floats per split CTA (O rows, then (max, sum) per row).
+constexpr int64_t kPrefillRecordO = 128 * 64;
+constexpr int64_t kPrefillRecordML = 128 * 2;
+int launch_prefill_merge(const PrefillArgs& a, int items, cudaStream_t stream);
 int launch_prefill_tc(const PrefillArgs& a, const CUtensorMap& qmap, const CUtensorMap& kmap,
                       const CUtensorMap& vmap, int grid, cudaStream_t stream);
 

@@ -103,13 +103,14 @@ def decode_workspace_bytes(num_seqs: int, num_heads: int, num_kv_heads: int, hea
     return got.value
 
 
-def prefill_workspace_bytes(num_tokens: int, num_heads: int, num_kv_heads: int, head_dim: int,
-                            block_size: int, dtype: torch.dtype) -> int:
+def prefill_workspace_bytes(num_tokens: int, num_rows: int, max_query_len: int, num_heads: int,
+                            num_kv_heads: int, head_dim: int, block_size: int,
+                            dtype: torch.dtype) -> int:
     """Workspace that ``prefill_attention`` needs for this shape."""
     got = ctypes.c_uint64(0)
     check(lib().bs_prefill_attention_workspace_bytes(
-        num_tokens, num_heads, num_kv_heads, head_dim, block_size, dtype_code(dtype),
-        ctypes.byref(got)))
+        num_tokens, num_rows, max_query_len, num_heads, num_kv_heads, head_dim, block_size,
+        dtype_code(dtype), ctypes.byref(got)))
     return got.value
 
 
@@ -561,12 +562,12 @@ def prefill_attention(query: torch.Tensor, key_pool: torch.Tensor, value_pool: t
     code = dtype_code(query.dtype)
     with torch.cuda.device(device):
         stream = torch.cuda.current_stream(device).cuda_stream
-        key = (device.index, T, H, Hkv, D, bs, code)
+        key = (device.index, T, R, int(max_query_len), H, Hkv, D, bs, code)
         need = _prefill_ws_bytes.get(key)
         if need is None:
             got = ctypes.c_uint64(0)
-            check(lib().bs_prefill_attention_workspace_bytes(T, H, Hkv, D, bs, code,
-                                                             ctypes.byref(got)))
+            check(lib().bs_prefill_attention_workspace_bytes(T, R, int(max_query_len), H, Hkv, D,
+                                                             bs, code, ctypes.byref(got)))
             need = _prefill_ws_bytes[key] = got.value
         ws = workspace_for(device, need)
         check(lib().bs_prefill_attention(

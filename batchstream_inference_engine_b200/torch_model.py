@@ -572,14 +572,16 @@ class TorchModel:
                 + [ts[0] for ts in tokens[:n_dec]] + [0] * pd + flat_p + [0] * (Q - len(flat_p)))
 
     def _reserve_graph_workspace(self, block_size: int) -> None:
-        """Sizes the graph stream's workspace for the largest graph before the
-        first capture: a captured launch keeps the buffer's address."""
+        """Sizes the graph stream's workspace for every graph shape before the
+        first capture: a captured launch keeps the buffer's address.  (A small
+        batch of chunks may need more than a large one: its key ranges split.)"""
         c = self.config
-        need = max(
-            ops.decode_workspace_bytes(self.max_graph_batch, c.num_heads, c.num_kv_heads,
-                                       c.head_dim, block_size, self.dtype),
-            ops.prefill_workspace_bytes(self.max_graph_prefill, c.num_heads, c.num_kv_heads,
-                                        c.head_dim, block_size, self.dtype))
+        need = ops.decode_workspace_bytes(self.max_graph_batch, c.num_heads, c.num_kv_heads,
+                                          c.head_dim, block_size, self.dtype)
+        for rows in _powers_of_two(1, self.max_graph_chunks):
+            for q in _powers_of_two(64, self.max_graph_prefill):
+                need = max(need, ops.prefill_workspace_bytes(
+                    q, rows, q, c.num_heads, c.num_kv_heads, c.head_dim, block_size, self.dtype))
         self._graph_ws = ops.workspace_for(self.device, need)
 
     def _capture(self, pool: PagedKVPool, key):
@@ -651,6 +653,14 @@ class TorchModel:
         st["launches"] += graph_launches
         index = list(range(n_dec)) + list(range(B, B + len(groups) - n_dec))
         return self._pending(ids, index)
+
+
+def _powers_of_two(lo: int, limit: int) -> list[int]:
+    """lo, 2 lo, ... up to the first value >= limit (the graph buckets)."""
+    out = [lo]
+    while out[-1] < limit:
+        out.append(out[-1] * 2)
+    return out
 
 
 __all__ = ["ModelConfig", "PagedKVPool", "PagedKVCache", "TorchModel", "QWEN25_05B",

@@ -181,7 +181,15 @@ int bs_prefill_attention(const void* query, int64_t query_token_stride, const in
                          double scaling, int32_t flags, void* output, int64_t output_token_stride,
                          void* workspace, uint64_t workspace_bytes, void* stream);
 
-int bs_prefill_attention_workspace_bytes(int64_t num_tokens, int64_t num_heads,
+/*
+ * Workspace for bs_prefill_attention over num_tokens tokens in num_rows chunks
+ * of at most max_query_len tokens.  On the tensor-core path a small batch of
+ * chunks (fewer query tiles than SMs) splits each tile's key range over up to
+ * 4 CTAs whose partial results a second kernel merges; the
+ * split records live in this workspace (a smaller one only turns the split off).
+ */
+int bs_prefill_attention_workspace_bytes(int64_t num_tokens, int64_t num_rows,
+                                         int64_t max_query_len, int64_t num_heads,
                                          int64_t num_kv_heads, int64_t head_dim,
                                          int64_t block_size, int32_t dtype, uint64_t* bytes_out);
 

@@ -171,6 +171,27 @@ def test_ragged_chunks_edge_cases():
     check_rows(slow, q, k, v, tables, chunks, priors, 7, 0.125, picks)
 
 
+@pytest.mark.parametrize("chunks,priors", [
+    ([300], [2000]),        # 42 query tiles: key ranges of 36 tiles in 4 CTAs each
+    ([70], [5000]),         # one tile, rows past the chunk: 4 ranges of ~20 tiles
+    ([512, 9], [900, 40]),  # a short prefix caps the split (at least 4 tiles each)
+])
+def test_split_key_ranges_match_the_oracle(chunks, priors):
+    # Fewer query tiles than SMs: each tile's key range is split over several
+    # CTAs and their partial results merged; every token against the oracle.
+    q, k, v, tables, bt, cu, ctx = mixed_prefill_batch(chunks, priors, seed=11)
+    args = (q.bfloat16().to(DEV), k.bfloat16().to(DEV), v.bfloat16().to(DEV), bt.to(DEV),
+            cu.to(DEV), ctx.to(DEV), 0.125)
+    out = ops.prefill_attention(*args, max_query_len=max(chunks))
+    assert ops.take_status() == 0
+    assert not out.isnan().any()
+    check_all_rows(out, fp32_reference(q, k, v, tables, chunks, priors, 7, 0.125))
+    picks = [(r, i) for r, c in enumerate(chunks) for i in range(c)]
+    check_rows(out, q, k, v, tables, chunks, priors, 7, 0.125, picks)
+    for _ in range(3):  # the split and its merge are deterministic
+        assert torch.equal(ops.prefill_attention(*args, max_query_len=max(chunks)), out)
+
+
 def test_prefill_repeated_calls_are_identical():
     q, k, v, tables, bt, cu, ctx = mixed_prefill_batch([200, 64], [500, 9], seed=8)
     args = (q.bfloat16().to(DEV), k.bfloat16().to(DEV), v.bfloat16().to(DEV), bt.to(DEV),
