@@ -39,6 +39,8 @@ class TokenGather:
                       for _ in range(2)]
         self._recv = [torch.zeros(self.world * self.width, dtype=torch.int32, device=self.device)
                       for _ in range(2)]
+        self._recv_host = [torch.zeros(self.world * self.width, dtype=torch.int32, pin_memory=cuda)
+                           for _ in range(2)]
         self._stream = torch.cuda.Stream(self.device) if cuda else None
         self._pending = None  # (work handle or None, buffer index) of the last submit
         self._turn = 0
@@ -68,20 +70,28 @@ class TokenGather:
         if self.world == 1:
             return None
         send, recv = self._send[i], self._recv[i]
-        send.copy_(rec, non_blocking=True)
         if self._stream is None:
+            send.copy_(rec)
             return dist.all_gather_into_tensor(recv, send, group=self.group, async_op=True)
-        self._stream.wait_stream(torch.cuda.current_stream(self.device))
+        # The record is host data: its copy and the gather wait for nothing on
+        # the compute stream, which may already hold the next steps.
         with torch.cuda.stream(self._stream):
+            send.copy_(rec, non_blocking=True)
             return dist.all_gather_into_tensor(recv, send, group=self.group, async_op=True)
 
     def _finish(self, work, i: int) -> tuple[bool, list[dict[int, int]]]:
         if self.world == 1:
             return self._decode(self._host[i][None])
-        work.wait()
-        if self._stream is not None:
-            self._stream.synchronize()
-        return self._decode(self._recv[i].view(self.world, -1).cpu())
+        if self._stream is None:
+            work.wait()
+            return self._decode(self._recv[i].view(self.world, -1))
+        # Wait and read back on the gather's stream: the compute stream, which
+        # may hold the next steps already, takes no dependency on the gather.
+        with torch.cuda.stream(self._stream):
+            work.wait()
+            self._recv_host[i].copy_(self._recv[i], non_blocking=True)
+        self._stream.synchronize()
+        return self._decode(self._recv_host[i].view(self.world, -1))
 
     def exchange(self, active: bool, outputs: dict[int, int]) -> tuple[bool, list[dict[int, int]]]:
         """Contributes this rank's {seq_id: token} of one step and returns, for
