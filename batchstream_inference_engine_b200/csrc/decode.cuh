@@ -386,10 +386,12 @@ __device__ __forceinline__ Span compute_warp_spans(const DecodeArgs& a, ScanSmem
   return sp;
 }
 
-// compute_warp_spans with one round of global loads: the raw lengths and table
-// rows of all `B` sequences are staged in `scratch` (2 * B int32 of shared
-// memory that nothing else uses until this returns), and both passes (total,
-// then the scan for the warp starts) run from there.  All threads call it.
+// compute_warp_spans with one round of global loads and one block scan: each
+// thread loads a run of consecutive sequences (their raw lengths and table rows
+// also go to `scratch`, 2 * B int32 of shared memory that nothing else uses
+// until this returns), one inclusive scan of the per-thread unit counts gives
+// every thread its prefix and everyone the total, and each thread then looks for
+// the warp start units among its own sequences.  All threads call it.
 template <int NW>
 __device__ __forceinline__ Span compute_warp_spans_smem(const DecodeArgs& a, ScanSmem& sm,
                                                         WarpStarts& ws, int32_t* scratch) {
@@ -401,8 +403,12 @@ __device__ __forceinline__ Span compute_warp_spans_smem(const DecodeArgs& a, Sca
   const int64_t Hkv = a.num_kv_heads;
   int32_t* lens = scratch;
   int32_t* rows = scratch + B;
+  const int32_t per = (B + nthr - 1) / nthr;
+  const int32_t i0 = tid * per;
   int64_t local = 0;
-  for (int32_t i = tid; i < B; i += nthr) {
+  for (int32_t k = 0; k < per; ++k) {
+    const int32_t i = i0 + k;
+    if (i >= B) break;
     const int32_t len = __ldg(a.context_lens + i);
     const int32_t row = a.seq_rows != nullptr ? __ldg(a.seq_rows + i) : i;
     lens[i] = len;
@@ -410,13 +416,15 @@ __device__ __forceinline__ Span compute_warp_spans_smem(const DecodeArgs& a, Sca
     int32_t l2, r2;
     local += seq_units_raw(a, len, row, l2, r2, c == 0);  // CTA 0 reports bad input once
   }
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) local += __shfl_xor_sync(0xffffffffu, local, o);
-  if (lane == 0) sm.warp_tot[warp] = local;
+  const int64_t incl = warp_inclusive_scan(local);
+  if (lane == 31) sm.warp_tot[warp] = incl;
   if (tid < NW) ws.seq[tid] = -1;
   __syncthreads();
-  int64_t total = 0;
-  for (int w = 0; w < nwarps; ++w) total += sm.warp_tot[w];
+  int64_t before = 0, total = 0;
+  for (int w = 0; w < nwarps; ++w) {
+    if (w < warp) before += sm.warp_tot[w];
+    total += sm.warp_tot[w];
+  }
   Span sp;
   sp.W = total * Hkv;
   sp.q = sp.W / C;
@@ -425,44 +433,32 @@ __device__ __forceinline__ Span compute_warp_spans_smem(const DecodeArgs& a, Sca
   sp.r1 = sp.r0 + sp.q + (c < sp.rem ? 1 : 0);
   sp.seq = -1;
   sp.prefix = 0;
-  __syncthreads();  // warp_tot reuse below
-  if (sp.r0 >= sp.r1) return sp;
-  const int64_t last_target = sp.r0 + (sp.r1 - sp.r0) * (NW - 1) / NW;
-  int64_t carry = 0;
-  for (int32_t base = 0; base < B; base += nthr) {
-    const int32_t i = base + tid;
-    int64_t nb = 0;
-    if (i < B) {
+  if (sp.r0 < sp.r1 && local > 0) {
+    int64_t run = before + incl - local;  // units before this thread's first sequence
+    for (int32_t k = 0; k < per; ++k) {
+      const int32_t i = i0 + k;
+      if (i >= B) break;
       int32_t len, row;
-      nb = seq_units_raw(a, lens[i], rows[i], len, row, false);
-    }
-    const int64_t incl = warp_inclusive_scan(nb);
-    if (lane == 31) sm.warp_tot[warp] = incl;
-    __syncthreads();
-    int64_t before = carry, chunk_total = 0;
-    for (int w = 0; w < nwarps; ++w) {
-      if (w < warp) before += sm.warp_tot[w];
-      chunk_total += sm.warp_tot[w];
-    }
-    const int64_t excl = before + incl - nb;
-    if (nb > 0) {
+      const int64_t nb = seq_units_raw(a, lens[i], rows[i], len, row, false);
+      if (nb > 0) {
 #pragma unroll
-      for (int k = 0; k < NW; ++k) {
-        const int64_t target = sp.r0 + (sp.r1 - sp.r0) * k / NW;
-        if (excl * Hkv <= target && target < (excl + nb) * Hkv) {
-          ws.seq[k] = i;
-          ws.prefix[k] = excl;
-          ws.len[k] = lens[i];
-          ws.row[k] = rows[i];
-          ws.nlen[k] = i + 1 < B ? lens[i + 1] : 0;
-          ws.nrow[k] = i + 1 < B ? rows[i + 1] : 0;
+        for (int t = 0; t < NW; ++t) {
+          const int64_t target = sp.r0 + (sp.r1 - sp.r0) * t / NW;
+          if (run * Hkv <= target && target < (run + nb) * Hkv) {
+            ws.seq[t] = i;
+            ws.prefix[t] = run;
+            ws.len[t] = lens[i];
+            ws.row[t] = rows[i];
+            ws.nlen[t] = i + 1 < B ? lens[i + 1] : 0;
+            ws.nrow[t] = i + 1 < B ? rows[i + 1] : 0;
+          }
         }
       }
+      run += nb;
     }
-    carry += chunk_total;
-    __syncthreads();  // warp_tot reuse; the starts are visible after the last one
-    if (carry * Hkv > last_target) break;
   }
+  __syncthreads();  // the starts are visible
+  if (sp.r0 >= sp.r1) return sp;
   sp.seq = ws.seq[0];
   sp.prefix = ws.prefix[0];
   if (sp.seq < 0) sp.r1 = sp.r0;  // cannot happen when r0 < W; never walk from nowhere
