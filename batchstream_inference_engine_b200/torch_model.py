@@ -584,6 +584,21 @@ class TorchModel:
                     q, rows, q, c.num_heads, c.num_kv_heads, c.head_dim, block_size, self.dtype))
         self._graph_ws = ops.workspace_for(self.device, need)
 
+    @torch.inference_mode()
+    def warm_graphs(self, pool: PagedKVPool) -> int:
+        """Captures the step graph of every padded shape for `pool` now, so no
+        later step waits for a capture; returns how many there are."""
+        if not self.step_graphs:
+            return 0
+        decode = sorted({self._decode_bucket(n) for n in range(self.max_graph_batch + 1)})
+        keys = [(b, 0, 0) for b in decode if b] + [
+            (b, rows, q) for b in decode for rows in _powers_of_two(1, self.max_graph_chunks)
+            for q in _powers_of_two(64, self.max_graph_prefill)]
+        for key in keys:
+            if (id(pool),) + key not in self._graphs:
+                self._capture(pool, key)
+        return len(keys)
+
     def _capture(self, pool: PagedKVPool, key):
         if self._graph_stream is None:
             self._graph_stream = torch.cuda.Stream(self.device)

@@ -54,6 +54,9 @@ WORKLOADS = {
     "decode_d128": dict(kind="decode", heads=28, kv_heads=4, head_dim=128),
     "prefill_d64": dict(kind="prefill", heads=14, kv_heads=2, head_dim=64),
     "engine": dict(kind="engine", heads=14, kv_heads=2, head_dim=64),
+    # Open-loop Poisson arrivals (--rate requests/s over all GPUs, --duration s):
+    # tokens/s over the makespan and TTFT / end-to-end latency percentiles.
+    "engine_load": dict(kind="engine_load", heads=14, kv_heads=2, head_dim=64),
 }
 SEQS_PER_GPU = 256
 BLOCK = 16
@@ -82,6 +85,10 @@ def parse_args():
     p.add_argument("--cpu-seconds", type=float, default=10.0,
                    help="CPU work per CPU-baseline measurement")
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--rate", type=float, default=128.0,
+                   help="engine_load: arrivals per second over all GPUs")
+    p.add_argument("--duration", type=float, default=30.0,
+                   help="engine_load: seconds of arrivals")
     p.add_argument("--pool-gb", type=float, default=0.0,
                    help="pool size per GPU in GB (default: 60%% of device memory)")
     args = p.parse_args()
@@ -979,6 +986,103 @@ def run_engine(args):
         print(json.dumps(result), flush=True)
 
 
+ENGINE_MAX_QUEUE = 1024  # waiting requests per GPU before arrivals are rejected
+
+
+def run_engine_load(args):
+    """The reference load test's shape (config: open-loop Poisson arrivals,
+    prompts U[4, 2048], max_tokens U[32, 512], 256 concurrent and a queue of 1024
+    per GPU, 512-token prefill budget, greedy): the global arrival stream is
+    dealt round-robin to the GPUs, each serving its share in real time; latency
+    is measured on the host clock from each request's scheduled arrival."""
+    import torch
+    import torch.distributed as dist
+
+    from batchstream_inference_engine_b200.backend import PagedBackend
+    from batchstream_inference_engine_b200.serve import (BlockBudget, load_summary,
+                                                          poisson_arrivals, run_open_loop)
+    from batchstream_inference_engine_b200.torch_model import (QWEN25_05B, TorchModel,
+                                                              random_weights)
+
+    world, rank, dev = setup_process()
+    model = TorchModel(QWEN25_05B, random_weights(), device=dev, dtype=torch.bfloat16)
+    blocks = ENGINE_CONCURRENT * -(-(ENGINE_PROMPT[1] + ENGINE_MAX_TOKENS[1]) // BLOCK)
+    backend = PagedBackend(model, blocks, BLOCK, ENGINE_PREFILL, max_seqs=ENGINE_CONCURRENT)
+    graphs = model.warm_graphs(backend.pool)
+    arrivals = poisson_arrivals(args.rate, args.duration, seed=2000, prompt_range=ENGINE_PROMPT,
+                                max_tokens_range=ENGINE_MAX_TOKENS)
+    mine = [a for i, a in enumerate(arrivals) if i % world == rank]
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    before = dict(model.stats)
+    with ClockSampler(dev) as clocks:
+        requests = run_open_loop(backend, mine, ENGINE_CONCURRENT, ENGINE_MAX_QUEUE,
+                                 BlockBudget(blocks, BLOCK), pipelined=True)
+    delta = {k: model.stats[k] - before[k] for k in model.stats}
+    rows = [(r.arrival, r.first_token_at, r.finished_at, r.status, len(r.tokens)) for r in requests]
+    if world > 1:
+        gathered = [None] * world
+        dist.all_gather_object(gathered, rows)
+        rows = [row for part in gathered for row in part]
+        steps = [None] * world
+        dist.all_gather_object(steps, delta)
+    else:
+        steps = [delta]
+    if rank == 0:
+        from batchstream_inference_engine_b200.serve import Request
+
+        merged = []
+        for arrival, first, finish, status, n in rows:
+            r = Request([], 0, arrival=arrival, first_token_at=first, finished_at=finish,
+                        status=status)
+            r.tokens = [0] * n
+            merged.append(r)
+        summ = load_summary(merged)
+        total_steps = sum(d["steps"] for d in steps)
+        rnd = lambda x: None if x is None else round(x, 4)  # noqa: E731
+        print(json.dumps({
+            "metric": "engine tokens/s under open-loop Poisson load",
+            "value": round(summ["tokens_per_s"], 1),
+            "unit": "tokens/s",
+            "n_gpus": world,
+            "steps": total_steps,
+            "warmup": 0,
+            "ms_per_step": round(summ["makespan_s"] * 1e3 * world / max(total_steps, 1), 4),
+            "higher_is_better": True,
+            "scaling": "strong",
+            "vs_baseline": None,
+            "dtype": "bf16",
+            "data": "synthetic (seeded Poisson arrivals of token-id prompts, random-init weights)",
+            "config": {
+                "workload": f"engine_load: open-loop Poisson {args.rate:g} requests/s over all GPUs "
+                            f"for {args.duration:g} s, prompts U{list(ENGINE_PROMPT)}, max_tokens "
+                            f"U{list(ENGINE_MAX_TOKENS)}, {ENGINE_CONCURRENT} concurrent and a queue "
+                            f"of {ENGINE_MAX_QUEUE} per GPU, {ENGINE_PREFILL}-token prefill budget, "
+                            f"greedy, block 16; {graphs} step graphs captured before the run",
+                "rate": args.rate, "duration_s": args.duration,
+                "parallelism": f"dp{world} replicas, arrivals dealt round-robin",
+            },
+            "latency": {"ttft_p50_s": rnd(summ["ttft_p50_s"]), "ttft_p99_s": rnd(summ["ttft_p99_s"]),
+                        "end_to_end_p50_s": rnd(summ["end_to_end_p50_s"]),
+                        "end_to_end_p99_s": rnd(summ["end_to_end_p99_s"]),
+                        "clock": "host wall clock from each request's scheduled arrival"},
+            "requests": {k: summ[k] for k in ("requests", "completed", "tokens",
+                                              "rejected_queue_full", "rejected_too_large",
+                                              "failed")},
+            "makespan_s": round(summ["makespan_s"], 3),
+            "e2e": {"value": round(summ["tokens_per_s"], 1), "unit": "tokens/s",
+                    "h2d_bytes_per_step": round(delta["h2d_bytes"] / max(delta["steps"], 1)),
+                    "d2h_bytes_per_step": round(delta["d2h_bytes"] / max(delta["steps"], 1)),
+                    "path": "the serving loop is the public API"},
+            "gpu_launches": sum(d["launches"] for d in steps),
+            "clocks": clocks.summary(),
+        }), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def time_cpu_engine(seconds, concurrent=16):
     """The oracle's CPU restatement of the reference model step (bf16, all host
     threads for torch) on the engine workload with `concurrent` sequences,
@@ -1015,7 +1119,7 @@ def run_reference(args):
         return
     w = WORKLOADS[args.workload]
     H, Hkv, D = w["heads"], w["kv_heads"], w["head_dim"]
-    if w["kind"] == "engine":
+    if w["kind"] in ("engine", "engine_load"):
         return run_reference_engine(args)
     prefill = w["kind"] == "prefill"
     # Each step is a bounded sample of the workload (decode: 64 of its sequences,
@@ -1091,6 +1195,8 @@ def main():
         run_prefill(args)
     elif kind == "engine":
         run_engine(args)
+    elif kind == "engine_load":
+        run_engine_load(args)
     else:
         run_decode(args)
 

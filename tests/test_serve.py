@@ -198,3 +198,87 @@ def test_qwen_ids_vocabulary():
 
 def test_request_kv_tokens():
     assert Request([1, 2, 3], 5).kv_tokens == 8
+
+
+class FakeClock:
+    def __init__(self):
+        self.t = 0.0
+
+    def __call__(self):
+        return self.t
+
+    def sleep(self, dt):
+        self.t += dt
+
+
+class TimedModel(FakeModel):
+    """Every step takes `dt` seconds of the fake clock."""
+
+    def __init__(self, clock, dt=0.01, **kw):
+        super().__init__(**kw)
+        self.clock, self.dt = clock, dt
+
+    def launch_tokens(self, groups):
+        self.clock.t += self.dt
+        return super().launch_tokens(groups)
+
+
+@pytest.mark.parametrize("pipelined", [False, True])
+def test_open_loop_latencies_are_measured_from_the_scheduled_arrival(pipelined):
+    from batchstream_inference_engine_b200.serve import Arrival, load_summary, run_open_loop
+
+    clock = FakeClock()
+    b = make_backend(TimedModel(clock, dt=0.01), num_blocks=64, prefill_chunk=64)
+    arrivals = [Arrival(0.0, [1] * 4, 3), Arrival(0.5, [2] * 4, 2), Arrival(0.505, [3] * 4, 2)]
+    reqs = run_open_loop(b, arrivals, max_concurrent=8, max_queue=8, budget=BlockBudget(64, 16),
+                         pipelined=pipelined, clock=clock, sleep=clock.sleep)
+    assert [r.status for r in reqs] == ["ok"] * 3
+    assert [len(r.tokens) for r in reqs] == [3, 2, 2]
+    # The first request's first token comes with its prefill step (one step,
+    # or two when its result is read one turn later).
+    steps = 2 if pipelined else 1
+    assert reqs[0].first_token_at == pytest.approx(0.01 * steps)
+    # The idle loop slept until the second arrival: no queueing delay counted.
+    assert reqs[1].first_token_at - reqs[1].arrival == pytest.approx(0.01 * steps)
+    s = load_summary(reqs)
+    assert s["completed"] == 3 and s["tokens"] == 7
+    assert s["makespan_s"] == pytest.approx(max(r.finished_at for r in reqs))
+    assert s["ttft_p99_s"] >= s["ttft_p50_s"] > 0
+
+
+def test_open_loop_rejects_when_the_queue_is_full_or_a_request_never_fits():
+    from batchstream_inference_engine_b200.serve import Arrival, load_summary, run_open_loop
+
+    clock = FakeClock()
+    b = make_backend(TimedModel(clock, dt=1.0), num_blocks=8, prefill_chunk=64)
+    # One active at a time, a queue of one, steps of one second: the second
+    # arrival finds the first still queued; the third comes after the first was
+    # admitted (the queue is empty again), the fourth while the third waits; a
+    # fifth can never fit 8 blocks.
+    arrivals = [Arrival(0.0, [1] * 4, 2), Arrival(0.0, [2] * 4, 2), Arrival(0.5, [3] * 4, 2),
+                Arrival(0.6, [4] * 4, 2), Arrival(0.7, [9] * 200, 1)]
+    reqs = run_open_loop(b, arrivals, max_concurrent=1, max_queue=1, budget=BlockBudget(8, 16),
+                         pipelined=True, clock=clock, sleep=clock.sleep)
+    assert [r.status for r in reqs] == ["ok", "rejected_queue_full", "ok", "rejected_queue_full",
+                                        "rejected_too_large"]
+    s = load_summary(reqs)
+    assert s["rejected_queue_full"] == 2 and s["rejected_too_large"] == 1 and s["completed"] == 2
+    # The third waited for the first to finish: its latency includes the queueing.
+    assert reqs[2].first_token_at - reqs[2].arrival > 1.0
+
+
+def test_nearest_rank_percentile_and_poisson_arrivals():
+    from batchstream_inference_engine_b200.serve import nearest_rank, poisson_arrivals
+
+    assert nearest_rank([5.0, 1.0, 3.0, 2.0, 4.0], 50) == 3.0
+    assert nearest_rank(list(range(1, 101)), 99) == 99
+    assert nearest_rank([], 50) is None
+    slow = poisson_arrivals(8, 30.0, seed=3)
+    fast = poisson_arrivals(128, 30.0, seed=3)
+    assert 160 <= len(slow) <= 320 and 3500 <= len(fast) <= 4200  # ~rate x duration
+    assert all(0 < a.time < 30 for a in fast)
+    assert all(b.time > a.time for a, b in zip(fast, fast[1:]))
+    # The same requests in the same order at every rate.
+    assert [(a.prompt_tokens, a.max_tokens) for a in slow] == \
+        [(a.prompt_tokens, a.max_tokens) for a in fast[: len(slow)]]
+    assert all(4 <= len(a.prompt_tokens) <= 2048 and 32 <= a.max_tokens <= 512 for a in fast)
