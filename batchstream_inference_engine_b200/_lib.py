@@ -33,6 +33,7 @@ EXPORTS = (
     "bs_rope_append",
     "bs_silu_mul",
     "bs_kernel_launches",
+    "bs_argmax_rows",
 )
 
 _i32, _i64, _u64, _p, _dbl = ctypes.c_int32, ctypes.c_int64, ctypes.c_uint64, ctypes.c_void_p, ctypes.c_double
@@ -97,6 +98,7 @@ _SIGNATURES = {
     ),
     "bs_silu_mul": ([_p, _i64, _i64, _i64, _i32, _p, _p], ctypes.c_int),
     "bs_kernel_launches": ([], ctypes.c_uint64),
+    "bs_argmax_rows": ([_p, _i64, _i64, _i64, _i32, _p, _p], ctypes.c_int),
 }
 
 _lib: ctypes.CDLL | None = None

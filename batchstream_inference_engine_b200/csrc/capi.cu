@@ -41,6 +41,8 @@ int launch_rope_append(const void* qkv, int64_t qkv_stride, const void* cos_t, c
                        uint32_t* status, cudaStream_t stream);
 int launch_silu_mul(const void* gate_up, int64_t stride, int32_t ntok, int32_t inter, void* out,
                     bool bf16, bool vec, int sms, cudaStream_t stream);
+int launch_argmax_rows(const void* x, int64_t stride, int32_t rows, int64_t cols, void* out,
+                       bool bf16, bool vec, cudaStream_t stream);
 int launch_decode_append(const int32_t* seq_rows, const int32_t* start_pos, int32_t R,
                          const int32_t* block_tables, int64_t bt_stride, int32_t bt_rows,
                          int32_t max_blocks, int32_t block_size, int32_t num_blocks,
@@ -872,6 +874,22 @@ int bs_silu_mul(const void* gate_up, int64_t row_stride, int64_t num_tokens, int
                                       static_cast<int32_t>(intermediate), out, dtype == BS_BF16,
                                       vec, d->sms, static_cast<cudaStream_t>(stream));
   if (rc != 0) return cuda_fail(static_cast<cudaError_t>(rc), "silu_mul launch");
+  count_launches(1);
+  return BS_OK;
+}
+
+int bs_argmax_rows(const void* logits, int64_t row_stride, int64_t rows, int64_t cols,
+                   int32_t dtype, int32_t* out, void* stream) {
+  BS_CHECK(dtype == BS_BF16 || dtype == BS_F32, "dtype must be bfloat16 or float32");
+  BS_CHECK(rows >= 0 && rows <= kInt32Max && cols > 0 && cols <= kInt32Max,
+           "rows or cols out of range");
+  BS_CHECK(row_stride >= cols, "row stride must cover cols");
+  if (rows == 0) return BS_OK;
+  BS_CHECK(logits && out, "null pointer argument");
+  const bool vec = cols % 8 == 0 && row_stride % 8 == 0 && aligned16(logits);
+  const int rc = bsb::launch_argmax_rows(logits, row_stride, static_cast<int32_t>(rows), cols, out,
+                                         dtype == BS_BF16, vec, static_cast<cudaStream_t>(stream));
+  if (rc != 0) return cuda_fail(static_cast<cudaError_t>(rc), "argmax launch");
   count_launches(1);
   return BS_OK;
 }

@@ -10,6 +10,7 @@
 //               q' = T(T(q * cos) + T(rotate_half(q) * sin)), the same for k;
 //               q' to the attention input, k' and v into their pool slots
 //   silu_mul    (:278-281)  T(T(silu(gate)) * up)
+//   argmax_rows (backend/paged.py:95-99) greedy token of each logits row
 //
 // T is the model dtype (bf16, or fp32 where the roundings vanish); cos/sin are
 // the bf16-rounded rotary tables gathered by position.  All are bandwidth-bound
@@ -238,6 +239,76 @@ __global__ void __launch_bounds__(128)
   }
 }
 
+// Greedy argmax of each row (the first index of the maximum; a NaN counts as
+// larger than any number, as torch.argmax has it): one CTA per row, 8 elements
+// per 16-byte load when VEC, then a warp and a block reduction of (value, index).
+constexpr int kArgmaxThreads = 512;
+
+__device__ __forceinline__ bool argmax_better(float v, int64_t i, float bv, int64_t bi) {
+  const bool vn = v != v, bn = bv != bv;
+  if (vn != bn) return vn;  // NaN wins over numbers
+  if (!vn && v != bv) return v > bv;
+  return i < bi;  // equal (or both NaN): the first index
+}
+
+template <typename T, bool VEC>
+__global__ void __launch_bounds__(kArgmaxThreads)
+    argmax_rows_kernel(const T* __restrict__ x, int64_t stride, int64_t cols,
+                       int32_t* __restrict__ out) {
+  pdl_trigger();
+  pdl_wait();
+  const T* row = x + static_cast<int64_t>(blockIdx.x) * stride;
+  float best = -INFINITY;
+  int64_t bi = cols;  // past every index: loses all ties
+  if constexpr (VEC) {
+    for (int64_t c = threadIdx.x * 8; c < cols; c += kArgmaxThreads * 8) {
+      float v[8];
+      load8(row + c, v);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        if (argmax_better(v[j], c + j, best, bi)) {
+          best = v[j];
+          bi = c + j;
+        }
+      }
+    }
+  } else {
+    for (int64_t c = threadIdx.x; c < cols; c += kArgmaxThreads) {
+      const float v = ld<T>(row + c);
+      if (argmax_better(v, c, best, bi)) {
+        best = v;
+        bi = c;
+      }
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+    const int64_t oi = __shfl_xor_sync(0xffffffffu, bi, o);
+    if (argmax_better(ov, oi, best, bi)) {
+      best = ov;
+      bi = oi;
+    }
+  }
+  __shared__ float wv[kArgmaxThreads / 32];
+  __shared__ int64_t wi[kArgmaxThreads / 32];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  if (lane == 0) {
+    wv[warp] = best;
+    wi[warp] = bi;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int w = 1; w < kArgmaxThreads / 32; ++w) {
+      if (argmax_better(wv[w], wi[w], best, bi)) {
+        best = wv[w];
+        bi = wi[w];
+      }
+    }
+    out[blockIdx.x] = static_cast<int32_t>(bi);
+  }
+}
+
 cudaLaunchConfig_t cfg_of(dim3 grid, int threads, cudaStream_t stream,
                           cudaLaunchAttribute* attr) {
   cudaLaunchConfig_t cfg = {};
@@ -323,6 +394,24 @@ int launch_silu_mul(const void* gate_up, int64_t stride, int32_t ntok, int32_t i
   if (vec) BS_SILU(float, true);
   BS_SILU(float, false);
 #undef BS_SILU
+}
+
+int launch_argmax_rows(const void* x, int64_t stride, int32_t rows, int64_t cols, void* out,
+                       bool bf16, bool vec, cudaStream_t stream) {
+  if (rows == 0) return 0;
+  cudaLaunchAttribute attr[1];
+  cudaLaunchConfig_t cfg = cfg_of(dim3(rows), kArgmaxThreads, stream, attr);
+#define BS_ARGMAX(T, V)                                                                         \
+  return static_cast<int>(cudaLaunchKernelEx(&cfg, argmax_rows_kernel<T, V>,                    \
+                                             static_cast<const T*>(x), stride, cols,            \
+                                             static_cast<int32_t*>(out)))
+  if (bf16) {
+    if (vec) BS_ARGMAX(__nv_bfloat16, true);
+    BS_ARGMAX(__nv_bfloat16, false);
+  }
+  if (vec) BS_ARGMAX(float, true);
+  BS_ARGMAX(float, false);
+#undef BS_ARGMAX
 }
 
 }  // namespace bsb

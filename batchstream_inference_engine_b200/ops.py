@@ -492,6 +492,23 @@ def silu_mul(gate_up: torch.Tensor, out: torch.Tensor | None = None) -> torch.Te
     return o
 
 
+def argmax_rows(logits: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """int32 greedy token of each row of `logits` [R, V]: the first index of
+    the maximum (a NaN counts as the maximum), as torch.argmax."""
+    device = _require_cuda("argmax_rows", logits, out)
+    if logits.dim() != 2 or logits.stride(1) != 1:
+        raise RuntimeError("logits must be [rows, vocab] with unit inner stride")
+    R, V = logits.shape
+    o = out if out is not None else torch.empty(R, dtype=torch.int32, device=device)
+    if o.dtype != torch.int32 or o.numel() < R or not o.is_contiguous():
+        raise RuntimeError("out must be int32 with a slot per row")
+    with torch.cuda.device(device):
+        stream = torch.cuda.current_stream(device).cuda_stream
+        check(lib().bs_argmax_rows(logits.data_ptr(), logits.stride(0), R, V,
+                                   dtype_code(logits.dtype), o.data_ptr(), stream))
+    return o
+
+
 __all__ = [
     "paged_attention",
     "paged_attention_batched",
@@ -501,6 +518,7 @@ __all__ = [
     "rms_norm",
     "rope_append",
     "silu_mul",
+    "argmax_rows",
     "take_status",
     "kernel_launches",
     "decode_workspace_bytes",

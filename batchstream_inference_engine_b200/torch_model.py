@@ -330,7 +330,7 @@ class TorchModel:
             return self._graph_step(groups, key)
         pool = groups[0][1]._pool
         logits = self.forward_batch(groups)
-        ids = logits.argmax(dim=-1).to(torch.int32)
+        ids = ops.argmax_rows(logits)
         pool.last_ids[: ids.numel()].copy_(ids)
         return self._pending(ids, list(range(len(groups))))
 
@@ -546,7 +546,7 @@ class TorchModel:
                                       max_query_len=Q, seq_rows=rows[B:], out=attended[B:])
 
         last = self._layers(pool, self._resolve(pool, tokens), positions, slots, ends, attend)
-        ids = F.linear(last, self.embed).argmax(dim=-1).to(torch.int32)
+        ids = ops.argmax_rows(F.linear(last, self.embed))
         pool.last_ids[:R].copy_(ids)
         return ids
 

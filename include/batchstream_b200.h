@@ -287,6 +287,13 @@ int bs_rope_append(const void* qkv, int64_t qkv_row_stride, int32_t dtype, const
                    uint32_t* status, void* stream);
 int bs_silu_mul(const void* gate_up, int64_t row_stride, int64_t num_tokens, int64_t intermediate,
                 int32_t dtype, void* out, void* stream);
+/*
+ * Greedy token of each logits row (backend/paged.py:95-99, on the device):
+ * out[r] = the first index of the row's maximum, a NaN counting as the maximum
+ * (torch.argmax's rule), over `cols` entries.
+ */
+int bs_argmax_rows(const void* logits, int64_t row_stride, int64_t rows, int64_t cols,
+                   int32_t dtype, int32_t* out, void* stream);
 
 /*
  * Waits for `stream`, then reads and clears the status word at the start of a

@@ -202,3 +202,18 @@ def test_kernel_launch_counter_counts_each_kernel():
     ops.paged_attention_batched(q, kp, vp, tables, ctx, D ** -0.5)
     ops.take_status(torch.device(DEV))
     assert ops.kernel_launches() - before == 2
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+@pytest.mark.parametrize("vocab", [151936, 1001], ids=["vector", "scalar"])
+def test_argmax_rows_matches_torch(dtype, vocab):
+    g = torch.Generator(device=DEV).manual_seed(5)
+    x = torch.randn(37, vocab, generator=g, device=DEV).to(dtype)
+    x[3, 10] = x[3, 500] = x[3].max() + 1  # a tie: the first index wins
+    x[4] = -float("inf")                   # all -inf: index 0
+    x[5, 77] = float("nan")                # NaN counts as the maximum
+    x[6, 900] = x[6, 100] = float("nan")   # the first NaN
+    got = ops.argmax_rows(x)
+    assert torch.equal(got.long(), x.float().argmax(dim=-1))
+    assert got[3].item() == 10 and got[4].item() == 0 and got[5].item() == 77
+    assert got[6].item() == 100
