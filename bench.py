@@ -72,7 +72,8 @@ ENGINE_PROMPT = (4, 2048)
 ENGINE_MAX_TOKENS = (32, 512)
 # Default --steps / --warmup per workload kind (engine steps reach steady
 # state only after the first admissions' prompts are through).
-DEFAULT_STEPS = {"decode": (1000, 20), "prefill": (1000, 20), "engine": (600, 600)}
+DEFAULT_STEPS = {"decode": (1000, 20), "prefill": (1000, 20), "engine": (600, 600),
+                 "engine_load": (0, 0)}  # engine_load runs for --duration instead
 
 
 def parse_args():
