@@ -176,23 +176,38 @@ WsLayout ws_layout(int64_t segments, int64_t staging_ints, int64_t grid, int64_t
 }
 
 // Split-KV factor of the tensor-core prefill: up to one CTA per SM.  A second
-// CTA on an SM adds no throughput (measured: the SM's softmax and operand
-// traffic are the bound, not one CTA's chain of waits), so only batches with
-// fewer query tiles than SMs are split.
+// CTA on an SM adds less than a first, and every piece costs a CTA's set-up and
+// a merge, so only batches with fewer query tiles than SMs are split.
 int prefill_splits(int64_t items, int sms) {
   if (items <= 0) return 1;
   const int64_t want = (static_cast<int64_t>(sms) + items - 1) / items;
   return static_cast<int>(std::min<int64_t>(std::max<int64_t>(want, 1), bsb::kMaxPrefillSplits));
 }
 
-// Workspace bytes of the prefill records (split > 1): they start where the
-// decode's scratch does, past the status word and the segment counters (which
-// stay zero between calls).
+// Rows x query tiles whose work the plan kernel ranks (0: no plan): only for
+// grids of more than one wave of resident CTAs (inside one wave the order does
+// not matter), and plans one CTA ranks (rts * max(splits, 2) entries at most).
+int64_t prefill_plan_rts(int64_t num_rows, int64_t qtiles, int64_t heads, int splits, int sms) {
+  const int64_t rts = num_rows * qtiles;
+  const int64_t slots = static_cast<int64_t>(sms) * bsb::prefill_ctas_per_sm();
+  if (rts <= 0 || rts * heads * splits <= slots ||
+      rts * std::max(splits, 2) > bsb::kMaxPlanEntries) {
+    return 0;
+  }
+  return rts;
+}
+
+// Workspace of the tensor-core prefill: the split records (splits > 1) start
+// where the decode's scratch does, past the status word and the segment
+// counters (which stay zero between calls); the plan follows them.
 int64_t prefill_split_offset() { return ws_layout(0, 0, 0, 0).staging; }
-int64_t prefill_split_bytes(int64_t items, int splits) {
-  if (splits <= 1) return 256;
-  return prefill_split_offset() +
-         items * splits * (bsb::kPrefillRecordO + bsb::kPrefillRecordML) * 4;
+int64_t prefill_records_bytes(int64_t items, int splits) {
+  return splits > 1 ? items * splits * (bsb::kPrefillRecordO + bsb::kPrefillRecordML) * 4 : 0;
+}
+int64_t prefill_ws_bytes(int64_t items, int splits, int64_t plan_entries) {
+  int64_t b = prefill_split_offset() + prefill_records_bytes(items, splits);
+  if (plan_entries > 0) b += (1 + 2 * plan_entries) * 16;
+  return b;
 }
 
 // ------------------------------------------------------------------ tensor maps
@@ -597,8 +612,11 @@ int bs_prefill_attention_workspace_bytes(int64_t num_tokens, int64_t num_rows,
   // The tensor-core path: split-KV records after the decode's counters.
   DeviceInfo* d = nullptr;
   if (int rc = current_device_info(&d)) return rc;
-  const int64_t items = num_rows * num_heads * ((max_query_len + 127) / 128);
-  need = std::max(need, prefill_split_bytes(items, prefill_splits(items, d->sms)));
+  const int64_t qtiles = (max_query_len + 127) / 128;
+  const int64_t items = num_rows * num_heads * qtiles;
+  const int splits = prefill_splits(items, d->sms);
+  const int64_t rts = prefill_plan_rts(num_rows, qtiles, num_heads, splits, d->sms);
+  need = std::max(need, prefill_ws_bytes(items, splits, rts * splits));
   *bytes_out = static_cast<uint64_t>(need);
   return BS_OK;
 }
@@ -682,13 +700,25 @@ int bs_prefill_attention(const void* query, int64_t query_token_stride, const in
     const int64_t items = num_rows * num_heads * p.qtiles;
     DeviceInfo* d = nullptr;
     if ((rc = current_device_info(&d))) return rc;
+    // Split and plan as far as the workspace holds them.
+    const int64_t wsb = static_cast<int64_t>(workspace_bytes);
     p.splits = prefill_splits(items, d->sms);
-    if (static_cast<int64_t>(workspace_bytes) < prefill_split_bytes(items, p.splits)) p.splits = 1;
+    if (wsb < prefill_ws_bytes(items, p.splits, 0)) p.splits = 1;
+    int64_t rts = prefill_plan_rts(num_rows, p.qtiles, num_heads, p.splits, d->sms);
+    if (wsb < prefill_ws_bytes(items, p.splits, rts * p.splits)) rts = 0;
     float* records = reinterpret_cast<float*>(ws + prefill_split_offset());
     p.part_o = records;
     p.part_ml = records + items * p.splits * bsb::kPrefillRecordO;
+    p.plan = rts > 0 ? reinterpret_cast<int4*>(ws + prefill_split_offset() +
+                                               prefill_records_bytes(items, p.splits))
+                     : nullptr;
     const int64_t grid = items * p.splits;
     if (grid > kInt32Max) return fail(BS_ERR_UNSUPPORTED, "too many query tiles");
+    if (p.plan != nullptr) {
+      rc = bsb::launch_prefill_plan(p, st);
+      if (rc != 0) return cuda_fail(static_cast<cudaError_t>(rc), "prefill plan launch");
+      count_launches(1);
+    }
     rc = bsb::launch_prefill_tc(p, qmap, kmap, vmap, static_cast<int>(grid), st);
     if (rc != 0) return cuda_fail(static_cast<cudaError_t>(rc), "prefill kernel launch");
     count_launches(1);

@@ -6,9 +6,13 @@
 // chunk and full over the cached part — the reference's _read_blocks + attend
 // with _causal_mask (src/server/torch_model.py:39-64, 165-167, 295-297).
 //
-// One CTA per (chunk, query head, 128-token query tile); CTAs are numbered so
-// the query tiles with the most keys start first.  Three roles, one warp each
-// for the first two:
+// One CTA per (chunk, query head, 128-token query tile, piece of its key
+// range; pieces only for batches with fewer query tiles than SMs, merged by
+// prefill_merge_kernel).  A CTA's time is its chain of key tiles, so when the
+// grid is more than one wave of resident CTAs a one-CTA plan kernel runs first
+// and ranks the work by key tiles: the longest chains start in the first wave
+// instead of whenever their index comes up.  Three roles, one warp each for
+// the first two:
 //   * loader (warp 5): the query tile as one TMA box of a [T, H, D] tensor map,
 //     then the sequence's K and V through the block table into a 4-stage K ring
 //     and a 3-stage V ring (64 keys = 4 blocks per stage, one TMA box per block).
@@ -152,20 +156,56 @@ __device__ __forceinline__ uint32_t swz128(int r, int c) {
   return r * 128 + ((((c >> 3) ^ (r & 7))) << 4) + (c & 7) * 2;
 }
 
-// Work item (chunk r, head h, query tile at t0) of CTA b and its key range
-// split sp: tiles with the most keys first (the last query tile of every
-// chunk, then the one before, ...), heads inside, splits innermost.
-__device__ __forceinline__ int cta_work(const PrefillArgs& a, int b, int& r, int& h, int& t0,
-                                        int& sp) {
-  sp = b % a.splits;
-  const int item = b / a.splits;
+// What one CTA computes: chunk r, head h, the query tile at t0 and piece sp of
+// its key range (record item * splits + sp), with the chunk's first token,
+// query tokens, context length and block-table row.
+struct Work {
+  int item, r, h, t0, sp;
+  int tok0, n, ctx, row_tab;
+};
+
+// Work of CTA b without a plan: tiles with the most keys first (the last
+// query tile of every chunk, then the one before, ...), heads inside, splits
+// innermost.  Also numbers the merge kernel's items (b = item * splits).
+__device__ __forceinline__ void item_work(const PrefillArgs& a, int b, Work& w) {
+  w.sp = b % a.splits;
+  w.item = b / a.splits;
   const int H = a.num_heads;
-  h = item % H;
-  const int rt = item / H;  // 0 .. num_rows * qtiles - 1
+  w.h = w.item % H;
+  const int rt = w.item / H;  // 0 .. num_rows * qtiles - 1
   const int t = a.qtiles - 1 - rt / a.num_rows;
-  r = rt % a.num_rows;
-  t0 = t * kRows;
-  return item;
+  w.r = rt % a.num_rows;
+  w.t0 = t * kRows;
+  w.tok0 = __ldg(a.cu_q + w.r);
+  w.n = __ldg(a.cu_q + w.r + 1) - w.tok0;
+  w.ctx = __ldg(a.context_lens + w.r);
+  w.row_tab = a.seq_rows != nullptr ? __ldg(a.seq_rows + w.r) : w.r;
+}
+
+// Work of CTA b: entry b / H of the plan (head b % H), or the plan-less
+// numbering.  False for CTAs past the plan's entries.
+__device__ __forceinline__ bool cta_work(const PrefillArgs& a, int b, Work& w) {
+  if (a.plan == nullptr) {
+    item_work(a, b, w);
+    return true;
+  }
+  const int H = a.num_heads;
+  const int d = b / H;  // < rows * qtiles * splits: inside the plan
+  const int4 head = __ldg(a.plan);
+  const int4 x = __ldg(a.plan + 1 + 2 * d);
+  const int4 y = __ldg(a.plan + 2 + 2 * d);
+  if (d >= head.x) return false;
+  w.h = b % H;
+  w.sp = x.x % a.splits;
+  const int rt = x.x / a.splits;
+  w.item = rt * H + w.h;
+  w.r = rt % a.num_rows;
+  w.t0 = (a.qtiles - 1 - rt / a.num_rows) * kRows;
+  w.tok0 = x.y;
+  w.n = x.z;
+  w.ctx = x.w;
+  w.row_tab = y.x;
+  return true;
 }
 
 __global__ void __launch_bounds__(kThreads, 2)
@@ -192,15 +232,14 @@ __global__ void __launch_bounds__(kThreads, 2)
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   pdl_wait();
 
-  int r, h, t0, sp;
-  const int item = cta_work(a, blockIdx.x, r, h, t0, sp);
-  const int tok0 = __ldg(a.cu_q + r);
-  const int n = __ldg(a.cu_q + r + 1) - tok0;
+  Work wk;
+  if (!cta_work(a, blockIdx.x, wk)) return;
+  const int item = wk.item, h = wk.h, t0 = wk.t0, sp = wk.sp, tok0 = wk.tok0, n = wk.n;
   if (t0 == 0 && h == 0 && tid == 0 && n > a.qtiles * kRows) set_status(a.status, kStatusBadLength);
   if (t0 >= n) return;
-  const int ctx = __ldg(a.context_lens + r);
+  const int ctx = wk.ctx;
   const int prior = ctx - n;
-  const int row_tab = a.seq_rows != nullptr ? __ldg(a.seq_rows + r) : r;
+  const int row_tab = wk.row_tab;
   if (n <= 0 || prior < 0 || row_tab < 0 || row_tab >= a.bt_rows ||
       ctx > a.max_blocks * 16) {
     if (tid == 0) set_status(a.status, row_tab < 0 || row_tab >= a.bt_rows ? kStatusBadRow
@@ -569,15 +608,14 @@ __global__ void __launch_bounds__(kThreads, 2)
 // whose key range was not split were written by the prefill kernel itself.
 __global__ void __launch_bounds__(kRows) prefill_merge_kernel(const PrefillArgs a) {
   pdl_wait();
-  int r, h, t0, sp;
-  const int item = cta_work(a, blockIdx.x * a.splits, r, h, t0, sp);
-  const int tok0 = __ldg(a.cu_q + r);
-  const int n = __ldg(a.cu_q + r + 1) - tok0;
+  Work wk;
+  item_work(a, blockIdx.x * a.splits, wk);
+  const int item = wk.item, h = wk.h, t0 = wk.t0, tok0 = wk.tok0, n = wk.n;
   const int row = threadIdx.x;
   if (t0 >= n || t0 + row >= n) return;
-  const int ctx = __ldg(a.context_lens + r);
+  const int ctx = wk.ctx;
   const int prior = ctx - n;
-  const int row_tab = a.seq_rows != nullptr ? __ldg(a.seq_rows + r) : r;
+  const int row_tab = wk.row_tab;
   if (prior < 0 || row_tab < 0 || row_tab >= a.bt_rows || ctx > a.max_blocks * 16) return;
   const int kv_end = min(ctx, prior + t0 + kRows);
   const int nsplit = prefill_tile_splits((kv_end + kKeys - 1) / kKeys, a.splits);
@@ -631,6 +669,70 @@ __global__ void __launch_bounds__(kRows) prefill_merge_kernel(const PrefillArgs 
   }
 }
 
+
+// Ranks the prefill work, one CTA: every (row, query tile) rt has
+//   tiles(rt) = ceil(min(ctx, prior + t0 + 128) / 64)
+// key tiles per head, cut into pieces as the kernel cuts them; the pieces are
+// ranked by size, largest first (ties by index), so that launched in that
+// order the longest chains start first.
+constexpr int kPlanThreads = kMaxPlanEntries;
+
+__global__ void __launch_bounds__(kPlanThreads) prefill_plan_kernel(const PrefillArgs a) {
+  // Per rt (at most half the entries: the host keeps rt * 2 within them): the
+  // row's first token, query tokens, context and block-table row.
+  __shared__ int4 s_row[kMaxPlanEntries / 2];
+  __shared__ int32_t s_size[kMaxPlanEntries];  // per slot rt * splits + piece, -1 unused
+  __shared__ int32_t s_cnt[kPlanThreads / 32];
+  pdl_trigger();  // the prefill CTAs may take their SMs and wait for the plan
+  pdl_wait();     // cu_q and context_lens come from the kernels just ahead
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int R = a.num_rows, Q = a.qtiles, S = a.splits;
+  const int n_slot = R * Q * S;  // <= kMaxPlanEntries (host)
+
+  // Slot rt * S + p holds piece p of rt while p < pieces(rt); a row without
+  // work keeps one entry, so the kernel still checks it.
+  int size = -1;
+  if (tid < n_slot) {
+    const int rt = tid / S, p = tid % S;
+    const int r = rt % R, t0 = (Q - 1 - rt / R) * kRows;
+    const int tok0 = __ldg(a.cu_q + r);
+    const int n = __ldg(a.cu_q + r + 1) - tok0;
+    const int ctx = __ldg(a.context_lens + r);
+    if (p == 0) {
+      const int row_tab = a.seq_rows != nullptr ? __ldg(a.seq_rows + r) : r;
+      s_row[rt] = make_int4(tok0, n, ctx, row_tab);
+    }
+    int tiles = 0;
+    // Rows the prefill kernel rejects or skips count as no work.
+    if (n > 0 && t0 < n && ctx >= n && ctx <= a.max_blocks * 16) {
+      const long long kv_end = min(static_cast<long long>(ctx),
+                                   static_cast<long long>(ctx - n) + t0 + kRows);
+      tiles = static_cast<int>((kv_end + kKeys - 1) / kKeys);
+    }
+    const int k = prefill_tile_splits(tiles, S);
+    if (p < k) size = (p + 1) * tiles / k - p * tiles / k;
+    s_size[tid] = size;
+  }
+  const unsigned valid = __ballot_sync(0xffffffffu, size >= 0);
+  if (lane == 0) s_cnt[warp] = __popc(valid);
+  __syncthreads();
+  if (size >= 0) {
+    int rank = 0;
+    for (int f = 0; f < n_slot; ++f) {
+      const int g = s_size[f];
+      rank += (g > size || (g == size && f < tid)) ? 1 : 0;
+    }
+    const int4 row = s_row[tid / S];
+    a.plan[1 + 2 * rank] = make_int4(tid, row.x, row.y, row.z);
+    a.plan[2 + 2 * rank] = make_int4(row.w, 0, 0, 0);
+  }
+  if (tid == 0) {
+    int entries = 0;
+    for (int w = 0; w < kPlanThreads / 32; ++w) entries += s_cnt[w];
+    a.plan[0] = make_int4(entries, 0, 0, 0);
+  }
+}
+
 }  // namespace
 
 int prefill_smem_bytes() { return kSmemBytes; }
@@ -648,8 +750,9 @@ int launch_prefill_merge(const PrefillArgs& a, int items, cudaStream_t stream) {
   return static_cast<int>(cudaLaunchKernelEx(&cfg, prefill_merge_kernel, a));
 }
 
-int launch_prefill_tc(const PrefillArgs& a, const CUtensorMap& qmap, const CUtensorMap& kmap,
-                      const CUtensorMap& vmap, int grid, cudaStream_t stream) {
+namespace {
+
+int configure_prefill() {
   static bool configured = false;
   if (!configured) {
     cudaError_t e = cudaFuncSetAttribute(prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -660,6 +763,53 @@ int launch_prefill_tc(const PrefillArgs& a, const CUtensorMap& qmap, const CUten
     if (e != cudaSuccess) return static_cast<int>(e);
     configured = true;
   }
+  return 0;
+}
+
+}  // namespace
+
+// Prefill CTAs resident on one SM: as many as its shared memory holds with the
+// whole unified L1 carved out as shared memory (the launch asks for that; the
+// occupancy calculator assumes the default carve-out and reports one), at most
+// two by TMEM (kTmemCols of 512 columns each) and by the launch bounds.
+int prefill_ctas_per_sm() {
+  static int ctas = 0;
+  if (ctas == 0) {
+    int dev = 0, smem_sm = 0, reserved = 0;
+    cudaFuncAttributes fa{};
+    if (cudaGetDevice(&dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&smem_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev) !=
+            cudaSuccess ||
+        cudaDeviceGetAttribute(&reserved, cudaDevAttrReservedSharedMemoryPerBlock, dev) !=
+            cudaSuccess ||
+        cudaFuncGetAttributes(&fa, prefill_kernel) != cudaSuccess) {
+      return 1;
+    }
+    const int per_cta = kSmemBytes + static_cast<int>(fa.sharedSizeBytes) + reserved;
+    const int by_smem = smem_sm / per_cta;
+    const int by_tmem = 512 / static_cast<int>(kTmemCols);
+    ctas = by_smem < by_tmem ? by_smem : by_tmem;
+    if (ctas < 1) ctas = 1;
+  }
+  return ctas;
+}
+
+int launch_prefill_plan(const PrefillArgs& a, cudaStream_t stream) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(1);
+  cfg.blockDim = dim3(kPlanThreads);
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return static_cast<int>(cudaLaunchKernelEx(&cfg, prefill_plan_kernel, a));
+}
+
+int launch_prefill_tc(const PrefillArgs& a, const CUtensorMap& qmap, const CUtensorMap& kmap,
+                      const CUtensorMap& vmap, int grid, cudaStream_t stream) {
+  if (int e = configure_prefill()) return e;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
   cfg.blockDim = dim3(kThreads);

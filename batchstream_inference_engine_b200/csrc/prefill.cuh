@@ -29,10 +29,21 @@ struct PrefillArgs {
   int32_t splits;
   float* part_o;
   float* part_ml;
+  // Work order (may be null), written by prefill_plan_kernel just ahead of the
+  // prefill kernel: plan[0] = {entries E, 0, 0, 0}; entry d, run by CTAs
+  // d * H .. d * H + H - 1 (one per query head), is
+  //   plan[1 + 2d] = {rt * splits + piece, first token, query tokens, context}
+  //   plan[2 + 2d] = {block-table row, 0, 0, 0}
+  // with rt the (row, query tile) index of the plan-less numbering.  Entries are
+  // ranked by key tiles, most first: when the grid is more than one wave of
+  // resident CTAs, the longest ranges then start in the first.
+  int4* plan;
 };
 
 constexpr int kMinSplitTiles = 4;
 constexpr int kMaxPrefillSplits = 4;
+// Largest plan ranked in one CTA (entries = rows x query tiles x splits).
+constexpr int kMaxPlanEntries = 1024;
 
 // Ranges a query tile with `ntiles` key tiles is cut into.
 __host__ __device__ __forceinline__ int prefill_tile_splits(int ntiles, int splits) {
@@ -45,6 +56,8 @@ int prefill_smem_bytes();
 constexpr int64_t kPrefillRecordO = 128 * 64;
 constexpr int64_t kPrefillRecordML = 128 * 2;
 int launch_prefill_merge(const PrefillArgs& a, int items, cudaStream_t stream);
+int launch_prefill_plan(const PrefillArgs& a, cudaStream_t stream);
+int prefill_ctas_per_sm();
 int launch_prefill_tc(const PrefillArgs& a, const CUtensorMap& qmap, const CUtensorMap& kmap,
                       const CUtensorMap& vmap, int grid, cudaStream_t stream);
 
