@@ -225,3 +225,59 @@ def test_prefill_bad_table_sets_status():
                           bad.to(DEV), cu.to(DEV), ctx.to(DEV), 0.125, max_query_len=40)
     with pytest.raises(RuntimeError, match="block table"):
         ops.take_status()
+
+
+def _prefill_launches(chunks, priors, max_query_len=None, seed=3):
+    q, k, v, tables, bt, cu, ctx = mixed_prefill_batch(chunks, priors, seed=seed)
+    args = (q.bfloat16().to(DEV), k.bfloat16().to(DEV), v.bfloat16().to(DEV), bt.to(DEV),
+            cu.to(DEV), ctx.to(DEV), 0.125)
+    mq = max_query_len or max(chunks)
+    ops.prefill_attention(*args, max_query_len=mq)  # workspace sized outside the count
+    torch.cuda.synchronize(DEV)
+    before = ops.kernel_launches()
+    out = ops.prefill_attention(*args, max_query_len=mq)
+    torch.cuda.synchronize(DEV)
+    assert ops.take_status() == 0
+    check_all_rows(out, fp32_reference(q, k, v, tables, chunks, priors, 7, 0.125))
+    return ops.kernel_launches() - before
+
+
+def test_prefill_launch_policy():
+    # Query tiles (chunks x heads x 128-token tiles) below the SM count: key
+    # ranges split, merged by a second kernel.  Up to one wave of resident CTAs
+    # (two per SM): the prefill kernel alone.  More than a wave: a planning
+    # kernel ranks the tiles first.
+    sms = torch.cuda.get_device_properties(DEV).multi_processor_count
+    small = ([300], [2000])                   # 14 x 3 = 42 tiles
+    one_wave = ([200] * 8, [64 * i for i in range(8)])   # 8 x 14 x 2 = 224 tiles
+    large = ([512] * 8, [3485, 2609, 2094, 1105, 1261, 167, 308, 67])  # 448 tiles
+    assert 42 < sms <= 224 <= 2 * sms < 448
+    base = _prefill_launches(*one_wave)
+    assert _prefill_launches(*small) == base + 1
+    assert _prefill_launches(*large) == base + 1
+
+
+def test_planned_prefill_bad_table_sets_status():
+    # The planned path reads each row from its plan entry; a bad block-table
+    # entry is still reported, not read.
+    chunks, priors = [512] * 8, [700, 9, 1500, 300, 64, 2048, 5, 900]
+    q, k, v, tables, bt, cu, ctx = mixed_prefill_batch(chunks, priors, seed=12)
+    bad = bt.clone()
+    bad[5, 7] = k.size(1) + 11
+    ops.prefill_attention(q.bfloat16().to(DEV), k.bfloat16().to(DEV), v.bfloat16().to(DEV),
+                          bad.to(DEV), cu.to(DEV), ctx.to(DEV), 0.125, max_query_len=512)
+    with pytest.raises(RuntimeError, match="block table"):
+        ops.take_status()
+
+
+def test_planned_prefill_chunk_longer_than_max_query_len_sets_status():
+    # 12 chunks x 14 heads x 2 tiles: a planned launch; chunk 3 holds more
+    # tokens than max_query_len allows.
+    chunks = [256] * 12
+    chunks[3] = 300
+    priors = [37 * i for i in range(12)]
+    q, k, v, tables, bt, cu, ctx = mixed_prefill_batch(chunks, priors, seed=13)
+    ops.prefill_attention(q.bfloat16().to(DEV), k.bfloat16().to(DEV), v.bfloat16().to(DEV),
+                          bt.to(DEV), cu.to(DEV), ctx.to(DEV), 0.125, max_query_len=256)
+    with pytest.raises(RuntimeError, match="context length"):
+        ops.take_status()
