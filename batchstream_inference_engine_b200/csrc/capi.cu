@@ -184,13 +184,17 @@ int prefill_splits(int64_t items, int sms) {
   return static_cast<int>(std::min<int64_t>(std::max<int64_t>(want, 1), bsb::kMaxPrefillSplits));
 }
 
-// Rows x query tiles whose work the plan kernel ranks (0: no plan): only for
-// grids of more than one wave of resident CTAs (inside one wave the order does
-// not matter), and plans one CTA ranks (rts * max(splits, 2) entries at most).
-int64_t prefill_plan_rts(int64_t num_rows, int64_t qtiles, int64_t heads, int splits, int sms) {
+// Rows x query tiles whose work the plan kernel ranks (0: no plan): only when
+// the query tiles that hold tokens — at most ceil(num_tokens / 128) + num_rows
+// of the rows x ceil(max_query_len / 128) launched, the rest exit at once —
+// are more than one wave of resident CTAs (inside one wave the order does not
+// matter), and for plans one CTA ranks (rts * max(splits, 2) entries at most).
+int64_t prefill_plan_rts(int64_t num_rows, int64_t qtiles, int64_t num_tokens, int64_t heads,
+                         int splits, int sms) {
   const int64_t rts = num_rows * qtiles;
+  const int64_t busy = std::min(rts, (num_tokens + 127) / 128 + num_rows);
   const int64_t slots = static_cast<int64_t>(sms) * bsb::prefill_ctas_per_sm();
-  if (rts <= 0 || rts * heads * splits <= slots ||
+  if (rts <= 0 || busy * heads * splits <= slots ||
       rts * std::max(splits, 2) > bsb::kMaxPlanEntries) {
     return 0;
   }
@@ -615,7 +619,7 @@ int bs_prefill_attention_workspace_bytes(int64_t num_tokens, int64_t num_rows,
   const int64_t qtiles = (max_query_len + 127) / 128;
   const int64_t items = num_rows * num_heads * qtiles;
   const int splits = prefill_splits(items, d->sms);
-  const int64_t rts = prefill_plan_rts(num_rows, qtiles, num_heads, splits, d->sms);
+  const int64_t rts = prefill_plan_rts(num_rows, qtiles, num_tokens, num_heads, splits, d->sms);
   need = std::max(need, prefill_ws_bytes(items, splits, rts * splits));
   *bytes_out = static_cast<uint64_t>(need);
   return BS_OK;
@@ -704,7 +708,8 @@ int bs_prefill_attention(const void* query, int64_t query_token_stride, const in
     const int64_t wsb = static_cast<int64_t>(workspace_bytes);
     p.splits = prefill_splits(items, d->sms);
     if (wsb < prefill_ws_bytes(items, p.splits, 0)) p.splits = 1;
-    int64_t rts = prefill_plan_rts(num_rows, p.qtiles, num_heads, p.splits, d->sms);
+    int64_t rts =
+        prefill_plan_rts(num_rows, p.qtiles, num_tokens, num_heads, p.splits, d->sms);
     if (wsb < prefill_ws_bytes(items, p.splits, rts * p.splits)) rts = 0;
     float* records = reinterpret_cast<float*>(ws + prefill_split_offset());
     p.part_o = records;
