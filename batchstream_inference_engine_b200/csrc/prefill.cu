@@ -682,10 +682,9 @@ __global__ void __launch_bounds__(kPlanThreads) prefill_plan_kernel(const Prefil
   // row's first token, query tokens, context and block-table row.
   __shared__ int4 s_row[kMaxPlanEntries / 2];
   __shared__ int32_t s_size[kMaxPlanEntries];  // per slot rt * splits + piece, -1 unused
-  __shared__ int32_t s_cnt[kPlanThreads / 32];
   pdl_trigger();  // the prefill CTAs may take their SMs and wait for the plan
   pdl_wait();     // cu_q and context_lens come from the kernels just ahead
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int tid = threadIdx.x;
   const int R = a.num_rows, Q = a.qtiles, S = a.splits;
   const int n_slot = R * Q * S;  // <= kMaxPlanEntries (host)
 
@@ -713,11 +712,11 @@ __global__ void __launch_bounds__(kPlanThreads) prefill_plan_kernel(const Prefil
     if (p < k) size = (p + 1) * tiles / k - p * tiles / k;
     s_size[tid] = size;
   }
-  const unsigned valid = __ballot_sync(0xffffffffu, size >= 0);
-  if (lane == 0) s_cnt[warp] = __popc(valid);
-  __syncthreads();
+  const int entries = __syncthreads_count(size >= 0);
+  if (tid == 0) a.plan[0] = make_int4(entries, 0, 0, 0);
   if (size >= 0) {
     int rank = 0;
+#pragma unroll 8
     for (int f = 0; f < n_slot; ++f) {
       const int g = s_size[f];
       rank += (g > size || (g == size && f < tid)) ? 1 : 0;
@@ -725,11 +724,6 @@ __global__ void __launch_bounds__(kPlanThreads) prefill_plan_kernel(const Prefil
     const int4 row = s_row[tid / S];
     a.plan[1 + 2 * rank] = make_int4(tid, row.x, row.y, row.z);
     a.plan[2 + 2 * rank] = make_int4(row.w, 0, 0, 0);
-  }
-  if (tid == 0) {
-    int entries = 0;
-    for (int w = 0; w < kPlanThreads / 32; ++w) entries += s_cnt[w];
-    a.plan[0] = make_int4(entries, 0, 0, 0);
   }
 }
 
