@@ -556,29 +556,38 @@ def run_decode(args):
     hdelta = torch.stack([torch.arange(B, dtype=torch.int64) * width,
                           torch.tensor([b - 1 for b in blocks], dtype=torch.int64)]).pin_memory()
     hout = torch.empty((B, H, D), dtype=torch.bfloat16).pin_memory()
-    dq, dk, dv = torch.empty_like(q[0]), torch.empty_like(k_new[0]), torch.empty_like(v_new[0])
-    dstart = torch.empty_like(start_pos)
-    ddelta = torch.empty((2, B), dtype=torch.int64, device=dev)
+    # Two device sets of inputs and outputs: a step computes on one while the
+    # next step's inputs arrive in, and the last step's result leaves, the other.
+    dq = [torch.empty_like(q[0]) for _ in range(2)]
+    dk = [torch.empty_like(k_new[0]) for _ in range(2)]
+    dv = [torch.empty_like(v_new[0]) for _ in range(2)]
+    dstart = [torch.empty_like(start_pos) for _ in range(2)]
+    ddelta = [torch.empty((2, B), dtype=torch.int64, device=dev) for _ in range(2)]
+    dout = [torch.empty_like(out) for _ in range(2)]
     e2e_table = tables[0].clone()
     last_col = torch.tensor([b - 1 for b in blocks], device=dev)
     last_entry = e2e_table[torch.arange(B, device=dev), last_col].to(torch.int64)
     h2d = sum(t.numel() * t.element_size() for t in (hq, hk, hv, hstart, hdelta))
     d2h = hout.numel() * hout.element_size()
 
-    def e2e_step():
-        dq.copy_(hq, non_blocking=True)
-        dk.copy_(hk, non_blocking=True)
-        dv.copy_(hv, non_blocking=True)
-        dstart.copy_(hstart, non_blocking=True)
-        ddelta.copy_(hdelta, non_blocking=True)
-        flat = e2e_table.view(-1)
-        flat.index_copy_(0, ddelta[0] + ddelta[1], last_entry.to(torch.int32))
-        ctx, _ = ops.decode_append(dk, dv, k_pool, v_pool, e2e_table, dstart)
-        ops.paged_attention_batched(dq, k_pool, v_pool, e2e_table, ctx, scale, out=out,
-                                    units_hint=units)
-        hout.copy_(out, non_blocking=True)
+    def copy_in(b):
+        dq[b].copy_(hq, non_blocking=True)
+        dk[b].copy_(hk, non_blocking=True)
+        dv[b].copy_(hv, non_blocking=True)
+        dstart[b].copy_(hstart, non_blocking=True)
+        ddelta[b].copy_(hdelta, non_blocking=True)
 
-    e2e_ms = time_e2e(e2e_step, args, dev, world)
+    def compute(b):
+        flat = e2e_table.view(-1)
+        flat.index_copy_(0, ddelta[b][0] + ddelta[b][1], last_entry.to(torch.int32))
+        ctx, _ = ops.decode_append(dk[b], dv[b], k_pool, v_pool, e2e_table, dstart[b])
+        ops.paged_attention_batched(dq[b], k_pool, v_pool, e2e_table, ctx, scale, out=dout[b],
+                                    units_hint=units)
+
+    def copy_out(b):
+        hout.copy_(dout[b], non_blocking=True)
+
+    e2e_ms = time_e2e(copy_in, compute, copy_out, args, dev, world)
     ops.take_status(dev)
 
     (total_ms, e2e_ms, decode_ms), (job_bytes,) = max_over_ranks(
@@ -627,7 +636,8 @@ def run_decode(args):
             "e2e": {"value": round(job_bytes * args.steps / (e2e_ms / 1e3) / 1e9, 1),
                     "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "ms_per_step": round(e2e_ms / args.steps, 4),
-                    "path": "pinned host -> device, decode append + decode, device -> pinned host"},
+                    "path": "pinned host -> device, decode append + decode, device -> pinned host; "
+                            "two buffer sets, the next step's copies overlap this step's kernels"},
             "gpu_launches": replayed_launches(step_counts, args.steps),
             "clocks": clock,
         }
@@ -640,24 +650,66 @@ def run_decode(args):
         print(json.dumps(result), flush=True)
 
 
-def time_e2e(step, args, dev, world):
-    """Device time of `steps` end-to-end steps after `warmup` untimed ones."""
+def time_e2e(copy_in, compute, copy_out, args, dev, world):
+    """Device time of `steps` end-to-end steps after `warmup` untimed ones.
+
+    A step's inputs come from pinned host memory (`copy_in(b)` into device set
+    b), the public API calls run on them (`compute(b)`), and the result goes back
+    to pinned host memory (`copy_out(b)`).  As a serving loop would, consecutive
+    steps alternate between two device sets and overlap: one CUDA graph per set
+    runs, in parallel branches, compute(b), copy_in(1 - b) (the next step's
+    inputs) and copy_out(1 - b) (the previous step's result).  Graph replays run
+    one after another, so the branches never share a buffer; every timed step
+    moves one step's input and output bytes across PCIe."""
     import torch
     import torch.distributed as dist
 
+    from batchstream_inference_engine_b200 import ops
+
     stream = torch.cuda.current_stream(dev)
-    for _ in range(args.warmup):
-        step()
+    cap = torch.cuda.Stream(dev)
+    xin, xout = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+    cap.wait_stream(stream)
+    with torch.cuda.stream(cap):
+        for i in range(max(args.warmup, 2)):
+            copy_in(i % 2)
+            compute(i % 2)
+            copy_out(i % 2)
+        ops.take_status(dev)
+    torch.cuda.synchronize(dev)
+    graphs = []
+    for b in range(2):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=cap):
+            xin.wait_stream(cap)
+            xout.wait_stream(cap)
+            with torch.cuda.stream(xin):
+                copy_in(1 - b)
+            with torch.cuda.stream(xout):
+                copy_out(1 - b)
+            compute(b)
+            cap.wait_stream(xin)
+            cap.wait_stream(xout)
+        graphs.append(g)
+    torch.cuda.synchronize(dev)
+    with torch.cuda.stream(cap):
+        copy_in(0)  # the first replayed step's inputs
+    torch.cuda.synchronize(dev)
+    for i in range(args.warmup):
+        graphs[i % 2].replay()
     torch.cuda.synchronize(dev)
     if world > 1:
         dist.barrier()
     a0 = torch.cuda.Event(enable_timing=True)
     a1 = torch.cuda.Event(enable_timing=True)
     a0.record(stream)
-    for _ in range(args.steps):
-        step()
+    for i in range(args.steps):
+        graphs[(args.warmup + i) % 2].replay()
     a1.record(stream)
     torch.cuda.synchronize(dev)
+    with torch.cuda.stream(cap):
+        ops.take_status(dev)  # the captured kernels report through that stream's workspace
+    del graphs
     return a0.elapsed_time(a1)
 
 
@@ -734,23 +786,30 @@ def run_prefill(args):
     hv = v_new[0].cpu().pin_memory()
     hstart = start_pos.cpu().pin_memory()
     hout = torch.empty((T, H, D), dtype=torch.bfloat16).pin_memory()
-    dq, dk, dv = torch.empty_like(q[0]), torch.empty_like(k_new[0]), torch.empty_like(v_new[0])
-    dstart = torch.empty_like(start_pos)
+    dq = [torch.empty_like(q[0]) for _ in range(2)]
+    dk = [torch.empty_like(k_new[0]) for _ in range(2)]
+    dv = [torch.empty_like(v_new[0]) for _ in range(2)]
+    dstart = [torch.empty_like(start_pos) for _ in range(2)]
+    dout = [torch.empty_like(out) for _ in range(2)]
     h2d = sum(t.numel() * t.element_size() for t in (hq, hk, hv, hstart))
     d2h = hout.numel() * hout.element_size()
 
-    def e2e_step():
-        dq.copy_(hq, non_blocking=True)
-        dk.copy_(hk, non_blocking=True)
-        dv.copy_(hv, non_blocking=True)
-        dstart.copy_(hstart, non_blocking=True)
-        cu, _, slots, ctx = ops.step_metadata(tables[0], dstart, n_new, T, BLOCK, nb)
-        ops.reshape_and_cache(dk, dv, k_pool, v_pool, slots)
-        ops.prefill_attention(dq, k_pool, v_pool, tables[0], cu, ctx, scale, max_query_len=n,
-                              out=out)
-        hout.copy_(out, non_blocking=True)
+    def copy_in(b):
+        dq[b].copy_(hq, non_blocking=True)
+        dk[b].copy_(hk, non_blocking=True)
+        dv[b].copy_(hv, non_blocking=True)
+        dstart[b].copy_(hstart, non_blocking=True)
 
-    e2e_ms = time_e2e(e2e_step, args, dev, world)
+    def compute(b):
+        cu, _, slots, ctx = ops.step_metadata(tables[0], dstart[b], n_new, T, BLOCK, nb)
+        ops.reshape_and_cache(dk[b], dv[b], k_pool, v_pool, slots)
+        ops.prefill_attention(dq[b], k_pool, v_pool, tables[0], cu, ctx, scale, max_query_len=n,
+                              out=dout[b])
+
+    def copy_out(b):
+        hout.copy_(dout[b], non_blocking=True)
+
+    e2e_ms = time_e2e(copy_in, compute, copy_out, args, dev, world)
     ops.take_status(dev)
 
     (total_ms, e2e_ms, kernel_ms), (job_flops,) = max_over_ranks(
@@ -795,8 +854,8 @@ def run_prefill(args):
             "e2e": {"value": round(job_flops * args.steps / (e2e_ms / 1e3) / 1e12, 2),
                     "unit": "TFLOP/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "ms_per_step": round(e2e_ms / args.steps, 4),
-                    "path": "pinned host -> device, metadata + slot write + prefill, "
-                            "device -> pinned host"},
+                    "path": "pinned host -> device, metadata + slot write + prefill, device -> "
+                            "pinned host; two buffer sets, the next step's copies overlap this step's kernels"},
             "gpu_launches": replayed_launches([g[3] for g in graphs], args.steps),
             "clocks": clock,
         }
