@@ -132,9 +132,11 @@ def algorithmic_bytes(lens, heads, kv_heads, head_dim) -> int:
 
 
 def prefill_priors(n_gpus: int, rank: int) -> np.ndarray:
-    """Prior context of each rank's chunks (rank 0: default_rng(0)'s first 8)."""
-    pri = np.random.default_rng(0).integers(0, 4097, PREFILL_CHUNKS * n_gpus)
-    return pri[rank * PREFILL_CHUNKS:(rank + 1) * PREFILL_CHUNKS].astype(np.int64)
+    """Prior context of each rank's chunks: default_rng(0)'s first 8 draws on
+    every rank (weak scaling: the same work per GPU), their order rotated by
+    the rank."""
+    pri = np.random.default_rng(0).integers(0, 4097, PREFILL_CHUNKS)
+    return np.roll(pri, rank).astype(np.int64)
 
 
 def prefill_flops(priors, heads, head_dim, n=PREFILL_CHUNK) -> int:
@@ -833,7 +835,8 @@ def run_prefill(args):
             "data": "synthetic (seeded priors, N(0,1) K/V/q, random block tables)",
             "config": {
                 "workload": f"{args.workload}: {R} prompt chunks x {n} tokens per GPU after prior "
-                            f"paged context U[0, 4096], {H}q/{Hkv}kv d{D}, block 16, one layer",
+                            f"paged context U[0, 4096] (the same 8 priors on every rank, order "
+                            f"rotated by rank), {H}q/{Hkv}kv d{D}, block 16, one layer",
                 "priors_rank0": [int(p) for p in prefill_priors(world, 0)],
                 "l2": f"inputs larger than L2: {rot} rotating batches with disjoint tables",
                 "step": "step metadata + K/V slot write + chunked-prefill attention",
