@@ -4,7 +4,7 @@ CPU restatement of the BatchStream reference's paged-attention arithmetic
 (plain C in ``paged_attention_oracle.c``, loaded through ctypes) plus a pure
 Python restatement of its block allocator.  Only ``tests/``,
 ``__graft_entry__.smoke()`` and the CPU-baseline leg of ``bench.py`` may import
-this package, and only as the checker or the timed CPU baseline.
+this package, and only as the parity reference or the timed CPU baseline.
 
 Pinning: the golden fixtures under ``tests/golden/`` were produced by the
 reference itself (its compiled C++ op and its Python op, see
