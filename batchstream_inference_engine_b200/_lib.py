@@ -29,6 +29,8 @@ EXPORTS = (
     "bs_decode_append",
     "bs_step_metadata",
     "bs_take_status",
+    "bs_reset_workspace",
+    "bs_set_wait_probe",
     "bs_rms_norm",
     "bs_rope_append",
     "bs_silu_mul",
@@ -87,6 +89,8 @@ _SIGNATURES = {
         ctypes.c_int,
     ),
     "bs_take_status": ([_p, _p, ctypes.POINTER(ctypes.c_uint32)], ctypes.c_int),
+    "bs_reset_workspace": ([_p, _p], ctypes.c_int),
+    "bs_set_wait_probe": ([_i32, _u64], ctypes.c_int),
     "bs_rms_norm": (
         [_p, _i64, _i64, _p, _i64, _p, _p, _i64, _i64, _dbl, _i32, _p, _i64, _p, _i64, _p, _p],
         ctypes.c_int,

@@ -66,6 +66,10 @@ std::atomic<uint64_t> g_launches{0};
 
 void count_launches(int n) { g_launches.fetch_add(static_cast<uint64_t>(n)); }
 
+// Settings of bs_set_wait_probe, read at each decode launch (test use only).
+std::atomic<uint64_t> g_wait_limit_ns{0};
+std::atomic<int32_t> g_probe_unarmed{0};
+
 int fail(int code, const char* fmt, ...) {
   char buf[512];
   va_list ap;
@@ -340,6 +344,7 @@ int launch_decode(bsb::DecodeArgs& a, int32_t dtype, int grid, cudaStream_t stre
                   bsb::MergeTask* tasks) {
   const bool mma = use_mma_path(dtype, a.block_size, a.head_dim, a.groups);
   a.tasks = mma ? tasks : nullptr;
+  bsb::apply_wait_probe(a);
   int rc;
   if (mma) {
     CUtensorMap kmap, vmap;
@@ -1016,9 +1021,42 @@ int bs_take_status(void* workspace, void* stream, uint32_t* status_out) {
   return BS_ERR_DEVICE;
 }
 
+int bs_reset_workspace(void* workspace, void* stream) {
+  BS_CHECK(workspace != nullptr, "workspace is null");
+  const cudaError_t e = cudaMemsetAsync(workspace, 0,
+                                        static_cast<size_t>(ws_layout(0, 0, 0, 0).staging),
+                                        static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "clearing the workspace counters");
+  return BS_OK;
+}
+
+int bs_set_wait_probe(int32_t unarmed, uint64_t wait_limit_ns) {
+  g_wait_limit_ns.store(wait_limit_ns);
+  g_probe_unarmed.store(unarmed != 0 ? 1 : 0);
+  return BS_OK;
+}
+
 }  // extern "C"
 
 namespace bsb {
 // Lets other translation units of the library report through bs_last_error().
 void set_last_error(const char* message) { g_error = message; }
+
+void apply_wait_probe(DecodeArgs& a) {
+  a.wait_limit_ns = g_wait_limit_ns.load(std::memory_order_relaxed);
+  a.probe_unarmed = g_probe_unarmed.load(std::memory_order_relaxed);
+}
+
+// The decode grid and kernel choice of the workspace entry points, shared with
+// the allocation-free one (noalloc.cu) so the two cannot drift apart.
+bool decode_uses_mma(int32_t dtype, int64_t block_size, int64_t head_dim, int64_t groups) {
+  return use_mma_path(dtype, block_size, head_dim, groups);
+}
+int decode_grid_for(bool mma, int32_t dtype, int64_t head_dim, int64_t groups, int* grid) {
+  return decode_grid(mma, dtype, head_dim, groups, grid);
+}
+int32_t decode_record_stride(int64_t groups, int64_t head_dim) {
+  return record_stride(groups, head_dim);
+}
+void add_kernel_launches(int n) { count_launches(n); }
 }  // namespace bsb

@@ -99,12 +99,14 @@ __device__ __forceinline__ bool mbar_try_wait_suspend(uint64_t* bar, uint32_t pa
 constexpr uint64_t kWaitLimitNs = 2000000000ull;
 constexpr uint32_t kSuspendNs = 20000;
 
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
+                                          uint64_t limit_ns = kWaitLimitNs) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t start = global_timer_ns();
+  const uint32_t hint = limit_ns < kSuspendNs ? static_cast<uint32_t>(limit_ns) : kSuspendNs;
   for (uint32_t i = 1; i < kSpinLimit; ++i) {
-    if (mbar_try_wait_suspend(bar, parity, kSuspendNs)) return true;
-    if (global_timer_ns() - start > kWaitLimitNs) return false;
+    if (mbar_try_wait_suspend(bar, parity, hint)) return true;
+    if (global_timer_ns() - start > limit_ns) return false;
   }
   return false;
 }
@@ -251,6 +253,22 @@ __device__ __forceinline__ void pdl_trigger() {
 // Consumer-only named barrier (id 1); the producer warp never joins it.
 __device__ __forceinline__ void named_barrier_sync(uint32_t id, uint32_t threads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+
+// Function attributes (dynamic shared memory above 48 KiB, carveout) belong to
+// the device that was current when they were set: a process that drives several
+// GPUs sets them once on each.  `done` holds one bit per device ordinal.
+template <typename SetFn>
+inline cudaError_t once_per_device(unsigned long long* done, SetFn&& set) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev >= 64) return set();  // no bit to remember it by: set it every time
+  const unsigned long long bit = 1ull << dev;
+  if (__atomic_load_n(done, __ATOMIC_ACQUIRE) & bit) return cudaSuccess;
+  e = set();
+  if (e == cudaSuccess) __atomic_fetch_or(done, bit, __ATOMIC_ACQ_REL);
+  return e;
 }
 
 }  // namespace bsb

@@ -64,7 +64,17 @@ struct DecodeArgs {
   // by decode_merge_kernel after the decode kernel instead of by the last CTA
   // to finish (atomic counters).
   MergeTask* tasks;
+  // Limit of each pipeline wait of the tensor-core kernel (0: kWaitLimitNs).
+  uint64_t wait_limit_ns;
+  // Test hook of the bounded-wait error path (bs_set_wait_probe): when set,
+  // warp 0 of CTA 0 never arms or fills its stages, so its first wait runs
+  // out with no copy in flight.  Zero in every production call.
+  int32_t probe_unarmed;
 };
+
+// Applies the process-wide wait settings of bs_set_wait_probe (capi.cu) to a
+// launch.
+void apply_wait_probe(DecodeArgs& a);
 
 // Units of a sequence from its raw length and table row (already loaded);
 // invalid ones count as 0 units with len = 0.

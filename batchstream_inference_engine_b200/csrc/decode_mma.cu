@@ -151,7 +151,12 @@ __global__ void __maxnreg__((Cfg<D, G16>::MAX_REGS))
     nxt_row = starts.nrow[warp];
   }
 
-  auto issue = [&](int stage) {
+  // Stages holding a copy that was started and not yet waited for (bit s).
+  uint32_t armed = 0;
+  // The probe hook leaves this warp's stages unarmed (see DecodeArgs).
+  const bool probe = a.probe_unarmed != 0 && blockIdx.x == 0 && warp == 0;
+  // `dry`: metadata only, no copy (the walk after a wait gave up).
+  auto issue = [&](int stage, bool dry) {
     const int32_t* table = a.block_tables + static_cast<int64_t>(crow) * a.bt_stride;
     // The window caches up to 32 entries of one table row, filled to the row's
     // width rather than this sequence's block count: sequences that share a row
@@ -168,7 +173,7 @@ __global__ void __maxnreg__((Cfg<D, G16>::MAX_REGS))
     const bool last = (cu == wr1 - 1) || (cb == cnb - 1);
     const bool whole = seg_unit >= wr0 && seg_unit + cnb <= wr1;
     if (lane == 0) {
-      if (!valid) set_status(a.status, kStatusBadBlock);
+      if (!valid && !dry) set_status(a.status, kStatusBadBlock);
       TileMeta& m = meta[warp][stage];
       m.seq = ci;
       m.kvh = ch;
@@ -178,6 +183,8 @@ __global__ void __maxnreg__((Cfg<D, G16>::MAX_REGS))
                 (seg_unit > wr0 ? kSlot1 : 0);
       m.nb = cnb;
       m.seg_unit = seg_unit;
+    }
+    if (lane == 0 && !dry && !probe) {
       uint8_t* st = wst + stage * C::STAGE_BYTES;
       const uint32_t bytes = (valid ? 2u * C::BLOCK_BYTES : 0u) + (first ? G * D * 2u : 0u);
       mbar_arrive_expect_tx(&full_bar[warp][stage], bytes);
@@ -199,6 +206,7 @@ __global__ void __maxnreg__((Cfg<D, G16>::MAX_REGS))
         bulk_load(st + 2 * C::BLOCK_BYTES, qsrc, G * D * 2u, &full_bar[warp][stage]);
       }
     }
+    if (!dry && !probe) armed |= 1u << stage;
     // Advance to the next unit.
     ++cu;
     if (++cb == cnb) {
@@ -224,10 +232,10 @@ __global__ void __maxnreg__((Cfg<D, G16>::MAX_REGS))
   if (early_loads) {
     // Stages up to (not including) the first block that ends a segment: the
     // append ahead may still be writing that one.
-    for (; issued < S && issued < ntiles && cb != cnb - 1; ++issued) issue(issued);
+    for (; issued < S && issued < ntiles && cb != cnb - 1; ++issued) issue(issued, false);
     pdl_wait();
   }
-  for (; issued < S && issued < ntiles; ++issued) issue(issued);
+  for (; issued < S && issued < ntiles; ++issued) issue(issued, false);
 
   // ---------------------------------------------------------------- compute
   const int g = lane >> 2, t = lane & 3;
@@ -237,16 +245,31 @@ __global__ void __maxnreg__((Cfg<D, G16>::MAX_REGS))
   float o[NTILES][4];
   float m2[2] = {-INFINITY, -INFINITY}, lsum[2] = {0.f, 0.f};
   const float scale = a.scale;
+  const uint64_t limit = a.wait_limit_ns != 0 ? a.wait_limit_ns : kWaitLimitNs;
+  // After a wait gave up the warp walks the rest of its span without data: it
+  // still parks (empty) portions, so the CTA merge and the per-segment counters
+  // of the launch see every portion they expect and end in their usual state.
+  bool dry = false;
 
   for (int32_t it = 0; it < ntiles; ++it) {
     const int stage = it % S;
     const uint32_t phase = (it / S) & 1;
     // Warp-uniform outcome: a lone lane leaving here would strand the others
     // at the warp-collective ldmatrix / mma.sync below.
-    if (!__all_sync(0xffffffffu, mbar_wait(&full_bar[warp][stage], phase))) {
+    if (!dry && !__all_sync(0xffffffffu, mbar_wait(&full_bar[warp][stage], phase, limit))) {
       if (lane == 0) set_status(a.status, kStatusWaitTimeout);
-      break;
+      // Wait (with the full limit) for the copies this warp started: none may
+      // still be writing its stages when they are reused or the CTA exits.
+      if (lane == 0) {
+        for (int32_t j = it; j < it + S && j < ntiles; ++j) {
+          if (armed & (1u << (j % S))) mbar_wait(&full_bar[warp][j % S], (j / S) & 1);
+        }
+      }
+      armed = 0;
+      dry = true;
+      __syncwarp();
     }
+    armed &= ~(1u << stage);
     const TileMeta mt = meta[warp][stage];
     const uint8_t* st = wst + stage * C::STAGE_BYTES;
     if (mt.flags & kFirst) {
@@ -254,6 +277,8 @@ __global__ void __maxnreg__((Cfg<D, G16>::MAX_REGS))
       lsum[0] = lsum[1] = 0.f;
 #pragma unroll
       for (int n = 0; n < NTILES; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
+    }
+    if (!dry && (mt.flags & kFirst)) {
       const uint32_t* sq = reinterpret_cast<const uint32_t*>(st + 2 * C::BLOCK_BYTES);
 #pragma unroll
       for (int kk = 0; kk < KSTEPS; ++kk) {
@@ -266,7 +291,7 @@ __global__ void __maxnreg__((Cfg<D, G16>::MAX_REGS))
         qa[kk][3] = (G16 && g + 8 < G) ? sq[w1 + 4] : 0u;
       }
     }
-    {
+    if (!dry) {
       const int tok0 = mt.blk * kBS;
       const int valid = min(kBS, mt.len - tok0);
       const uint32_t kbase = smem_u32(st);
@@ -361,7 +386,7 @@ __global__ void __maxnreg__((Cfg<D, G16>::MAX_REGS))
     __syncwarp();
     if (it + S < ntiles) {
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-      issue(stage);
+      issue(stage, dry);
     }
 
     if (mt.flags & kLast) {
@@ -531,14 +556,12 @@ template <int D, bool G16>
 int launch_one(const DecodeArgs& a, const CUtensorMap& kmap, const CUtensorMap& vmap, int grid,
                cudaStream_t stream) {
   using C = Cfg<D, G16>;
-  static bool configured = false;
-  if (!configured) {
-    cudaError_t e = cudaFuncSetAttribute(decode_mma_kernel<D, G16>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         C::SMEM_BYTES);
-    if (e != cudaSuccess) return static_cast<int>(e);
-    configured = true;
-  }
+  static unsigned long long configured = 0;  // one bit per device
+  cudaError_t e = once_per_device(&configured, [] {
+    return cudaFuncSetAttribute(decode_mma_kernel<D, G16>,
+                                cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
+  });
+  if (e != cudaSuccess) return static_cast<int>(e);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
   cfg.blockDim = dim3(C::W * 32);
@@ -595,12 +618,17 @@ int launch_decode_mma(const DecodeArgs& a, const CUtensorMap& kmap, const CUtens
   // Merge pass: at most `grid` records per segment.
   const int smem = static_cast<int>((2 * static_cast<int64_t>(grid) * a.groups + 2 * a.groups) *
                                     sizeof(float));
-  static int configured_smem = 0;
-  if (smem > configured_smem) {
-    cudaError_t e = cudaFuncSetAttribute(decode_merge_kernel,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  // The attribute is per device: set it on the current one whenever the
+  // size grows past what that device was given.
+  static int configured_smem[64] = {};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return static_cast<int>(e);
+  if (dev >= 64 || smem > configured_smem[dev]) {
+    e = cudaFuncSetAttribute(decode_merge_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             smem);
     if (e != cudaSuccess) return static_cast<int>(e);
-    configured_smem = smem;
+    if (dev < 64) configured_smem[dev] = smem;
   }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);

@@ -11,10 +11,10 @@
 // GPU as soon as the library's kernels are loaded on it, and is never freed
 // before the process exits.
 //
-// Limits: at most kMaxSegments (sequence, kv head) pairs per call and
-// kScratchBytes of scratch in total (status word, segment counters, partial
-// records of the persistent grid); bigger calls are rejected with an error
-// message.  Every call uses the same array, so calls that overlap on the GPU
+// Limits: at most kMaxSegments (sequence, kv head) pairs per call (bigger calls
+// are rejected with an error message) and kScratchBytes of scratch in total
+// (status word, segment counters, two partial records per CTA: a shape whose
+// records for the regular grid do not fit runs on fewer CTAs).  Every call uses the same array, so calls that overlap on the GPU
 // (two streams, two threads) race and must be serialised by the caller.
 #include <cuda.h>
 #include <cuda_runtime.h>
@@ -29,7 +29,13 @@
 #include "decode.cuh"
 
 namespace bsb {
-void set_last_error(const char* message);  // capi.cu
+// capi.cu: messages, launch count and the workspace entry points' choice of
+// kernel and grid, which this entry point shares.
+void set_last_error(const char* message);
+void add_kernel_launches(int n);
+bool decode_uses_mma(int32_t dtype, int64_t block_size, int64_t head_dim, int64_t groups);
+int decode_grid_for(bool mma, int32_t dtype, int64_t head_dim, int64_t groups, int* grid);
+int32_t decode_record_stride(int64_t groups, int64_t head_dim);
 }  // namespace bsb
 
 namespace {
@@ -58,9 +64,6 @@ int noalloc_fail(int code, const char* fmt, ...) {
 
 struct DeviceScratch {
   uint8_t* base = nullptr;  // device address of g_noalloc_scratch on that GPU
-  int sms = 0;
-  int occ[2][2] = {{0, 0}, {0, 0}};  // tensor-core kernel: [d128][g16]
-  int occ_simt[2] = {0, 0};          // SIMT kernel: [bf16]
 };
 
 std::mutex g_mu;
@@ -87,10 +90,6 @@ int scratch_for_current_device(DeviceScratch** out) {
     if (e == cudaSuccess) e = cudaDeviceSynchronize();
     if (e != cudaSuccess) {
       return noalloc_fail(BS_ERR_CUDA, "clearing the scratch array: %s", cudaGetErrorString(e));
-    }
-    e = cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, dev);
-    if (e != cudaSuccess) {
-      return noalloc_fail(BS_ERR_CUDA, "cudaDeviceGetAttribute: %s", cudaGetErrorString(e));
     }
     d.base = static_cast<uint8_t*>(p);
   }
@@ -170,12 +169,16 @@ extern "C" int bs_paged_attention_batched_noalloc(
                         static_cast<long long>(num_seqs * num_kv_heads),
                         static_cast<long long>(kMaxSegments));
   }
+  if (device_status == nullptr) {
+    // The array's own status word has no reader: without the caller's word a
+    // kernel-side problem would go unreported.
+    return noalloc_fail(BS_ERR_INVALID, "device_status must point to a device word");
+  }
   if (num_seqs == 0) return BS_OK;
   if (!query || !key_pool || !value_pool || !block_tables || !context_lens || !output) {
     return noalloc_fail(BS_ERR_INVALID, "null pointer argument");
   }
-  const bool mma =
-      dtype == BS_BF16 && block_size == 16 && (head_dim == 64 || head_dim == 128);
+  const bool mma = bsb::decode_uses_mma(dtype, block_size, head_dim, groups);
   if (mma && (!is_aligned16(query) || !is_aligned16(key_pool) || !is_aligned16(value_pool) ||
               (query_seq_stride * 2) % 16 != 0)) {
     return noalloc_fail(BS_ERR_INVALID, "query, pools and query rows must be 16-byte aligned");
@@ -183,28 +186,21 @@ extern "C" int bs_paged_attention_batched_noalloc(
 
   DeviceScratch* d = nullptr;
   if (int rc = scratch_for_current_device(&d)) return rc;
-  int occ = 0;
-  {
-    std::lock_guard<std::mutex> lock(g_mu);
-    int* slot = mma ? &d->occ[head_dim == 128][groups > 8] : &d->occ_simt[dtype == BS_BF16];
-    if (*slot == 0) {
-      *slot = mma ? bsb::decode_mma_ctas_per_sm(static_cast<int>(head_dim),
-                                                static_cast<int>(groups))
-                  : bsb::decode_simt_ctas_per_sm(static_cast<int>(head_dim),
-                                                 static_cast<int>(groups), dtype == BS_BF16);
-    }
-    occ = *slot;
-  }
-  if (occ <= 0) return noalloc_fail(BS_ERR_CUDA, "occupancy query for the decode kernel failed");
-  const int grid = d->sms * occ;
-  const int64_t rec_stride = ((groups * head_dim + 2 * groups) + 3) / 4 * 4;
-  const size_t records = size_t(2) * grid * rec_stride * sizeof(float);
-  if (kRecordsOffset + records > kScratchBytes) {
+  // The same kernel and persistent grid as bs_paged_attention_batched.
+  int grid = 0;
+  if (int rc = bsb::decode_grid_for(mma, dtype, head_dim, groups, &grid)) return rc;
+  const int64_t rec_stride = bsb::decode_record_stride(groups, head_dim);
+  // Two partial records per CTA.  Where the persistent grid's records do not
+  // fit the array, fewer CTAs run (the split points move; the answer does not).
+  const size_t per_cta = size_t(2) * rec_stride * sizeof(float);
+  const int64_t fit = static_cast<int64_t>((kScratchBytes - kRecordsOffset) / per_cta);
+  if (fit < 1) {
     return noalloc_fail(BS_ERR_UNSUPPORTED,
-                        "this shape needs %zu bytes of scratch; the allocation-free entry point "
-                        "holds %zu",
-                        kRecordsOffset + records, kScratchBytes);
+                        "this shape needs %zu bytes of scratch per CTA; the allocation-free entry "
+                        "point holds %zu",
+                        kRecordsOffset + per_cta, kScratchBytes);
   }
+  if (grid > fit) grid = static_cast<int>(fit);
 
   bsb::DecodeArgs a{};
   a.q = query;
@@ -230,8 +226,9 @@ extern "C" int bs_paged_attention_batched_noalloc(
   a.partials = reinterpret_cast<float*>(d->base + kRecordsOffset);
   a.rec_stride = static_cast<int32_t>(rec_stride);
   a.seg_counters = reinterpret_cast<int32_t*>(d->base + kStatusBytes);
-  a.status = device_status != nullptr ? device_status : reinterpret_cast<uint32_t*>(d->base);
+  a.status = device_status;
   a.lens_ready = 0;
+  bsb::apply_wait_probe(a);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   int rc;
   if (mma) {
@@ -247,5 +244,6 @@ extern "C" int bs_paged_attention_batched_noalloc(
     return noalloc_fail(BS_ERR_CUDA, "decode kernel launch: %s",
                         cudaGetErrorString(static_cast<cudaError_t>(rc)));
   }
+  bsb::add_kernel_launches(1);
   return BS_OK;
 }

@@ -747,17 +747,15 @@ int launch_prefill_merge(const PrefillArgs& a, int items, cudaStream_t stream) {
 namespace {
 
 int configure_prefill() {
-  static bool configured = false;
-  if (!configured) {
+  static unsigned long long configured = 0;  // one bit per device
+  return static_cast<int>(once_per_device(&configured, [] {
     cudaError_t e = cudaFuncSetAttribute(prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          kSmemBytes);
-    if (e != cudaSuccess) return static_cast<int>(e);
+    if (e != cudaSuccess) return e;
     // All of the unified L1 as shared memory: two CTAs per SM.
-    e = cudaFuncSetAttribute(prefill_kernel, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
-    if (e != cudaSuccess) return static_cast<int>(e);
-    configured = true;
-  }
-  return 0;
+    return cudaFuncSetAttribute(prefill_kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                100);
+  }));
 }
 
 }  // namespace

@@ -89,8 +89,20 @@ def take_status(device: torch.device | None = None) -> int:
     stream = torch.cuda.current_stream(device).cuda_stream
     ws = _workspaces.get(device, stream, 0)
     bits = ctypes.c_uint32(0)
-    check(lib().bs_take_status(ws.data_ptr(), stream, ctypes.byref(bits)))
+    rc = lib().bs_take_status(ws.data_ptr(), stream, ctypes.byref(bits))
+    if bits.value:
+        # A launch that reported a problem may have left segment counters set:
+        # clear them so that the next call on this workspace starts clean.
+        check(lib().bs_reset_workspace(ws.data_ptr(), stream))
+    check(rc)
     return bits.value
+
+
+def set_wait_probe(unarmed: bool, wait_limit_ns: int = 0) -> None:
+    """Test hook of the bounded-wait error path (bs_set_wait_probe): the wait
+    limit of the tensor-core decode kernel (0: the default of about 2 s) and,
+    with ``unarmed``, one warp that waits on stages nothing fills."""
+    check(lib().bs_set_wait_probe(1 if unarmed else 0, int(wait_limit_ns)))
 
 
 def decode_workspace_bytes(num_seqs: int, num_heads: int, num_kv_heads: int, head_dim: int,

@@ -57,13 +57,14 @@ enum bs_error {
 /* Message of the last failing call on this thread ("" if none). */
 const char* bs_last_error(void);
 
-/* Library version string. */
 /*
  * Kernels this library has launched in this process (each successful entry
  * adds the kernels it enqueued, e.g. 2 for a tensor-core decode with its merge
  * pass).  A launch recorded into a CUDA graph counts once at capture.
  */
 uint64_t bs_kernel_launches(void);
+
+/* Library version string. */
 const char* bs_version(void);
 
 /*
@@ -132,15 +133,16 @@ int bs_paged_attention_batched(const void* query, int64_t query_seq_stride, cons
  * whose device memory already belongs to a fixed pool, an FFI caller without an
  * allocator of its own, a step that must not block on an allocation.  Its
  * scratch is one static device array of 8 MiB per GPU, present from the moment
- * the library's kernels load on that GPU until the process exits.  Limits: at
- * most 16384 (sequence, kv head) pairs per call, and shapes whose partial
- * records fit the array (on B200 the bf16 path at head_dim 64 and 128 always does);
- * larger calls fail with BS_ERR_UNSUPPORTED and a message.  The first call on
+ * the library's kernels load on that GPU until the process exits.  Limit: at
+ * most 16384 (sequence, kv head) pairs per call; a larger call fails with
+ * BS_ERR_UNSUPPORTED and a message.  Shapes whose partial records for the
+ * regular grid would not fit the array run on fewer CTAs.  The first call on
  * each GPU finds the array's device address and clears it (synchronising that
  * GPU once), so make that first call before capturing a stream.  All calls share
  * the array: calls that overlap on the GPU race, so serialise them.  Kernel-side
- * problems (bad table entry, length or row) are OR-ed into *device_status (a
- * device word the caller zeroes) when it is not NULL.
+ * problems (bad table entry, length or row, a wait that gave up) are OR-ed into
+ * *device_status, a device word the caller zeroes and reads; it must not be
+ * NULL (BS_ERR_INVALID), since nothing else would report them.
  */
 int bs_paged_attention_batched_noalloc(const void* query, int64_t query_seq_stride,
                                        const void* key_pool, const void* value_pool,
@@ -303,6 +305,27 @@ int bs_argmax_rows(const void* logits, int64_t row_stride, int64_t rows, int64_t
  * bit was set, BS_OK otherwise; *status_out gets the bits.
  */
 int bs_take_status(void* workspace, void* stream, uint32_t* status_out);
+
+/*
+ * Zero-fills the status word and the per-segment counters of a workspace (its
+ * first 256 KiB + 256 bytes) on `stream`.  A launch that reported a problem
+ * (any status bit) may have stopped short of the work that returns the
+ * counters to zero; call this after such a launch before the workspace is used
+ * again.  No counterpart in the reference, whose op keeps no state between
+ * calls.
+ */
+int bs_reset_workspace(void* workspace, void* stream);
+
+/*
+ * Test hook of the bounded-wait error path; no counterpart in the reference.
+ * Sets, for every later decode launch of this process, the limit of each
+ * pipeline wait of the tensor-core decode kernel (0 restores the default of
+ * about 2 s) and, when `unarmed` is non-zero, makes one warp of that kernel wait
+ * on stages that nothing fills, so the wait runs out with no copy in flight: the
+ * launch then sets BS_STATUS_WAIT_TIMEOUT and finishes without faulting.  Never
+ * set outside tests.
+ */
+int bs_set_wait_probe(int32_t unarmed, uint64_t wait_limit_ns);
 
 #ifdef __cplusplus
 }

@@ -181,9 +181,9 @@ def test_large_ragged_batch_against_oracle(heads, kv_heads, head_dim):
     out = ops.paged_attention_batched(q, k, v, bt, lens_d, head_dim ** -0.5)
     assert ops.take_status() == 0
     assert not out.isnan().any()
-    rng = np.random.default_rng(1)
-    sample = sorted(set(rng.choice(256, 24, replace=False).tolist()) | {int(np.argmax(lens))})
-    check_against_oracle(out, lens, tables, q, k, v, heads // kv_heads, head_dim ** -0.5, sample)
+    # Every one of the 256 sequences against the oracle.
+    check_against_oracle(out, lens, tables, q, k, v, heads // kv_heads, head_dim ** -0.5,
+                         range(256))
     # Same inputs, same bits: counters and records are left clean between calls.
     again = ops.paged_attention_batched(q, k, v, bt, lens_d, head_dim ** -0.5)
     assert torch.equal(out, again)
@@ -351,6 +351,29 @@ def test_one_workspace_serves_calls_of_any_size_in_any_order():
         assert ops.take_status() == 0
         assert not out.isnan().any()
         assert (one.float() - out[0].float()).abs().max().item() <= 1e-2
-        rng = np.random.default_rng(seed)
-        sample = sorted(set(rng.choice(B, min(B, 12), replace=False).tolist()))
-        check_against_oracle(out, lens, tables, q, k, v, 7, 0.125, sample)
+        check_against_oracle(out, lens, tables, q, k, v, 7, 0.125, range(B))
+
+
+@pytest.mark.parametrize("head_dim", [64, 128])
+def test_a_wait_that_runs_out_reports_a_timeout_and_the_next_call_is_correct(head_dim):
+    """The bounded-wait error path, made to happen without a fault: through the
+    test hook, one warp of the tensor-core kernel waits on stages that nothing
+    fills, with a 200 us limit.  The launch must finish, report the timeout bit
+    (a RuntimeError on the host), leave no copy in flight, and leave the
+    workspace so that the next call -- default limit -- is correct."""
+    heads, kv_heads = (14, 2) if head_dim == 64 else (28, 4)
+    lens, tables, bt, q, k, v = ragged_batch(64, heads, kv_heads, head_dim, torch.bfloat16,
+                                             median=600, seed=21)
+    lens_d = torch.tensor(lens, dtype=torch.int32, device=DEV)
+    scale = head_dim ** -0.5
+    ops.set_wait_probe(True, 200_000)
+    try:
+        ops.paged_attention_batched(q, k, v, bt, lens_d, scale)
+        with pytest.raises(RuntimeError, match="timed out"):
+            ops.take_status()
+    finally:
+        ops.set_wait_probe(False, 0)
+    for _ in range(2):
+        out = ops.paged_attention_batched(q, k, v, bt, lens_d, scale)
+        assert ops.take_status() == 0
+        check_against_oracle(out, lens, tables, q, k, v, heads // kv_heads, scale, range(64))
