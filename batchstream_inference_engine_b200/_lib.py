@@ -19,6 +19,7 @@ EXPORTS = (
     "bs_last_error",
     "bs_version",
     "bs_paged_attention",
+    "bs_paged_attention_check",
     "bs_paged_attention_workspace_bytes",
     "bs_paged_attention_batched",
     "bs_paged_attention_batched_workspace_bytes",
@@ -49,6 +50,11 @@ _SIGNATURES = {
          _p, _i32, _i32, _pi64, _pi64,
          _p, _i32, _i32, _pi64, _pi64,
          _pi64, _i64, _i64, _i64, _i64, _dbl, _p, _p, _u64, _p],
+        ctypes.c_int,
+    ),
+    "bs_paged_attention_check": (
+        [_i32, _i32, _pi64, _pi64, _i32, _i32, _pi64, _pi64, _i32, _i32, _pi64, _pi64,
+         _pi64, _i64, _i64, _i64, _i64],
         ctypes.c_int,
     ),
     "bs_paged_attention_workspace_bytes": (

@@ -388,15 +388,13 @@ int bs_paged_attention_workspace_bytes(int64_t num_heads, int64_t num_kv_heads, 
   return BS_OK;
 }
 
-int bs_paged_attention(const void* query, int32_t query_dtype, int32_t query_ndim,
-                       const int64_t* query_shape, const int64_t* query_strides,
-                       const void* keys, int32_t keys_dtype, int32_t keys_ndim,
-                       const int64_t* keys_shape, const int64_t* keys_strides,
-                       const void* values, int32_t values_dtype, int32_t values_ndim,
-                       const int64_t* values_shape, const int64_t* values_strides,
-                       const int64_t* block_table, int64_t block_table_len, int64_t length,
-                       int64_t block_size, int64_t groups, double scaling, void* output,
-                       void* workspace, uint64_t workspace_bytes, void* stream) {
+int bs_paged_attention_check(int32_t query_dtype, int32_t query_ndim, const int64_t* query_shape,
+                             const int64_t* query_strides, int32_t keys_dtype, int32_t keys_ndim,
+                             const int64_t* keys_shape, const int64_t* keys_strides,
+                             int32_t values_dtype, int32_t values_ndim,
+                             const int64_t* values_shape, const int64_t* values_strides,
+                             const int64_t* block_table, int64_t block_table_len, int64_t length,
+                             int64_t block_size, int64_t groups) {
   // The reference's checks, in its order (csrc/paged_attention.cpp:25-43).
   BS_CHECK((query_dtype == BS_BF16 || query_dtype == BS_F32) && keys_dtype == query_dtype &&
                values_dtype == query_dtype,
@@ -421,6 +419,29 @@ int bs_paged_attention(const void* query, int32_t query_dtype, int32_t query_ndi
   for (int64_t i = 0; i < blocks_needed; ++i) {
     BS_CHECK(block_table[i] >= 0 && block_table[i] < num_blocks, "block table entry out of range");
   }
+  (void)query_strides;
+  return BS_OK;
+}
+
+int bs_paged_attention(const void* query, int32_t query_dtype, int32_t query_ndim,
+                       const int64_t* query_shape, const int64_t* query_strides,
+                       const void* keys, int32_t keys_dtype, int32_t keys_ndim,
+                       const int64_t* keys_shape, const int64_t* keys_strides,
+                       const void* values, int32_t values_dtype, int32_t values_ndim,
+                       const int64_t* values_shape, const int64_t* values_strides,
+                       const int64_t* block_table, int64_t block_table_len, int64_t length,
+                       int64_t block_size, int64_t groups, double scaling, void* output,
+                       void* workspace, uint64_t workspace_bytes, void* stream) {
+  // The reference's checks, in its order (csrc/paged_attention.cpp:25-43).
+  if (int rc = bs_paged_attention_check(query_dtype, query_ndim, query_shape, query_strides,
+                                        keys_dtype, keys_ndim, keys_shape, keys_strides,
+                                        values_dtype, values_ndim, values_shape, values_strides,
+                                        block_table, block_table_len, length, block_size,
+                                        groups)) {
+    return rc;
+  }
+  const int64_t blocks_needed = (length + block_size - 1) / block_size;
+  const int64_t num_blocks = keys_shape[1];
   // This library's own requirements.
   const int64_t heads = query_shape[0], head_dim = query_shape[1], kv_heads = keys_shape[0];
   BS_CHECK(is_contiguous(2, query_shape, query_strides),

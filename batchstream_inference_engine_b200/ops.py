@@ -141,10 +141,21 @@ def paged_attention(query: torch.Tensor, keys: torch.Tensor, values: torch.Tenso
                     scaling: float) -> torch.Tensor:
     """Drop-in for the reference op ``paged_attention`` (csrc/paged_attention.cpp:76-105).
 
-    Same positional signature and the same malformed-input errors; runs on CUDA
-    tensors and accepts float32 when query, keys and values are all float32.
-    Returns [heads, head_dim] in the query dtype on the query's device.
+    Same positional signature and the same malformed-input errors; accepts
+    float32 when query, keys and values are all float32.  Returns
+    [heads, head_dim] in the query dtype on the query's device.
+
+    The attention always runs in this library's CUDA kernels.  The reference's
+    own callers keep the pool on the host (PagedKVPool allocates it with
+    torch.zeros, src/server/torch_model.py:120-122): when query, keys and values
+    are all host tensors, the inputs are checked as the reference checks them,
+    the sequence's blocks (and the query) are staged on the current CUDA device,
+    and the result comes back as a host tensor -- so the op drops into those
+    callers unchanged.
     """
+    if not (query.is_cuda or keys.is_cuda or values.is_cuda):
+        return _paged_attention_from_host(query, keys, values, block_table, length, block_size,
+                                          groups, scaling)
     if query.dim() == 2:
         query = query.contiguous()  # the reference copies it too (paged_attention.cpp:81)
     table = [int(b) for b in block_table]
@@ -175,6 +186,32 @@ def paged_attention(query: torch.Tensor, keys: torch.Tensor, values: torch.Tenso
             i64_array(table), len(table), int(length), int(block_size), int(groups),
             float(scaling), out.data_ptr(), ws_ptr, ws_bytes, stream))
     return out
+
+
+def _paged_attention_from_host(query, keys, values, block_table, length, block_size, groups,
+                               scaling):
+    """paged_attention on host tensors: validate, stage the blocks the table
+    names (in table order, so the staged table is 0 .. n - 1) and the query on
+    the current device, run the device op, return the output on the host."""
+    table = [int(b) for b in block_table]
+    qn, qs, qst = _shape_args(query)
+    kn, ks, kst = _shape_args(keys)
+    vn, vs, vst = _shape_args(values)
+    check(lib().bs_paged_attention_check(
+        dtype_code(query.dtype), qn, qs, qst, dtype_code(keys.dtype), kn, ks, kst,
+        dtype_code(values.dtype), vn, vs, vst, i64_array(table), len(table), int(length),
+        int(block_size), int(groups)))
+    if not torch.cuda.is_available():
+        raise RuntimeError("paged_attention: no CUDA device to run on")
+    device = torch.device("cuda", torch.cuda.current_device())
+    need = -(-int(length) // int(block_size))
+    rows = torch.tensor(table[:need], dtype=torch.long)
+    k_dev = keys.index_select(1, rows).to(device, non_blocking=False)
+    v_dev = values.index_select(1, rows).to(device, non_blocking=False)
+    q_dev = query.contiguous().to(device)
+    out = paged_attention(q_dev, k_dev, v_dev, list(range(need)), length, block_size, groups,
+                          scaling)
+    return out.cpu()
 
 
 class _NullContext:

@@ -90,6 +90,21 @@ int bs_paged_attention(const void* query, int32_t query_dtype, int32_t query_ndi
                        int64_t block_size, int64_t groups, double scaling, void* output,
                        void* workspace, uint64_t workspace_bytes, void* stream);
 
+/*
+ * The sixteen input checks of bs_paged_attention alone (the reference's
+ * check_inputs, csrc/paged_attention.cpp:22-44), touching no memory but the
+ * shape, stride and table arrays: BS_OK or BS_ERR_INVALID with the message
+ * bs_paged_attention would give.  A binding that receives the reference's host
+ * tensors validates them with this before staging them on the device.
+ */
+int bs_paged_attention_check(int32_t query_dtype, int32_t query_ndim, const int64_t* query_shape,
+                             const int64_t* query_strides, int32_t keys_dtype, int32_t keys_ndim,
+                             const int64_t* keys_shape, const int64_t* keys_strides,
+                             int32_t values_dtype, int32_t values_ndim,
+                             const int64_t* values_shape, const int64_t* values_strides,
+                             const int64_t* block_table, int64_t block_table_len, int64_t length,
+                             int64_t block_size, int64_t groups);
+
 /* Workspace bytes bs_paged_attention needs for this shape (current device). */
 int bs_paged_attention_workspace_bytes(int64_t num_heads, int64_t num_kv_heads, int64_t head_dim,
                                        int64_t block_table_len, int32_t dtype,

@@ -111,3 +111,16 @@ PREFILL_CASES = [(1, 0, 4, 2), (5, 0, 4, 2), (16, 0, 4, 2), (17, 3, 4, 2), (33, 
                  (40, 16, 4, 2), (24, 9, 14, 2)]
 SCATTERED_LENGTHS = [1, 3, 4, 5, 8, 9, 15, 16, 17, 100, 1000]
 F32_LENGTHS = [1, 3, 4, 5, 8, 9, 15]
+
+
+def mixed_step_shapes():
+    """The mixed chunked-prefill + decode step of one GPU, all from
+    ``np.random.default_rng(0)``: 8 chunk priors U[0, 4096], then 248 decode
+    context lengths log-normal (median 768, sigma 1), rounded and clipped to
+    [16, 8192] (each counting the step's new token)."""
+    import math
+
+    rng = np.random.default_rng(0)
+    priors = rng.integers(0, 4097, 8).astype(np.int64)
+    lens = np.clip(np.rint(rng.lognormal(math.log(768.0), 1.0, 248)), 16, 8192).astype(np.int64)
+    return priors, lens

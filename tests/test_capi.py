@@ -78,10 +78,30 @@ def test_host_validation_rejects_bad_input_with_runtime_error(change):
     assert "CUDA" not in str(err.value) and "cuda" not in str(err.value)
 
 
-def test_valid_host_tensors_are_refused_not_computed():
+def test_valid_host_tensors_are_never_computed_on_the_host():
+    # Host tensors pass the reference's checks and are then staged on a CUDA
+    # device; without one the call is refused -- there is no host arithmetic.
     query, keys, values, table = inputs.scattered_bf16(5)
-    with pytest.raises(RuntimeError):
+    if torch.cuda.is_available():
+        pytest.skip("a CUDA device is present: the host-tensor path runs on it (gpu tests)")
+    with pytest.raises(RuntimeError, match="no CUDA device"):
         paged_attention(query, keys, values, table, 5, 4, 2, 0.5)
+
+
+def test_check_entry_point_runs_the_reference_checks_alone():
+    from batchstream_inference_engine_b200._lib import i64_array
+
+    lib = _lib.lib()
+    args = lambda length, table: (  # noqa: E731
+        _lib.BS_BF16, 2, i64_array([4, 8]), i64_array([8, 1]), _lib.BS_BF16, 4,
+        i64_array([2, 5, 4, 8]), i64_array([160, 32, 8, 1]), _lib.BS_BF16, 4,
+        i64_array([2, 5, 4, 8]), i64_array([160, 32, 8, 1]), i64_array(table), len(table),
+        length, 4, 2)
+    assert lib.bs_paged_attention_check(*args(5, [3, 1])) == 0
+    assert lib.bs_paged_attention_check(*args(13, [3, 1])) != 0
+    assert b"too short" in lib.bs_last_error()
+    assert lib.bs_paged_attention_check(*args(5, [3, 5])) != 0
+    assert b"out of range" in lib.bs_last_error()
 
 
 def test_error_codes_come_with_messages():

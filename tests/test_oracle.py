@@ -143,3 +143,27 @@ def test_torch_generator_recipes_are_stable():
     lengths, _, q, k, v = inputs.op_level_batch()
     assert lengths == load("decode_op_level.npz")["lengths"].tolist()
     assert q.dtype == torch.float32 and k.shape == (2, 256, 16, 64)
+
+
+def test_recorded_reference_pool_calls_match_the_oracle_bit_for_bit():
+    """The op calls recorded from the reference's own PagedKVPool (fixture
+    reference_callers.npz): the C oracle on the recorded blocks reproduces the
+    reference op's recorded outputs exactly, and the rebuilt arguments have the
+    caller's forms (the query's view of the step's rotated queries, the pool's
+    layer view)."""
+    from tests.test_reference_callers_gpu import _calls, _events, _rebuild
+
+    calls = _calls()
+    assert len(calls) == 30
+    for call in calls:
+        query, keys, values, table = _rebuild(call)
+        assert list(query.stride()) == call["q_stride"].tolist()
+        assert query.storage_offset() == int(call["q_offset"])
+        assert keys.storage_offset() == int(call["pool_offset"])
+        got = oracle.decode(inputs.bf16_bits(query.contiguous()), inputs.bf16_bits(keys),
+                            inputs.bf16_bits(values), table, int(call["length"]),
+                            int(call["block_size"]), int(call["groups"]), float(call["scaling"]))
+        assert np.array_equal(got, call["out"].reshape(got.shape))
+    events = _events()
+    assert sum(e[0] == "start" for e in events) == 24
+    assert sum(e[0] == "release" for e in events) == 24
