@@ -17,7 +17,8 @@ import torch
 
 
 class OutOfBlocks(RuntimeError):
-    pass
+    """The pool (or the device table) cannot hold a sequence's next blocks;
+    nothing was taken.  A RuntimeError, as the reference raises it."""
 
 
 class BlockAllocator:
@@ -52,11 +53,15 @@ class BlockAllocator:
         return self._block_size
 
     def allocate(self, seq_id: int, total_tokens: int) -> None:
-        """Grow a sequence's block table until it covers total_tokens."""
+        """Extends seq_id's table (creating it if new) to ceil(total_tokens /
+        block_size) blocks, taking each from the end of the free list; takes
+        none and raises OutOfBlocks when the free list is too short."""
         table = self._tables.get(seq_id, [])
-        needed = -(-total_tokens // self._block_size) - len(table)
-        if needed > len(self._free):
-            raise OutOfBlocks(f"need {needed} blocks, {len(self._free)} free")
+        missing = -(-total_tokens // self._block_size) - len(table)
+        if missing > len(self._free):
+            raise OutOfBlocks(f"sequence {seq_id} needs {missing} more blocks but only "
+                              f"{len(self._free)} are free")
+        needed = missing
         if self.device_tables is not None:
             if len(table) + max(needed, 0) > self.max_blocks_per_seq:
                 raise OutOfBlocks(

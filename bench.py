@@ -1547,33 +1547,29 @@ def run_engine_load(args):
 
 
 def time_cpu_engine(seconds, concurrent=16):
-    """The oracle's CPU restatement of the reference model step (bf16, all host
-    threads for torch) on the engine workload with `concurrent` sequences,
-    stepped until `seconds` have passed; generated tokens per second."""
+    """The reference's paged backend and scheduler loop as the oracle restates
+    them (oracle/engine.py: model step, batch composition, allocator,
+    admission), bf16 on all host threads for torch, on the engine workload with
+    `concurrent` sequences, stepped until `seconds` have passed; generated
+    tokens per second."""
     import torch
 
-    from batchstream_inference_engine_b200.serve import BlockBudget, OfflineScheduler
     from batchstream_inference_engine_b200.torch_model import QWEN25_05B, random_weights
-    from oracle.engine import cpu_backend
+    from oracle.engine import cpu_backend, run_for
 
     cores = os.cpu_count() or 1
     torch.set_num_threads(cores)
     blocks = concurrent * -(-(ENGINE_PROMPT[1] + ENGINE_MAX_TOKENS[1]) // BLOCK)
     backend = cpu_backend(random_weights(), torch.bfloat16, QWEN25_05B, blocks, BLOCK,
-                          ENGINE_PREFILL, max_seqs=concurrent)
-    sched = OfflineScheduler(backend, engine_specs(), concurrent, BlockBudget(blocks, BLOCK))
-    sched.step()  # warm-up
-    generated, steps = 0, 0
-    start = time.perf_counter()
-    while time.perf_counter() - start < seconds:
-        generated += len(sched.step())
-        steps += 1
-    elapsed = time.perf_counter() - start
+                          ENGINE_PREFILL)
+    generated, steps, elapsed = run_for(backend, engine_specs(), concurrent, blocks, BLOCK,
+                                        seconds)
     return {"value": round(generated / elapsed, 3), "unit": "tokens/s", "cores": cores,
             "kind": "port",
             "sample": f"{steps} engine steps of the workload with {concurrent} concurrent "
-                      f"sequences through the oracle's CPU restatement of the reference "
-                      f"model step (bf16), {elapsed:.1f} s, {generated} tokens generated"}
+                      f"sequences through the oracle's restatement of the reference model "
+                      f"step, paged backend and scheduler loop (bf16), {elapsed:.1f} s, "
+                      f"{generated} tokens generated"}
 
 
 def run_reference(args):
@@ -1676,8 +1672,9 @@ def run_reference_engine(args):
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (seeded token-id prompts, random-init weights seed 0 N(0,0.02))",
-        "config": {"workload": "engine: oracle CPU restatement of the reference model step, "
-                               "16 concurrent sequences, on host cores"},
+        "config": {"workload": "engine: the oracle's restatement of the reference model step, "
+                               "paged backend and scheduler loop, 16 concurrent sequences, on "
+                               "host cores"},
         "cpu_baseline": base,
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},

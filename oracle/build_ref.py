@@ -7,21 +7,32 @@ git-ignored ``oracle/_ref/``.  The built module travels with the repository to
 machines without the checkout, where ``oracle.load_reference_op()`` imports it
 directly.  The reference's own build system (setup.py) is not run.
 
-    python oracle/build_ref.py [reference_root]
+    python oracle/build_ref.py <reference checkout>   (or BS_REFERENCE_DIR)
 """
 
 from __future__ import annotations
 
+import os
 import sys
 from pathlib import Path
 
 HERE = Path(__file__).resolve().parent
 OUT = HERE / "_ref"
-DEFAULT_REFERENCE = Path("/root/reference")
 
 
-def build(reference_root: Path = DEFAULT_REFERENCE) -> Path | None:
-    source = reference_root / "csrc" / "paged_attention.cpp"
+def reference_root(explicit: str | Path | None = None) -> Path | None:
+    """The reference checkout: the given path, else BS_REFERENCE_DIR, else none."""
+    found = explicit or os.environ.get("BS_REFERENCE_DIR")
+    return Path(found) if found else None
+
+
+def build(root: str | Path | None = None) -> Path | None:
+    """Builds the op from the checkout at `root` (or BS_REFERENCE_DIR); returns
+    the module's path, or None without a checkout."""
+    root = reference_root(root)
+    if root is None:
+        return None
+    source = root / "csrc" / "paged_attention.cpp"
     if not source.exists():
         return None
     existing = sorted(OUT.glob("paged_attention_cpp*.so"))
@@ -42,5 +53,4 @@ def build(reference_root: Path = DEFAULT_REFERENCE) -> Path | None:
 
 
 if __name__ == "__main__":
-    root = Path(sys.argv[1]) if len(sys.argv) > 1 else DEFAULT_REFERENCE
-    print(build(root))
+    print(build(sys.argv[1] if len(sys.argv) > 1 else None))

@@ -12,8 +12,10 @@ RMSNorm with fp32 statistics cast back (:283-287), bf16-rounded rotary tables
 and attention (PagedKVCache.attend :155-167 through paged_attention :67-80 for
 one token and _read_blocks + attend with _causal_mask :39-64, 295-297 for a
 chunk), o_proj, the SwiGLU MLP (:278-281), the final norm and the tied output
-projection (:223-229).  The pool and the block tables are the ones of the
-``PagedKVCache`` objects it is given (the package's bookkeeping, kept on CPU).
+projection (:223-229).  ``ReferenceBackend`` restates the reference's paged
+backend (src/server/backend/paged.py:21-99) around it over a host pool and the
+oracle's allocator, and ``run_for`` the scheduler's admission loop
+(src/server/scheduler.py:112-158): no part of the package runs in the baseline.
 """
 
 from __future__ import annotations
@@ -35,9 +37,6 @@ class ReferenceModelStep:
         self.eps = rms_norm_eps
         half = torch.arange(0, self.head_dim, 2, dtype=torch.float)
         self.inv_freq = 1.0 / (rope_theta ** (half / self.head_dim))
-        # Interface the package's PagedBackend expects of a model.
-        self.device = torch.device("cpu")
-        self.max_position = 1 << 20
 
     # -------------------------------------------------------------- pieces
 
@@ -130,33 +129,146 @@ class ReferenceModelStep:
     def next_tokens(self, groups) -> list[int]:
         return self.forward_batch(groups).float().argmax(dim=-1).tolist()
 
-    def launch_tokens(self, groups) -> "_Done":
-        """The backend's launch interface, computed at once (the CPU backend
-        runs the plain loop: every input token is an id, never a reference)."""
-        if any(t < 0 for tokens, _ in groups for t in tokens):
-            raise ValueError("the reference model step takes token ids only")
-        return _Done(self.next_tokens(groups))
+
+class _Pool:
+    """src/server/torch_model.py:115-137 on the host: [layers, kv_heads, blocks,
+    block_size, head_dim] pools and the oracle's restated BlockAllocator."""
+
+    def __init__(self, config, num_blocks: int, block_size: int, dtype: torch.dtype):
+        from oracle import Allocator
+
+        shape = (config.num_layers, config.num_kv_heads, num_blocks, block_size, config.head_dim)
+        self.keys = torch.zeros(shape, dtype=dtype)
+        self.values = torch.zeros(shape, dtype=dtype)
+        self.block_size = block_size
+        self.allocator = Allocator(num_blocks, block_size)
+
+    @property
+    def free_blocks(self) -> int:
+        return len(self.allocator.free_list)
+
+    def block_table(self, seq_id: int) -> list[int]:
+        return self.allocator.tables[seq_id]
+
+    def new_cache(self, seq_id: int) -> "_Cache":
+        return _Cache(self, seq_id)
+
+    def release(self, cache: "_Cache") -> None:
+        self.allocator.free(cache.seq_id)
 
 
-class _Done:
-    def __init__(self, values: list[int]):
-        self._values = values
+class _Cache:
+    """src/server/torch_model.py:140-147, 169-170: length bookkeeping."""
 
-    def ref(self, i: int) -> int:
-        return -1 - i
+    def __init__(self, pool: _Pool, seq_id: int):
+        self._pool = pool
+        self.seq_id = seq_id
+        self.length = 0
 
-    def result(self) -> list[int]:
-        return self._values
+    def reserve(self, count: int) -> None:
+        self._pool.allocator.allocate(self.seq_id, self.length + count)
+
+    def advance(self, count: int) -> None:
+        self.length += count
 
 
-def cpu_backend(weights, dtype, config, num_blocks: int, block_size: int, prefill_chunk: int,
-                max_seqs: int = 256):
-    """The package's PagedBackend bookkeeping (reference batch composition and
-    allocator) over ``ReferenceModelStep`` with a CPU pool."""
-    from batchstream_inference_engine_b200.backend import PagedBackend
+class ReferenceBackend:
+    """src/server/backend/paged.py:21-99 restated over ``ReferenceModelStep``:
+    generating sequences' next tokens first, then prompt pieces under the
+    prefill budget in sequence order; a sequence whose prompt is used up gets
+    its greedy token; release frees its blocks.  Token ids only (end of
+    generation: Qwen2.5's 151643 / 151645)."""
 
+    END_OF_GENERATION = frozenset({151643, 151645})
+
+    def __init__(self, model: ReferenceModelStep, pool: _Pool, prefill_chunk: int):
+        self._model = model
+        self.pool = pool
+        self._prefill_chunk = prefill_chunk
+        self._next_id = 0
+        self._sequences: dict[int, dict] = {}
+
+    def start_sequence(self, prompt_tokens: list[int]) -> int:
+        seq_id, self._next_id = self._next_id, self._next_id + 1
+        cache = self.pool.new_cache(seq_id)
+        cache.reserve(0)
+        self._sequences[seq_id] = dict(cache=cache, pending=list(prompt_tokens), next=None,
+                                       finished=False)
+        return seq_id
+
+    def step(self) -> dict[int, tuple[int, bool]]:
+        batch = [(s, [q["next"]]) for s, q in self._sequences.items()
+                 if not q["pending"] and not q["finished"]]
+        budget = self._prefill_chunk
+        for s, q in self._sequences.items():
+            take = min(budget, len(q["pending"]))
+            if take:
+                batch.append((s, q["pending"][:take]))
+                del q["pending"][:take]
+                budget -= take
+        if not batch:
+            return {}
+        tokens = self._model.next_tokens([(t, self._sequences[s]["cache"]) for s, t in batch])
+        outputs = {}
+        for (s, _), token in zip(batch, tokens):
+            q = self._sequences[s]
+            if not q["pending"]:
+                q["next"] = token
+                q["finished"] = token in self.END_OF_GENERATION
+                outputs[s] = (token, q["finished"])
+        return outputs
+
+    def release_sequence(self, seq_id: int) -> None:
+        self.pool.release(self._sequences.pop(seq_id)["cache"])
+
+
+def cpu_backend(weights, dtype, config, num_blocks: int, block_size: int, prefill_chunk: int):
+    """The restated reference backend over ``ReferenceModelStep`` with a host
+    pool of `dtype` (the reference's own pool is bf16; fp32 serves parity)."""
     model = ReferenceModelStep(weights, dtype, config.num_layers, config.num_heads,
                                config.num_kv_heads, config.rope_theta, config.rms_norm_eps)
-    model.config = config
-    model.dtype = dtype
-    return PagedBackend(model, num_blocks, block_size, prefill_chunk, max_seqs=max_seqs)
+    return ReferenceBackend(model, _Pool(config, num_blocks, block_size, dtype), prefill_chunk)
+
+
+def run_for(backend: ReferenceBackend, specs, max_concurrent: int, num_blocks: int,
+            block_size: int, seconds: float, warmup: bool = True) -> tuple[int, int, float]:
+    """src/server/scheduler.py:112-158 (BatchingScheduler, its BlockBudget
+    src/server/kv_budget.py) restated as a plain loop over queued requests:
+    admit from the head while under max_concurrent and the budget reserves
+    ceil((prompt + max_tokens) / block_size) blocks, step, count tokens,
+    complete at max_tokens or end of generation.  Steps until `seconds` pass
+    or every request is done; returns (tokens generated, steps, elapsed
+    seconds), the first step untimed when `warmup`."""
+    import time
+    from collections import deque
+
+    waiting = deque((list(p), int(m)) for p, m in specs)
+    active: dict[int, list] = {}
+    available = num_blocks
+    blocks = lambda p, m: -(-(len(p) + m) // block_size)  # noqa: E731
+
+    def turn() -> int:
+        nonlocal available
+        while (waiting and len(active) < max_concurrent
+               and blocks(*waiting[0]) <= available):
+            p, m = waiting.popleft()
+            available -= blocks(p, m)
+            active[backend.start_sequence(p)] = [p, m, 0]
+        outputs = backend.step()
+        for s, (_, finished) in outputs.items():
+            req = active[s]
+            req[2] += 1
+            if finished or req[2] >= req[1]:
+                available += blocks(req[0], req[1])
+                del active[s]
+                backend.release_sequence(s)
+        return len(outputs)
+
+    if warmup:
+        turn()
+    generated, steps = 0, 0
+    start = time.perf_counter()
+    while (waiting or active) and time.perf_counter() - start < seconds:
+        generated += turn()
+        steps += 1
+    return generated, steps, time.perf_counter() - start

@@ -16,11 +16,12 @@ BatchingScheduler, src/server/kv_budget.py BlockBudget) on the CPU:
 * vocabulary: token ids only; end of generation = Qwen2.5's 151643 / 151645
   (the GGUF vocabulary and llama.cpp are not on this path).
 
-Usage: python tests/golden/make_engine_golden.py  (needs the reference sources
-at /root/reference; takes a few minutes on 8 cores).
+Usage: BS_REFERENCE_DIR=<reference checkout> python tests/golden/make_engine_golden.py
+(takes a few minutes on 8 cores).
 """
 
 import asyncio
+import os
 import sys
 import time
 import types
@@ -31,9 +32,10 @@ import numpy as np
 import torch
 
 ROOT = Path(__file__).resolve().parents[2]
-REFERENCE = Path("/root/reference/src")
+if not os.environ.get("BS_REFERENCE_DIR"):
+    raise SystemExit("set BS_REFERENCE_DIR to the reference checkout")
 sys.path.insert(0, str(ROOT))
-sys.path.insert(0, str(REFERENCE))
+sys.path.insert(0, str(Path(os.environ["BS_REFERENCE_DIR"]) / "src"))
 
 from batchstream_inference_engine_b200.serve import engine_workload  # noqa: E402
 from batchstream_inference_engine_b200.torch_model import random_weights  # noqa: E402
