@@ -260,37 +260,6 @@ def capture_steps(step, rotations, dev):
     return graphs, capture, counts
 
 
-def capture_parts(parts, rotations, dev):
-    """Like capture_steps, with each step split into consecutive parts (one
-    graph per part and rotation; a part takes and returns the state the next
-    one needs), so events between the replays time each part."""
-    import torch
-
-    from batchstream_inference_engine_b200 import ops
-
-    stream = torch.cuda.current_stream(dev)
-    capture = torch.cuda.Stream(dev)
-    capture.wait_stream(stream)
-    with torch.cuda.stream(capture):
-        for r in range(rotations):
-            state = None
-            for part in parts:
-                state = part(r, state)
-        torch.cuda.synchronize(dev)
-        ops.take_status(dev)
-        graphs = []
-        for r in range(rotations):
-            state, row = None, []
-            for part in parts:
-                g = torch.cuda.CUDAGraph()
-                with torch.cuda.graph(g, stream=capture):
-                    state = part(r, state)
-                row.append((g, state))  # the state keeps the tensors a graph uses alive
-            graphs.append(row)
-    torch.cuda.synchronize(dev)
-    return graphs, capture
-
-
 def take_all_status(capture, dev):
     """Raises if a replayed graph (workspace of the capture stream) or an eager
     call (current stream) recorded a device-side problem."""
@@ -334,32 +303,47 @@ def timed_windows(replay, steps, warmup, windows, dev, world, clocks=None):
     return times
 
 
-def timed_parts(graphs, steps, warmup, dev, world):
-    """Replays split graphs (capture_parts) with an event after every part;
-    returns the mean ms of each part over `steps` steps."""
+def time_kernel_chain(launch, rotations, repeats, steps, warmup, dev, world):
+    """Mean device time of one launch: a CUDA graph of rotations x repeats
+    launches back to back (launch(r) for each rotation r in turn) replayed
+    until about `steps` launches were timed, with CUDA events around the
+    replays on the launching stream."""
     import torch
     import torch.distributed as dist
 
+    from batchstream_inference_engine_b200 import ops
+
     stream = torch.cuda.current_stream(dev)
-    nparts = len(graphs[0])
-    for i in range(warmup):
-        for g, _ in graphs[i % len(graphs)]:
-            g.replay()
+    capture = torch.cuda.Stream(dev)
+    capture.wait_stream(stream)
+    with torch.cuda.stream(capture):
+        for r in range(rotations):
+            launch(r)
+        torch.cuda.synchronize(dev)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=capture):
+            for _ in range(repeats):
+                for r in range(rotations):
+                    launch(r)
+    torch.cuda.synchronize(dev)
+    per = rotations * repeats
+    replays = max(1, -(-steps // per))
+    for _ in range(max(1, warmup // per)):
+        graph.replay()
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize(dev)
-    marks = [[torch.cuda.Event(enable_timing=True) for _ in range(nparts + 1)]
-             for _ in range(steps)]
-    for i in range(steps):
-        row = graphs[i % len(graphs)]
-        marks[i][0].record(stream)
-        for p, (g, _) in enumerate(row):
-            g.replay()
-            marks[i][p + 1].record(stream)
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    for _ in range(replays):
+        graph.replay()
+    t1.record(stream)
     torch.cuda.synchronize(dev)
-    if world > 1:
-        dist.barrier()
-    return [statistics.mean(m[p].elapsed_time(m[p + 1]) for m in marks) for p in range(nparts)]
+    with torch.cuda.stream(capture):
+        ops.take_status(dev)
+    del graph
+    return t0.elapsed_time(t1) / (replays * per)
 
 
 def gather_rows(values, dev, world):
@@ -688,16 +672,19 @@ def decode_core(args, world, rank, dev, H, Hkv, D, steps, warmup, windows, label
                                                            ROTATIONS, dev)
     times = timed_windows(lambda i: step_graphs[i % ROTATIONS].replay(), steps, warmup, windows,
                           dev, world, clocks)
-    part_graphs, part_capture = capture_parts([append, decode], ROTATIONS, dev)
-    _, decode_ms = timed_parts(part_graphs, max(steps, 20), warmup, dev, world)
-    take_all_status(part_capture, dev)
+    # The decode kernel's own launch time: one graph of decode launches back to
+    # back over the rotations (each launch after the previous one, as in the
+    # step), timed over whole replays.
+    decode_ms = time_kernel_chain(lambda r: decode(r, lens_d), ROTATIONS, 2, steps, warmup,
+                                  dev, world)
     take_all_status(step_capture, dev)
-    del part_graphs
 
     e2e = per_call = None
     if extras:
+        e2e_steps = max(steps, 200)
         e2e, per_call = decode_e2e(args, world, dev, q, k_new, v_new, k_pool, v_pool, tables,
-                                   start_pos, blocks, width, units, scale, out, steps, warmup)
+                                   start_pos, blocks, width, units, scale, out, e2e_steps,
+                                   max(warmup, 5))
 
     rows = gather_rows(times, dev, world)
     (decode_ms,), _ = max_over_ranks([decode_ms], [], dev, world)
@@ -739,7 +726,7 @@ def decode_core(args, world, rank, dev, H, Hkv, D, steps, warmup, windows, label
             "timing": spread,
             "roofline": {
                 "bound": "hbm",
-                "kernel": "decode_mma_kernel + decode_merge_kernel (split-K decode)",
+                "kernel": "decode_mma_kernel + decode_merge_kernel (split-K decode, merge pass)",
                 "achieved": round(achieved, 1),
                 "peak": peak,
                 "peak_source": peak_note,
@@ -747,6 +734,8 @@ def decode_core(args, world, rank, dev, H, Hkv, D, steps, warmup, windows, label
                 "frac": round(achieved / peak, 4),
                 "traffic": None,
                 "decode_ms": round(decode_ms, 5),
+                "decode_ms_how": "mean time of one decode launch (kernel + merge pass) over a "
+                                 "graph of back-to-back launches (the rotations in turn)",
                 "algorithmic_bytes_per_launch": step_bytes,
             },
             "gpu_launches": sum(step_counts[i % ROTATIONS] for i in range(steps)) * windows,
@@ -754,16 +743,16 @@ def decode_core(args, world, rank, dev, H, Hkv, D, steps, warmup, windows, label
         if e2e is not None:
             h2d, d2h = e2e[1], e2e[2]
             result["e2e"] = {
-                "value": round(job_bytes * steps / (e2e_ms / 1e3) / 1e9, 1),
+                "value": round(job_bytes * e2e_steps / (e2e_ms / 1e3) / 1e9, 1),
                 "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                "ms_per_step": round(e2e_ms / steps, 5),
+                "ms_per_step": round(e2e_ms / e2e_steps, 5), "steps": e2e_steps,
                 "path": "pinned host -> device, decode append + decode, device -> pinned host "
                         "through the public API; two buffer sets in CUDA graphs, the next "
                         "step's copies overlap this step's kernels"}
             result["e2e_per_call"] = {
-                "value": round(job_bytes * steps / (call_ms / 1e3) / 1e9, 1),
+                "value": round(job_bytes * e2e_steps / (call_ms / 1e3) / 1e9, 1),
                 "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                "ms_per_step": round(call_ms / steps, 5),
+                "ms_per_step": round(call_ms / e2e_steps, 5), "steps": e2e_steps,
                 "path": "every step a plain call of the public API from Python (argument "
                         "checks, ctypes, tensor-map lookup on the host each step), copies in "
                         "and out on the same stream, no CUDA graph"}
@@ -953,11 +942,12 @@ def prefill_core(args, world, rank, dev, steps, warmup, windows, clocks=None, ex
                                                            dev)
     times = timed_windows(lambda i: step_graphs[i % rot].replay(), steps, warmup, windows, dev,
                           world, clocks)
-    part_graphs, part_capture = capture_parts([prep, prefill], rot, dev)
-    _, kernel_ms = timed_parts(part_graphs, max(steps, 20), warmup, dev, world)
-    take_all_status(part_capture, dev)
+    # The prefill kernels' own launch time: a graph of prefill launches back to
+    # back over the rotations (metadata and slot writes done beforehand).
+    metas = [prep(r) for r in range(rot)]
+    kernel_ms = time_kernel_chain(lambda r: prefill(r, metas[r]), rot, 1, steps, warmup, dev,
+                                  world)
     take_all_status(step_capture, dev)
-    del part_graphs
     step_flops = prefill_flops(priors, H, D)
 
     e2e = None
@@ -1139,11 +1129,12 @@ def mixed_core(args, world, rank, dev, steps, warmup, windows, clocks=None):
     step_graphs, step_capture, step_counts = capture_steps(step, rot, dev)
     times = timed_windows(lambda i: step_graphs[i % rot].replay(), steps, warmup, windows, dev,
                           world, clocks)
-    part_graphs, part_capture = capture_parts([prep, decode, prefill], rot, dev)
-    prep_ms, decode_ms, prefill_ms = timed_parts(part_graphs, max(steps, 20), warmup, dev, world)
-    take_all_status(part_capture, dev)
+    # Each part's own launch time: graphs of that part's launches back to back
+    # over the rotations.
+    prep_ms = time_kernel_chain(lambda r: prep(r), rot, 1, steps, warmup, dev, world)
+    decode_ms = time_kernel_chain(lambda r: decode(r, None), rot, 1, steps, warmup, dev, world)
+    prefill_ms = time_kernel_chain(lambda r: prefill(r, None), rot, 1, steps, warmup, dev, world)
     take_all_status(step_capture, dev)
-    del part_graphs
     dec_bytes = algorithmic_bytes(dec_lens, H, Hkv, D)
     pre_flops = prefill_flops(priors, H, D)
     rows = gather_rows(times, dev, world)
@@ -1180,7 +1171,9 @@ def mixed_core(args, world, rank, dev, steps, warmup, windows, clocks=None):
             },
             "timing": spread,
             "parts_ms": {"metadata_and_slot_write": round(prep_ms, 5),
-                         "decode": round(decode_ms, 5), "prefill": round(prefill_ms, 5)},
+                         "decode": round(decode_ms, 5), "prefill": round(prefill_ms, 5),
+                         "how": "mean launch time of each part over a graph of its launches "
+                                "back to back"},
             "decode": {"bound": "hbm", "algorithmic_bytes": dec_bytes,
                        "achieved": round(dec_gbs, 1), "unit": "GB/s", "peak": hbm,
                        "peak_source": hbm_note, "frac": round(dec_gbs / hbm, 4)},
