@@ -141,6 +141,9 @@ __global__ void __maxnreg__((Cfg<D, G16>::MAX_REGS))
   int32_t clen = 0, crow = 0, cnb = 0, ch = 0, cb = 0;
   int32_t nxt_len = 0, nxt_row = 0;
   int32_t win_row = -1, win0 = 0, win_val = 0;
+  // The window that follows the current one, loaded when the current one is
+  // (its latency then hides behind the blocks the current window still holds).
+  int32_t pre_row = -1, pre0 = 0, pre_val = 0;
   int64_t cu = wr0;
   if (ntiles > 0) {
     cnb = units_of(a, starts.len[warp], starts.row[warp], clen, crow);
@@ -156,15 +159,43 @@ __global__ void __maxnreg__((Cfg<D, G16>::MAX_REGS))
   // The probe hook leaves this warp's stages unarmed (see DecodeArgs).
   const bool probe = a.probe_unarmed != 0 && blockIdx.x == 0 && warp == 0;
   // `dry`: metadata only, no copy (the walk after a wait gave up).
+  // Lane i's entry of the 32-entry window of table row `row` starting at entry
+  // `e0` (0 past the row's usable entries).
+  auto window = [&](int32_t row, int32_t e0) -> int32_t {
+    const int32_t* table = a.block_tables + static_cast<int64_t>(row) * a.bt_stride;
+    return (e0 + lane < a.max_blocks) ? __ldg(table + e0 + lane) : 0;
+  };
   auto issue = [&](int stage, bool dry) {
-    const int32_t* table = a.block_tables + static_cast<int64_t>(crow) * a.bt_stride;
     // The window caches up to 32 entries of one table row, filled to the row's
     // width rather than this sequence's block count: sequences that share a row
     // (the tokens of a prefill chunk) have different lengths and reuse it.
     if (win_row != crow || cb < win0 || cb >= win0 + 32) {
-      win_row = crow;
-      win0 = cb;
-      win_val = (cb + lane < a.max_blocks) ? __ldg(table + cb + lane) : 0;
+      if (pre_row == crow && cb >= pre0 && cb < pre0 + 32) {
+        win_row = pre_row;
+        win0 = pre0;
+        win_val = pre_val;
+      } else {
+        win_row = crow;
+        win0 = cb;
+        win_val = window(crow, cb);
+      }
+      // Prefetch the window the cursor needs next: the rest of this segment,
+      // else this sequence's other kv heads (the same row from entry 0), else
+      // the next sequence's row.
+      int32_t next_row = -1, next0 = 0;
+      if (win0 + 32 < cnb) {
+        next_row = crow;
+        next0 = win0 + 32;
+      } else if (ch + 1 < a.num_kv_heads) {
+        next_row = crow;
+      } else if (ci + 1 < a.num_seqs && nxt_row >= 0 && nxt_row < a.bt_rows) {
+        next_row = nxt_row;
+      }
+      if (next_row >= 0 && !(next_row == win_row && next0 == win0)) {
+        pre_row = next_row;
+        pre0 = next0;
+        pre_val = window(next_row, next0);
+      }
     }
     const int32_t blk = __shfl_sync(0xffffffffu, win_val, cb - win0);
     const bool valid = blk >= 0 && blk < a.num_blocks;

@@ -115,8 +115,9 @@ def parse_args():
     p.add_argument("--cpu-seconds", type=float, default=10.0,
                    help="CPU work per CPU-baseline measurement")
     p.add_argument("--no-cpu-baseline", action="store_true")
-    p.add_argument("--rate", type=float, default=128.0,
-                   help="engine_load: arrivals per second over all GPUs")
+    p.add_argument("--rate", default="128",
+                   help="engine_load: arrivals per second over all GPUs (a comma list runs "
+                        "each rate in turn on the same replicas)")
     p.add_argument("--duration", type=float, default=30.0,
                    help="engine_load: seconds of arrivals")
     p.add_argument("--pool-gb", type=float, default=0.0,
@@ -1450,53 +1451,73 @@ def run_engine_load(args):
     prompts U[4, 2048], max_tokens U[32, 512], 256 concurrent and a queue of 1024
     per GPU, 512-token prefill budget, greedy): the global arrival stream is
     dealt round-robin to the GPUs, each serving its share in real time; latency
-    is measured on the host clock from each request's scheduled arrival."""
+    is measured on the host clock from each request's scheduled arrival.  Each
+    rate of --rate runs in turn on the same replicas (step graphs captured once,
+    before the first)."""
     import torch
     import torch.distributed as dist
 
     from batchstream_inference_engine_b200.backend import PagedBackend
-    from batchstream_inference_engine_b200.serve import (BlockBudget, load_summary,
+    from batchstream_inference_engine_b200.serve import (BlockBudget, Request, load_summary,
                                                           poisson_arrivals, run_open_loop)
     from batchstream_inference_engine_b200.torch_model import (QWEN25_05B, TorchModel,
                                                               random_weights)
 
+    rates = [float(r) for r in str(args.rate).split(",") if r.strip()]
     world, rank, dev = setup_process()
     model = TorchModel(QWEN25_05B, random_weights(), device=dev, dtype=torch.bfloat16)
     blocks = ENGINE_CONCURRENT * -(-(ENGINE_PROMPT[1] + ENGINE_MAX_TOKENS[1]) // BLOCK)
     backend = PagedBackend(model, blocks, BLOCK, ENGINE_PREFILL, max_seqs=ENGINE_CONCURRENT)
     graphs = model.warm_graphs(backend.pool)
-    arrivals = poisson_arrivals(args.rate, args.duration, seed=2000, prompt_range=ENGINE_PROMPT,
-                                max_tokens_range=ENGINE_MAX_TOKENS)
-    mine = [a for i, a in enumerate(arrivals) if i % world == rank]
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize(dev)
-    before = dict(model.stats)
-    with ClockSampler(dev) as clocks:
-        requests = run_open_loop(backend, mine, ENGINE_CONCURRENT, ENGINE_MAX_QUEUE,
-                                 BlockBudget(blocks, BLOCK), pipelined=True)
-    delta = {k: model.stats[k] - before[k] for k in model.stats}
-    rows = [(r.arrival, r.first_token_at, r.finished_at, r.status, len(r.tokens)) for r in requests]
-    if world > 1:
-        gathered = [None] * world
-        dist.all_gather_object(gathered, rows)
-        rows = [row for part in gathered for row in part]
-        steps = [None] * world
-        dist.all_gather_object(steps, delta)
-    else:
-        steps = [delta]
+    rnd = lambda x: None if x is None else round(x, 4)  # noqa: E731
+    results, launches, clock_list, last = [], 0, [], None
+    for rate in rates:
+        arrivals = poisson_arrivals(rate, args.duration, seed=2000, prompt_range=ENGINE_PROMPT,
+                                    max_tokens_range=ENGINE_MAX_TOKENS)
+        mine = [a for i, a in enumerate(arrivals) if i % world == rank]
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize(dev)
+        before = dict(model.stats)
+        with ClockSampler(dev) as clocks:
+            requests = run_open_loop(backend, mine, ENGINE_CONCURRENT, ENGINE_MAX_QUEUE,
+                                     BlockBudget(blocks, BLOCK), pipelined=True)
+        delta = {k: model.stats[k] - before[k] for k in model.stats}
+        rows = [(r.arrival, r.first_token_at, r.finished_at, r.status, len(r.tokens))
+                for r in requests]
+        if world > 1:
+            gathered = [None] * world
+            dist.all_gather_object(gathered, rows)
+            rows = [row for part in gathered for row in part]
+            steps = [None] * world
+            dist.all_gather_object(steps, delta)
+        else:
+            steps = [delta]
+        if rank == 0:
+            merged = []
+            for arrival, first, finish, status, n in rows:
+                r = Request([], 0, arrival=arrival, first_token_at=first, finished_at=finish,
+                            status=status)
+                r.tokens = [0] * n
+                merged.append(r)
+            summ = load_summary(merged)
+            total_steps = sum(d["steps"] for d in steps)
+            launches += sum(d["launches"] for d in steps)
+            clock_list.append(clocks.summary())
+            last = (summ, total_steps, delta)
+            results.append({
+                "rate": rate, "duration_s": args.duration,
+                "tokens_per_s": round(summ["tokens_per_s"], 1),
+                "makespan_s": round(summ["makespan_s"], 3), "steps": total_steps,
+                "ttft_p50_s": rnd(summ["ttft_p50_s"]), "ttft_p99_s": rnd(summ["ttft_p99_s"]),
+                "end_to_end_p50_s": rnd(summ["end_to_end_p50_s"]),
+                "end_to_end_p99_s": rnd(summ["end_to_end_p99_s"]),
+                "requests": {k: summ[k] for k in ("requests", "completed", "tokens",
+                                                  "rejected_queue_full", "rejected_too_large",
+                                                  "failed")},
+                "clocks": clocks.summary()})
     if rank == 0:
-        from batchstream_inference_engine_b200.serve import Request
-
-        merged = []
-        for arrival, first, finish, status, n in rows:
-            r = Request([], 0, arrival=arrival, first_token_at=first, finished_at=finish,
-                        status=status)
-            r.tokens = [0] * n
-            merged.append(r)
-        summ = load_summary(merged)
-        total_steps = sum(d["steps"] for d in steps)
-        rnd = lambda x: None if x is None else round(x, 4)  # noqa: E731
+        summ, total_steps, delta = last
         print(json.dumps({
             "metric": "engine tokens/s under open-loop Poisson load",
             "value": round(summ["tokens_per_s"], 1),
@@ -1511,28 +1532,23 @@ def run_engine_load(args):
             "dtype": "bf16",
             "data": "synthetic (seeded Poisson arrivals of token-id prompts, random-init weights)",
             "config": {
-                "workload": f"engine_load: open-loop Poisson {args.rate:g} requests/s over all GPUs "
-                            f"for {args.duration:g} s, prompts U{list(ENGINE_PROMPT)}, max_tokens "
+                "workload": f"engine_load: open-loop Poisson arrivals over all GPUs at "
+                            f"{', '.join(f'{r:g}' for r in rates)} requests/s, {args.duration:g} s "
+                            f"each, prompts U{list(ENGINE_PROMPT)}, max_tokens "
                             f"U{list(ENGINE_MAX_TOKENS)}, {ENGINE_CONCURRENT} concurrent and a queue "
                             f"of {ENGINE_MAX_QUEUE} per GPU, {ENGINE_PREFILL}-token prefill budget, "
                             f"greedy, block 16; {graphs} step graphs captured before the run",
-                "rate": args.rate, "duration_s": args.duration,
+                "rates": rates, "duration_s": args.duration,
                 "parallelism": f"dp{world} replicas, arrivals dealt round-robin",
+                "value_is": "the last rate's tokens/s",
             },
-            "latency": {"ttft_p50_s": rnd(summ["ttft_p50_s"]), "ttft_p99_s": rnd(summ["ttft_p99_s"]),
-                        "end_to_end_p50_s": rnd(summ["end_to_end_p50_s"]),
-                        "end_to_end_p99_s": rnd(summ["end_to_end_p99_s"]),
-                        "clock": "host wall clock from each request's scheduled arrival"},
-            "requests": {k: summ[k] for k in ("requests", "completed", "tokens",
-                                              "rejected_queue_full", "rejected_too_large",
-                                              "failed")},
-            "makespan_s": round(summ["makespan_s"], 3),
+            "by_rate": results,
             "e2e": {"value": round(summ["tokens_per_s"], 1), "unit": "tokens/s",
                     "h2d_bytes_per_step": round(delta["h2d_bytes"] / max(delta["steps"], 1)),
                     "d2h_bytes_per_step": round(delta["d2h_bytes"] / max(delta["steps"], 1)),
                     "path": "the serving loop is the public API"},
-            "gpu_launches": sum(d["launches"] for d in steps),
-            "clocks": clocks.summary(),
+            "gpu_launches": launches,
+            "clocks": clock_list[-1],
         }), flush=True)
     if world > 1:
         dist.barrier()
