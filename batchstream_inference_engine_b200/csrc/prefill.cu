@@ -52,13 +52,7 @@ constexpr int kKeys = 64;    // keys per KV tile (4 blocks)
 constexpr int kD = 64;
 constexpr int kKStages = 4;  // K ring depth
 constexpr int kVStages = 3;  // V ring depth
-// Warps 0-7 softmax (two per TMEM lane quarter, each on 32 of a tile's 64 keys),
-// warp 8 MMA issuer, warp 9 loader.
-constexpr int kSoftmaxThreads = 256;
-constexpr int kMmaWarp = 8;
-constexpr int kLoaderWarp = 9;
-constexpr int kThreads = 320;
-constexpr int kHalfKeys = 32;  // keys of a tile per softmax thread
+constexpr int kThreads = 192;  // warps 0-3 softmax, warp 4 MMA issuer, warp 5 loader
 constexpr int kTileBytes = kKeys * kD * 2;  // 8 KiB: K or V of one tile
 constexpr int kQBytes = kRows * kD * 2;     // 16 KiB
 constexpr int kPBytes = kRows * kKeys * 2;  // 16 KiB per P buffer
@@ -224,11 +218,6 @@ __global__ void __launch_bounds__(kThreads, 2)
   __shared__ uint64_t q_full, k_full[kKStages], k_empty[kKStages], v_full[kVStages],
       v_empty[kVStages], s_full[2], p_full[2], o_full, o_last, mma_done;
   __shared__ uint32_t tmem_base;
-  // The two softmax threads of a row exchange their halves' maxima (two
-  // buffers, by tile parity) and, at the end, their sums.
-  __shared__ float xch_max[2][2][kRows];
-  __shared__ float xch_sum[2][kRows];
-  __shared__ uint64_t xch_bar[4][2], sum_bar[4];  // 64 arrivals: the two warps of a lane quarter
 
   const uint32_t raw = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + (((raw + 1023u) & ~1023u) - raw);
@@ -279,12 +268,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&s_full[b], 1);
-      mbar_init(&p_full[b], kSoftmaxThreads);
-    }
-    for (int qq = 0; qq < 4; ++qq) {
-      mbar_init(&xch_bar[qq][0], 64);
-      mbar_init(&xch_bar[qq][1], 64);
-      mbar_init(&sum_bar[qq], 64);
+      mbar_init(&p_full[b], kRows);
     }
     mbar_init(&o_full, 1);
     mbar_init(&o_last, 1);
@@ -310,7 +294,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     return __all_sync(0xffffffffu, mbar_wait(bar, parity)) != 0;
   };
 
-  if (warp == kLoaderWarp) {
+  if (warp == 5) {
     // ---------------------------------------------------------------- loader
     // Table window: lane i holds entry 32 w + i of window w (0 past the row).
     auto fetch = [&](int w) {
@@ -386,7 +370,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       drained = wait_all(&v_full[t % kVStages], (t / kVStages) & 1) && drained;
     }
     if ((!ok || !drained) && lane == 0) set_status(a.status, kStatusWaitTimeout);
-  } else if (warp == kMmaWarp) {
+  } else if (warp == 4) {
     // ---------------------------------------------------------------- MMA issuer
     auto issue_s = [&](int j) {
       if (lane == 0) {
@@ -444,18 +428,9 @@ __global__ void __launch_bounds__(kThreads, 2)
     if ((!ok || !drained) && lane == 0) set_status(a.status, kStatusWaitTimeout);
   } else {
     // ---------------------------------------------------------------- softmax
-    // Two threads per query row: warp w reads TMEM lane quarter w % 4 (rows
-    // 32 (w % 4) ..), and half = w / 4 picks the tile's keys [32 half, 32 half
-    // + 32).  The pair exchanges its halves' maxima through shared memory once
-    // per tile (a 64-arrival mbarrier per lane quarter and tile parity, waited
-    // on with the usual bound), so both rescale and exponentiate against the
-    // same row maximum; each keeps its own part of the row sum and owns O's
-    // columns [32 half, 32 half + 32) in TMEM.
-    const int quarter = warp & 3, half = warp >> 2;
-    const int row = quarter * 32 + lane;  // TMEM lane and query row
+    const int row = tid;  // TMEM lane and query row
     const int qpos = prior + t0 + row;  // position of this row's token
-    const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
-    const uint32_t col0 = half * kHalfKeys;
+    const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
     // z = score * scale * log2(e); rows keep m (max z used for P) and l.
     const float zscale = (a.exact_scale ? a.scale : 1.f) * kLog2eP;
     float m_used = -INFINITY, l_run = 0.f;
@@ -466,29 +441,31 @@ __global__ void __launch_bounds__(kThreads, 2)
       tc_fence_after();
       // Scores rounded to bf16 (the reference's first rounding), kept as packed
       // pairs: lane bits [15:0] hold key 2i, [31:16] key 2i + 1.
-      uint32_t sp[kHalfKeys / 2];
+      uint32_t sp[kKeys / 2];
       {
-        uint32_t v0[32];
-        tmem_ld32(tmem + lane_base + (j & 1) * kKeys + col0, v0);
+        uint32_t v0[32], v1[32];
+        tmem_ld32(tmem + lane_base + (j & 1) * kKeys, v0);
+        tmem_ld32(tmem + lane_base + (j & 1) * kKeys + 32, v1);
         tmem_wait_ld();
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
           sp[i] = pack_bf16x2(__uint_as_float(v0[2 * i]), __uint_as_float(v0[2 * i + 1]));
+          sp[16 + i] = pack_bf16x2(__uint_as_float(v1[2 * i]), __uint_as_float(v1[2 * i + 1]));
         }
       }
       if (!a.exact_scale) {
 #pragma unroll
-        for (int i = 0; i < kHalfKeys / 2; ++i) {
+        for (int i = 0; i < kKeys / 2; ++i) {
           sp[i] = pack_bf16x2(__uint_as_float(sp[i] << 16) * a.scale,
                               __uint_as_float(sp[i] & 0xFFFF0000u) * a.scale);
         }
       }
-      const int key0 = (j_lo + j) * kKeys + col0;  // this thread's first key
-      // Halves wholly at or before the first row's position need no mask;
+      const int key0 = (j_lo + j) * kKeys;
+      // Tiles wholly at or before the first row's position need no mask;
       // masked keys become bf16 -inf.
-      if (key0 + kHalfKeys - 1 > prior + t0) {
+      if (key0 + kKeys - 1 > prior + t0) {
 #pragma unroll
-        for (int i = 0; i < kHalfKeys / 2; ++i) {
+        for (int i = 0; i < kKeys / 2; ++i) {
           const int k0 = key0 + 2 * i;
           const bool lo = k0 <= qpos && k0 < ctx, hi = k0 + 1 <= qpos && k0 + 1 < ctx;
           sp[i] = (lo ? (sp[i] & 0xFFFFu) : 0xFF80u) | (hi ? (sp[i] & 0xFFFF0000u) : 0xFF800000u);
@@ -496,15 +473,9 @@ __global__ void __launch_bounds__(kThreads, 2)
       }
       uint32_t mp[4] = {sp[0], sp[1], sp[2], sp[3]};
 #pragma unroll
-      for (int i = 4; i < kHalfKeys / 2; ++i) mp[i & 3] = max_bf16x2(mp[i & 3], sp[i]);
+      for (int i = 4; i < kKeys / 2; ++i) mp[i & 3] = max_bf16x2(mp[i & 3], sp[i]);
       const uint32_t m2 = max_bf16x2(max_bf16x2(mp[0], mp[1]), max_bf16x2(mp[2], mp[3]));
-      const float m_half = fmaxf(__uint_as_float(m2 << 16), __uint_as_float(m2 & 0xFFFF0000u));
-      // The row's maximum over both halves.
-      xch_max[j & 1][half][row] = m_half;
-      mbar_arrive(&xch_bar[quarter][j & 1]);
-      ok = wait_all(&xch_bar[quarter][j & 1], (j >> 1) & 1);
-      if (!ok) break;
-      const float m_tile = fmaxf(m_half, xch_max[j & 1][half ^ 1][row]);
+      const float m_tile = fmaxf(__uint_as_float(m2 << 16), __uint_as_float(m2 & 0xFFFF0000u));
       const float m_tile_z = m_tile * zscale;
       // Key 0 is visible to every row, so m_used is finite from the first tile
       // on when the range starts at key 0; a later range's first tiles may hide
@@ -513,34 +484,36 @@ __global__ void __launch_bounds__(kThreads, 2)
       if (j == 0) {
         m_used = m_tile_z;
       } else if (__any_sync(0xffffffffu, grow)) {
-        // tcgen05.ld/st are warp-collective: the warp rescales its columns if
-        // any row grew past the slack (factor 1 for the others).  Both warps of
-        // a lane quarter see the same rows, so they decide alike.
+        // tcgen05.ld/st are warp-collective: the warp rescales if any row
+        // grew past the slack (factor 1 for the others).
         ok = wait_all(&o_full, (j - 1) & 1);  // P V of the previous tile is done
         if (!ok) break;
         tc_fence_after();
         const float m_new = grow ? m_tile_z : m_used;
         const float corr = grow ? fast_exp2(m_used - m_new) : 1.f;
-        uint32_t v[32];
-        tmem_ld32(tmem + kTmemO + lane_base + col0, v);
-        tmem_wait_ld();
 #pragma unroll
-        for (int c = 0; c < 32; ++c) v[c] = __float_as_uint(__uint_as_float(v[c]) * corr);
-        tmem_st32(tmem + kTmemO + lane_base + col0, v);
+        for (int c0 = 0; c0 < kD; c0 += 32) {
+          uint32_t v[32];
+          tmem_ld32(tmem + kTmemO + lane_base + c0, v);
+          tmem_wait_ld();
+#pragma unroll
+          for (int c = 0; c < 32; ++c) v[c] = __float_as_uint(__uint_as_float(v[c]) * corr);
+          tmem_st32(tmem + kTmemO + lane_base + c0, v);
+        }
         tmem_wait_st();
         l_run *= corr;
         m_used = m_new;
       }
       // P = 2^(z - m_used) <= 2^8, packed to bf16 into P buffer j & 1 (free:
       // s_full of tile j implies the P V of tile j - 2 that read it is done).
-      // Sums kept in 4 partials, two per packed register.
+      // Sums kept in 8 partials (key index mod 8), two per packed register.
       float2 ps[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f),
                       make_float2(0.f, 0.f)};
       const float m_base = m_used == -INFINITY ? 0.f : m_used;  // no -inf - -inf
       const float2 zs = make_float2(zscale, zscale), mm = make_float2(-m_base, -m_base);
       uint8_t* prow = sP(j & 1);
 #pragma unroll
-      for (int ch = 0; ch < kHalfKeys / 8; ++ch) {
+      for (int ch = 0; ch < kKeys / 8; ++ch) {
         uint32_t w[4];
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
@@ -551,21 +524,18 @@ __global__ void __launch_bounds__(kThreads, 2)
           ps[e] = __fadd2_rn(ps[e], pe);
           w[e] = pack_bf16x2(pe.x, pe.y);
         }
-        *reinterpret_cast<uint4*>(prow + swz128(row, half * 4 * 8 + ch * 8)) =
-            make_uint4(w[0], w[1], w[2], w[3]);
+        *reinterpret_cast<uint4*>(prow + swz128(row, ch * 8)) = make_uint4(w[0], w[1], w[2], w[3]);
       }
       l_run += ((ps[0].x + ps[0].y) + (ps[1].x + ps[1].y)) + ((ps[2].x + ps[2].y) + (ps[3].x + ps[3].y));
       // Keys no row of this CTA sees (past the context, or past the last row's
       // position): their V rows hold stale pool data or never-loaded shared
       // memory, possibly NaN, which would poison 0 * V in the tensor core.
-      // The first half's threads of rows 0-63 own V row `row`.
-      const int tile0 = (j_lo + j) * kKeys;
-      if (half == 0 && j == ntiles - 1 && row < kKeys && tile0 + kKeys > kv_end) {
+      if (j == ntiles - 1 && row < kKeys && key0 + kKeys > kv_end) {
         // The V tile must have landed before its tail rows are overwritten.
         ok = wait_all(&v_full[j % kVStages], (j / kVStages) & 1);
         if (!ok) break;
       }
-      if (half == 0 && row < kKeys && tile0 + row >= kv_end) {
+      if (row < kKeys && key0 + row >= kv_end) {
         uint4 z = make_uint4(0u, 0u, 0u, 0u);
         uint8_t* vrow = sV(j % kVStages) + row * 128;
 #pragma unroll
@@ -576,56 +546,53 @@ __global__ void __launch_bounds__(kThreads, 2)
       mbar_arrive(&p_full[j & 1]);
     }
     if (ok) ok = wait_all(&o_last, 0);
-    // The row's sum: this thread's part plus its partner's.
-    float l_row = l_run;
-    if (ok) {
-      xch_sum[half][row] = l_run;
-      mbar_arrive(&sum_bar[quarter]);
-      ok = wait_all(&sum_bar[quarter], 0);
-      if (ok) l_row = xch_sum[0][row] + xch_sum[1][row];
-    }
     if (ok && nsplit > 1) {
       tc_fence_after();
       // One record per CTA: unnormalised O, then (max, sum) of the row.
       const int64_t rec = static_cast<int64_t>(item) * a.splits + sp;
-      float* orow = a.part_o + (rec * kRows + row) * kD + col0;
-      uint32_t v[32];
-      tmem_ld32(tmem + kTmemO + lane_base + col0, v);
-      tmem_wait_ld();
+      float* orow = a.part_o + (rec * kRows + row) * kD;
 #pragma unroll
-      for (int c = 0; c < 32; c += 4) {
-        *reinterpret_cast<float4*>(orow + c) =
-            make_float4(__uint_as_float(v[c]), __uint_as_float(v[c + 1]),
-                        __uint_as_float(v[c + 2]), __uint_as_float(v[c + 3]));
+      for (int c0 = 0; c0 < kD; c0 += 32) {
+        uint32_t v[32];
+        tmem_ld32(tmem + kTmemO + lane_base + c0, v);
+        tmem_wait_ld();
+#pragma unroll
+        for (int c = 0; c < 32; c += 4) {
+          *reinterpret_cast<float4*>(orow + c0 + c) =
+              make_float4(__uint_as_float(v[c]), __uint_as_float(v[c + 1]),
+                          __uint_as_float(v[c + 2]), __uint_as_float(v[c + 3]));
+        }
       }
-      if (half == 0) {
-        *reinterpret_cast<float2*>(a.part_ml + (rec * kRows + row) * 2) = make_float2(m_used, l_row);
-      }
+      *reinterpret_cast<float2*>(a.part_ml + (rec * kRows + row) * 2) = make_float2(m_used, l_run);
     } else if (ok) {
       tc_fence_after();
       // Every lane reads its TMEM row (warp-collective); rows past the chunk
       // are not stored.
-      const float inv = 1.f / l_row;
       const bool store = t0 + row < n;
       __nv_bfloat16* dst = static_cast<__nv_bfloat16*>(a.out) +
                            static_cast<int64_t>(tok0 + t0 + (store ? row : 0)) * a.o_stride_tok +
-                           static_cast<int64_t>(h) * kD + col0;
-      uint32_t v[32];
-      tmem_ld32(tmem + kTmemO + lane_base + col0, v);
-      tmem_wait_ld();
-      if (store) {
+                           static_cast<int64_t>(h) * kD;
+      const float inv = 1.f / l_run;
 #pragma unroll
-        for (int c = 0; c < 32; c += 8) {
-          uint4 w;
-          w.x = pack_bf16x2(__uint_as_float(v[c]) * inv, __uint_as_float(v[c + 1]) * inv);
-          w.y = pack_bf16x2(__uint_as_float(v[c + 2]) * inv, __uint_as_float(v[c + 3]) * inv);
-          w.z = pack_bf16x2(__uint_as_float(v[c + 4]) * inv, __uint_as_float(v[c + 5]) * inv);
-          w.w = pack_bf16x2(__uint_as_float(v[c + 6]) * inv, __uint_as_float(v[c + 7]) * inv);
-          *reinterpret_cast<uint4*>(dst + c) = w;
+      for (int c0 = 0; c0 < kD; c0 += 32) {
+        uint32_t v[32];
+        tmem_ld32(tmem + kTmemO + lane_base + c0, v);
+        tmem_wait_ld();
+        if (store) {
+#pragma unroll
+          for (int c = 0; c < 32; c += 8) {
+            uint4 w;
+            w.x = pack_bf16x2(__uint_as_float(v[c]) * inv, __uint_as_float(v[c + 1]) * inv);
+            w.y = pack_bf16x2(__uint_as_float(v[c + 2]) * inv, __uint_as_float(v[c + 3]) * inv);
+            w.z = pack_bf16x2(__uint_as_float(v[c + 4]) * inv, __uint_as_float(v[c + 5]) * inv);
+            w.w = pack_bf16x2(__uint_as_float(v[c + 6]) * inv, __uint_as_float(v[c + 7]) * inv);
+            *reinterpret_cast<uint4*>(dst + c0 + c) = w;
+          }
         }
       }
+    } else if (tid == 0) {
+      set_status(a.status, kStatusWaitTimeout);
     }
-    if (!ok && lane == 0) set_status(a.status, kStatusWaitTimeout);
   }
   tc_fence_before();
   __syncthreads();
