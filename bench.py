@@ -1271,8 +1271,22 @@ def engine_core(args, world, rank, dev, steps, warmup, clocks=None):
     ms = t0.elapsed_time(t1)
     delta = {k: model.stats[k] - before[k] for k in model.stats}
     flops = model_flops(delta, QWEN25_05B, QWEN25_05B_VOCAB, QWEN25_05B_INTERMEDIATE)
+    # The same loop for half as many steps without the token gather: what the
+    # gather costs each rank (at one GPU there is no collective either way).
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize(dev)
+    quiet = max(1, steps // 2)
+    u0 = torch.cuda.Event(enable_timing=True)
+    u1 = torch.cuda.Event(enable_timing=True)
+    u0.record(stream)
+    for _ in range(quiet):
+        sched.step()
+    u1.record(stream)
+    torch.cuda.synchronize(dev)
+    ms_quiet = u0.elapsed_time(u1) / quiet
     per_rank = gather_rows([ms, wall * 1e3, waited[0] * 1e3, float(delta["tokens"]),
-                            float(delta["rows"]), float(delta["steps"])], dev, world)
+                            float(delta["rows"]), float(delta["steps"]), ms_quiet], dev, world)
     (ms_max,), (job_flops, job_tokens) = max_over_ranks(
         [ms], [float(flops), float(delta["tokens"])], dev, world)
     if world > 1:
@@ -1285,6 +1299,7 @@ def engine_core(args, world, rank, dev, steps, warmup, clocks=None):
         dev_ms = [r[0] for r in per_rank]
         wall_ms = [r[1] for r in per_rank]
         wait_ms = [r[2] for r in per_rank]
+        quiet_ms = [r[6] for r in per_rank]
         result = {
             "metric": "engine tokens/s",
             "value": round(value, 1),
@@ -1319,10 +1334,11 @@ def engine_core(args, world, rank, dev, steps, warmup, clocks=None):
                 "ms_per_step": [round(x / steps, 4) for x in dev_ms],
                 "host_ms_per_step": [round(x / steps, 4) for x in wall_ms],
                 "gather_wait_ms_per_step": [round(x / steps, 4) for x in wait_ms],
+                "ms_per_step_without_gather": [round(x, 4) for x in quiet_ms],
                 "processed_tokens": [int(r[3]) for r in per_rank],
                 "rows": [int(r[4]) for r in per_rank],
             },
-            "limiter": engine_limiter(dev_ms, wall_ms, wait_ms, world),
+            "limiter": engine_limiter([x / steps for x in dev_ms], quiet_ms, world),
             "roofline": {
                 "bound": "tensor",
                 "kernel": "whole engine step (cuBLAS GEMMs + this package's attention kernels)",
@@ -1343,28 +1359,23 @@ def engine_core(args, world, rank, dev, steps, warmup, clocks=None):
     return result
 
 
-def engine_limiter(dev_ms, wall_ms, wait_ms, world):
-    """Names what bounds the multi-GPU engine from the per-rank figures: a
-    straggler (the slowest rank's device time over the median), the token
-    gather (host time spent waiting for it), or host scheduling (host time per
-    step above device time)."""
-    med = statistics.median(dev_ms)
-    worst = max(dev_ms)
-    gather_share = max(w / t for w, t in zip(wait_ms, wall_ms)) if world > 1 else 0.0
-    host_share = max(h / d for h, d in zip(wall_ms, dev_ms)) - 1.0
-    notes = {"straggler_over_median": round(worst / med - 1.0, 4),
-             "gather_wait_share_of_host_time": round(gather_share, 4),
-             "host_over_device_time": round(host_share, 4)}
+def engine_limiter(step_ms, quiet_ms, world):
+    """Names what bounds the multi-GPU engine from per-rank step times: a
+    straggler (the slowest rank over the median), or the token gather (a rank's
+    step with the gather over the same loop without it), or neither."""
+    med = statistics.median(step_ms)
+    straggler = max(step_ms) / med - 1.0
+    gather = max(s / q - 1.0 for s, q in zip(step_ms, quiet_ms))
+    notes = {"straggler_over_median": round(straggler, 4),
+             "gather_cost_over_step": round(gather, 4)}
     if world == 1:
         notes["named"] = "single GPU (no gather)"
-    elif gather_share > 0.05:
-        notes["named"] = "token gather"
-    elif worst / med - 1.0 > 0.03:
+    elif straggler > 0.03:
         notes["named"] = "straggler rank"
-    elif host_share > 0.05:
-        notes["named"] = "host scheduling"
+    elif gather > 0.03:
+        notes["named"] = "token gather"
     else:
-        notes["named"] = "none above 3-5%: ranks run at their single-GPU rate"
+        notes["named"] = "none above 3%: every rank steps at its rate without the gather"
     return notes
 
 
