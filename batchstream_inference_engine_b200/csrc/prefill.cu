@@ -25,8 +25,11 @@
 //   * MMA issuer (warp 4), from one thread:
 //       S  = Q K^T   tcgen05.mma kind::f16, M=128 N=64 K=64  -> TMEM, 2 buffers
 //       O += P V     tcgen05.mma kind::f16, M=128 N=64 K=64  -> TMEM
-//     in the order PV(j), S(j+2): the tensor core computes the scores two tiles
-//     ahead while the softmax warps work on tile j+1;
+//     in steps of PV(j), S(j+2) and ONE commit: the tensor core computes the
+//     scores two tiles ahead while the softmax warps work on tile j+1.  Each
+//     tcgen05 instruction takes the issuing thread tens of nanoseconds, so a
+//     step waits for all its operands first and signals every consumer (the
+//     softmax, the loader's K and V stages) through that single commit;
 //   * softmax (warps 0-3) own the 128 query
 // rows (TMEM lane = row): they read their row of S (tcgen05.ld), apply the
 // reference's rounding points (bf16(bf16(q.k) * scale); the second rounding is
@@ -52,6 +55,9 @@ constexpr int kKeys = 64;    // keys per KV tile (4 blocks)
 constexpr int kD = 64;
 constexpr int kKStages = 4;  // K ring depth
 constexpr int kVStages = 3;  // V ring depth
+constexpr int kSteps = 4;    // MMA step barriers (>= kKStages, >= kVStages + 1)
+static_assert(kSteps >= kKStages && kSteps >= kVStages + 1 && kSteps >= 3,
+              "a step waiter could fall a whole ring of step barriers behind");
 constexpr int kThreads = 192;  // warps 0-3 softmax, warp 4 MMA issuer, warp 5 loader
 constexpr int kTileBytes = kKeys * kD * 2;  // 8 KiB: K or V of one tile
 constexpr int kQBytes = kRows * kD * 2;     // 16 KiB
@@ -212,11 +218,14 @@ __global__ void __launch_bounds__(kThreads, 2)
     prefill_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap kmap,
                    const __grid_constant__ CUtensorMap vmap, const PrefillArgs a) {
   extern __shared__ uint8_t smem_raw[];
-  // o_full completes once per P V product (the rescale waits for the previous
-  // tile's); o_last once, after the last one: a parity wait on o_full could not
-  // tell "done" from "two products behind" at the end.
-  __shared__ uint64_t q_full, k_full[kKStages], k_empty[kKStages], v_full[kVStages],
-      v_empty[kVStages], s_full[2], p_full[2], o_full, o_last, mma_done;
+  // MMA step u issues P V(u - 2) (u >= 2), then S(u) (u < ntiles), and makes
+  // one commit, to step_done[u % kSteps]: "S(j) is in TMEM", "K stage of S(j)
+  // is free", "P V(t) is done" and "V stage of P V(t) is free" are all waits on
+  // the step that holds the product (a commit completes once every MMA issued
+  // before it has).  Every waiter checks a step less than kSteps steps behind
+  // the newest one that can complete, so a parity wait is never ambiguous.
+  __shared__ uint64_t q_full, k_full[kKStages], v_full[kVStages], step_done[kSteps], p_full[2],
+      mma_done;
   __shared__ uint32_t tmem_base;
 
   const uint32_t raw = smem_u32(smem_raw);
@@ -258,20 +267,10 @@ __global__ void __launch_bounds__(kThreads, 2)
 
   if (tid == 0) {
     mbar_init(&q_full, 1);
-    for (int s = 0; s < kKStages; ++s) {
-      mbar_init(&k_full[s], 1);
-      mbar_init(&k_empty[s], 1);
-    }
-    for (int s = 0; s < kVStages; ++s) {
-      mbar_init(&v_full[s], 1);
-      mbar_init(&v_empty[s], 1);
-    }
-    for (int b = 0; b < 2; ++b) {
-      mbar_init(&s_full[b], 1);
-      mbar_init(&p_full[b], kRows);
-    }
-    mbar_init(&o_full, 1);
-    mbar_init(&o_last, 1);
+    for (int s = 0; s < kKStages; ++s) mbar_init(&k_full[s], 1);
+    for (int s = 0; s < kVStages; ++s) mbar_init(&v_full[s], 1);
+    for (int s = 0; s < kSteps; ++s) mbar_init(&step_done[s], 1);
+    for (int b = 0; b < 2; ++b) mbar_init(&p_full[b], kRows);
     mbar_init(&mma_done, 1);
     fence_barrier_init();
   }
@@ -293,6 +292,7 @@ __global__ void __launch_bounds__(kThreads, 2)
   auto wait_all = [&](uint64_t* bar, uint32_t parity) {
     return __all_sync(0xffffffffu, mbar_wait(bar, parity)) != 0;
   };
+  auto wait_step = [&](int u) { return wait_all(&step_done[u % kSteps], (u / kSteps) & 1); };
 
   if (warp == 5) {
     // ---------------------------------------------------------------- loader
@@ -335,8 +335,9 @@ __global__ void __launch_bounds__(kThreads, 2)
       if (i < ntiles) {
         const int st = i % kKStages;
         if (i >= kKStages) {
-          // K stage st is free once S of tile i - kKStages has read it.
-          ok = wait_all(&k_empty[st], ((i - kKStages) / kKStages) & 1);
+          // K stage st is free once S of tile i - kKStages has read it (step
+          // i - kKStages; step i cannot complete before K(i) lands).
+          ok = wait_step(i - kKStages);
           if (!ok) break;
         }
         if (((j_lo + i) * 4) / 32 != win) {
@@ -353,8 +354,9 @@ __global__ void __launch_bounds__(kThreads, 2)
       if (t >= 0 && t < ntiles) {
         const int st = t % kVStages;
         if (t >= kVStages) {
-          // V stage st is free once P V of tile t - kVStages has read it.
-          ok = wait_all(&v_empty[st], ((t - kVStages) / kVStages) & 1);
+          // V stage st is free once P V of tile t - kVStages has read it (step
+          // t - kVStages + 2; that step + kSteps needs V(t + 1), not loaded yet).
+          ok = wait_step(t - kVStages + 2);
           if (!ok) break;
         }
         load(&vmap, sV(st), &v_full[st], vblk);
@@ -372,53 +374,41 @@ __global__ void __launch_bounds__(kThreads, 2)
     if ((!ok || !drained) && lane == 0) set_status(a.status, kStatusWaitTimeout);
   } else if (warp == 4) {
     // ---------------------------------------------------------------- MMA issuer
-    auto issue_s = [&](int j) {
-      if (lane == 0) {
-        const int st = j % kKStages;
-        const uint32_t d = tmem + (j & 1) * kKeys;
-#pragma unroll
-        for (int k = 0; k < kD / 16; ++k) {
-          umma_f16(d, umma_desc(smem_u32(sQ) + 32 * k, 16, 1024),
-                   umma_desc(smem_u32(sK(st)) + 32 * k, 16, 1024), kIdescS, k > 0 ? 1u : 0u);
-        }
-        umma_commit(&s_full[j & 1]);
-        umma_commit(&k_empty[st]);
-      }
-      __syncwarp();
-    };
     bool ok = wait_all(&q_full, 0);
-    // Scores of the first two tiles.
-    for (int j = 0; j < 2 && j < ntiles && ok; ++j) {
-      ok = wait_all(&k_full[j % kKStages], (j / kKStages) & 1);
-      if (!ok) break;
-      tc_fence_after();
-      issue_s(j);
-    }
-    for (int j = 0; j < ntiles && ok; ++j) {
-      const int st = j % kVStages;
-      ok = wait_all(&p_full[j & 1], (j >> 1) & 1) && wait_all(&v_full[st], (j / kVStages) & 1);
+    for (int u = 0; u < ntiles + 2 && ok; ++u) {
+      // Step u: P V(j = u - 2) once softmax(j) has written P(j) (which also
+      // frees S buffer j & 1), then S(u) into that buffer, then one commit.
+      // The waits come first, so the step's MMAs issue back to back.
+      const int j = u - 2;
+      if (j >= 0) {
+        ok = wait_all(&p_full[j & 1], (j >> 1) & 1) &&
+             wait_all(&v_full[j % kVStages], (j / kVStages) & 1);
+      }
+      if (ok && u < ntiles) ok = wait_all(&k_full[u % kKStages], (u / kKStages) & 1);
       if (!ok) break;
       tc_fence_after();
       if (lane == 0) {
-        const uint32_t p0 = smem_u32(sP(j & 1));
-        const uint32_t v0 = smem_u32(sV(st));
+        if (j >= 0) {
+          const uint32_t p0 = smem_u32(sP(j & 1));
+          const uint32_t v0 = smem_u32(sV(j % kVStages));
 #pragma unroll
-        for (int k = 0; k < kKeys / 16; ++k) {
-          umma_f16(tmem + kTmemO, umma_desc(p0 + 32 * k, 16, 1024),
-                   umma_desc(v0 + 2048 * k, 8192, 1024), kIdescO, (j > 0 || k > 0) ? 1u : 0u);
+          for (int k = 0; k < kKeys / 16; ++k) {
+            umma_f16(tmem + kTmemO, umma_desc(p0 + 32 * k, 16, 1024),
+                     umma_desc(v0 + 2048 * k, 8192, 1024), kIdescO, (j > 0 || k > 0) ? 1u : 0u);
+          }
         }
-        umma_commit(&o_full);
-        umma_commit(&v_empty[st]);
-        if (j == ntiles - 1) umma_commit(&o_last);
+        if (u < ntiles) {
+          const uint32_t d = tmem + (u & 1) * kKeys;
+          const uint32_t k0 = smem_u32(sK(u % kKStages));
+#pragma unroll
+          for (int k = 0; k < kD / 16; ++k) {
+            umma_f16(d, umma_desc(smem_u32(sQ) + 32 * k, 16, 1024),
+                     umma_desc(k0 + 32 * k, 16, 1024), kIdescS, k > 0 ? 1u : 0u);
+          }
+        }
+        umma_commit(&step_done[u % kSteps]);
       }
       __syncwarp();
-      if (j + 2 < ntiles) {
-        // S buffer j & 1 is free: softmax(j) read it before arriving on p_full.
-        ok = wait_all(&k_full[(j + 2) % kKStages], ((j + 2) / kKStages) & 1);
-        if (!ok) break;
-        tc_fence_after();
-        issue_s(j + 2);
-      }
     }
     // Drain: no MMA may still use TMEM once the CTA frees it.  The commit
     // tracks every MMA issued above.
@@ -436,7 +426,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     float m_used = -INFINITY, l_run = 0.f;
     bool ok = true;
     for (int j = 0; j < ntiles; ++j) {
-      ok = wait_all(&s_full[j & 1], (j >> 1) & 1);
+      ok = wait_step(j);  // S(j) is in TMEM
       if (!ok) break;
       tc_fence_after();
       // Scores rounded to bf16 (the reference's first rounding), kept as packed
@@ -486,7 +476,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       } else if (__any_sync(0xffffffffu, grow)) {
         // tcgen05.ld/st are warp-collective: the warp rescales if any row
         // grew past the slack (factor 1 for the others).
-        ok = wait_all(&o_full, (j - 1) & 1);  // P V of the previous tile is done
+        ok = wait_step(j + 1);  // P V of the previous tile is done
         if (!ok) break;
         tc_fence_after();
         const float m_new = grow ? m_tile_z : m_used;
@@ -505,7 +495,7 @@ __global__ void __launch_bounds__(kThreads, 2)
         m_used = m_new;
       }
       // P = 2^(z - m_used) <= 2^8, packed to bf16 into P buffer j & 1 (free:
-      // s_full of tile j implies the P V of tile j - 2 that read it is done).
+      // the step of S(j) also holds the P V of tile j - 2 that read it).
       // Sums kept in 8 partials (key index mod 8), two per packed register.
       float2 ps[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f),
                       make_float2(0.f, 0.f)};
@@ -545,7 +535,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       tc_fence_before();
       mbar_arrive(&p_full[j & 1]);
     }
-    if (ok) ok = wait_all(&o_last, 0);
+    if (ok) ok = wait_step(ntiles + 1);  // the last P V is done
     if (ok && nsplit > 1) {
       tc_fence_after();
       // One record per CTA: unnormalised O, then (max, sum) of the row.
