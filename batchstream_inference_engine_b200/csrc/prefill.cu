@@ -182,10 +182,10 @@ __device__ __forceinline__ void item_work(const PrefillArgs& a, int b, Work& w) 
   const int t = a.qtiles - 1 - rt / a.num_rows;
   w.r = rt % a.num_rows;
   w.t0 = t * kRows;
-  w.tok0 = __ldg(a.cu_q + w.r);
-  w.n = __ldg(a.cu_q + w.r + 1) - w.tok0;
-  w.ctx = __ldg(a.context_lens + w.r);
-  w.row_tab = a.seq_rows != nullptr ? __ldg(a.seq_rows + w.r) : w.r;
+  w.tok0 = __ldcg(a.cu_q + w.r);
+  w.n = __ldcg(a.cu_q + w.r + 1) - w.tok0;
+  w.ctx = __ldcg(a.context_lens + w.r);
+  w.row_tab = a.seq_rows != nullptr ? __ldcg(a.seq_rows + w.r) : w.r;
 }
 
 // Work of CTA b: entry b / H of the plan (head b % H), or the plan-less
@@ -197,9 +197,11 @@ __device__ __forceinline__ bool cta_work(const PrefillArgs& a, int b, Work& w) {
   }
   const int H = a.num_heads;
   const int d = b / H;  // < rows * qtiles * splits: inside the plan
-  const int4 head = __ldg(a.plan);
-  const int4 x = __ldg(a.plan + 1 + 2 * d);
-  const int4 y = __ldg(a.plan + 2 + 2 * d);
+  // Coherent loads: the plan kernel just ahead writes these while this grid,
+  // launched early, is already resident (no read-only cache path for them).
+  const int4 head = __ldcg(a.plan);
+  const int4 x = __ldcg(a.plan + 1 + 2 * d);
+  const int4 y = __ldcg(a.plan + 2 + 2 * d);
   if (d >= head.x) return false;
   w.h = b % H;
   w.sp = x.x % a.splits;
@@ -684,11 +686,11 @@ __global__ void __launch_bounds__(kPlanThreads) prefill_plan_kernel(const Prefil
   if (tid < n_slot) {
     const int rt = tid / S, p = tid % S;
     const int r = rt % R, t0 = (Q - 1 - rt / R) * kRows;
-    const int tok0 = __ldg(a.cu_q + r);
-    const int n = __ldg(a.cu_q + r + 1) - tok0;
-    const int ctx = __ldg(a.context_lens + r);
+    const int tok0 = __ldcg(a.cu_q + r);
+    const int n = __ldcg(a.cu_q + r + 1) - tok0;
+    const int ctx = __ldcg(a.context_lens + r);
     if (p == 0) {
-      const int row_tab = a.seq_rows != nullptr ? __ldg(a.seq_rows + r) : r;
+      const int row_tab = a.seq_rows != nullptr ? __ldcg(a.seq_rows + r) : r;
       s_row[rt] = make_int4(tok0, n, ctx, row_tab);
     }
     int tiles = 0;

@@ -587,7 +587,7 @@ def prefill_attention(query: torch.Tensor, key_pool: torch.Tensor, value_pool: t
                       scaling: float, max_query_len: int, seq_rows: torch.Tensor | None = None,
                       out: torch.Tensor | None = None, per_token: bool = False,
                       max_blocks_per_seq: int | None = None) -> torch.Tensor:
-    """Causal attention of prompt chunks over their paged context, in one launch.
+    """Causal attention of prompt chunks over their paged context, in one call.
 
     query [T, H, D] holds the chunks back to back (chunk r is rows cu_q[r] ..
     cu_q[r+1]); context_lens[r] counts the sequence's cached tokens including the

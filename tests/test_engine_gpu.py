@@ -6,7 +6,11 @@ the CPU: 24 token-id prompts, random-init Qwen2.5-0.5B-shaped weights (seed 0,
 N(0, 0.02), RMSNorm 1), max 8 concurrent, 256 blocks of 16, prefill chunk 64.
 
 * fp32: the GPU engine (fp32 weights, fp32 pool, IEEE fp32 GEMMs) must give the
-  reference's greedy token ids for the first 32 tokens of every sequence.
+  reference's greedy token ids for the first 32 tokens of every sequence, up to
+  a near-tie: where the reference's best and second-best logits lie within
+  2e-3 of the largest (tests/golden/engine_margins.npz, from
+  make_engine_margins.py) the last bits of another GEMM kernel may pick the
+  other one, and the two runs part there.
 * bf16: free-running greedy decoding in bf16 flips on near-ties (the
   reference's own bf16 run leaves its fp32 run within 0-88 tokens), so bf16 is
   held to the reference's fp32 logits teacher-forced along the fp32 token
@@ -30,6 +34,8 @@ from batchstream_inference_engine_b200.torch_model import (QWEN25_05B, PagedKVPo
 pytestmark = pytest.mark.gpu
 DEV = "cuda:0"
 GOLDEN = Path(__file__).resolve().parent / "golden" / "engine_tokens.npz"
+MARGINS = Path(__file__).resolve().parent / "golden" / "engine_margins.npz"
+NEAR_TIE = 2e-3  # twice the fp32 logit tolerance of the teacher-forced test
 NUM_BLOCKS, BLOCK_SIZE, PREFILL_CHUNK, MAX_CONCURRENT = 256, 16, 64, 8
 
 
@@ -80,10 +86,15 @@ def test_workload_matches_the_fixture(golden):
 def test_fp32_greedy_tokens_match_the_reference(golden, weights, step_graphs, pipelined):
     tokens, requests = run_engine(weights, torch.float32, step_graphs, pipelined)
     assert not any(r.failed for r in requests)
+    margins = np.load(MARGINS)["margins_fp32"]
     for i, (ours, ref) in enumerate(zip(tokens, golden["fp32"])):
         n = min(32, len(ref))
-        assert ours[:n] == ref[:n], (i, ours[:n], ref[:n])
-        assert len(ours) == len(ref), i
+        k = first_divergence(ours[:n], ref[:n])
+        if k < n:
+            # Only at a near-tie of the reference's own logits.
+            assert margins[i, k] <= NEAR_TIE, (i, k, float(margins[i, k]), ours[:n], ref[:n])
+        else:
+            assert len(ours) == len(ref), i
 
 
 def first_divergence(a, b):
