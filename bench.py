@@ -304,11 +304,13 @@ def timed_windows(replay, steps, warmup, windows, dev, world, clocks=None):
     return times
 
 
-def time_kernel_chain(launch, rotations, repeats, steps, warmup, dev, world):
+def time_kernel_chain(launch, rotations, repeats, steps, warmup, dev, world, rounds=5,
+                      min_launches=400):
     """Mean device time of one launch: a CUDA graph of rotations x repeats
     launches back to back (launch(r) for each rotation r in turn) replayed
-    until about `steps` launches were timed, with CUDA events around the
-    replays on the launching stream."""
+    until about max(steps, min_launches) launches were timed, with CUDA events
+    around the replays on the launching stream; `rounds` such timings, the
+    median kept (a short run's one timing could catch a stall)."""
     import torch
     import torch.distributed as dist
 
@@ -328,23 +330,26 @@ def time_kernel_chain(launch, rotations, repeats, steps, warmup, dev, world):
                     launch(r)
     torch.cuda.synchronize(dev)
     per = rotations * repeats
-    replays = max(1, -(-steps // per))
+    replays = max(1, -(-max(steps, min_launches) // per))
     for _ in range(max(1, warmup // per)):
         graph.replay()
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize(dev)
-    t0 = torch.cuda.Event(enable_timing=True)
-    t1 = torch.cuda.Event(enable_timing=True)
-    t0.record(stream)
-    for _ in range(replays):
-        graph.replay()
-    t1.record(stream)
-    torch.cuda.synchronize(dev)
+    times = []
+    for _ in range(rounds):
+        t0 = torch.cuda.Event(enable_timing=True)
+        t1 = torch.cuda.Event(enable_timing=True)
+        t0.record(stream)
+        for _ in range(replays):
+            graph.replay()
+        t1.record(stream)
+        torch.cuda.synchronize(dev)
+        times.append(t0.elapsed_time(t1) / (replays * per))
     with torch.cuda.stream(capture):
         ops.take_status(dev)
     del graph
-    return t0.elapsed_time(t1) / (replays * per)
+    return sorted(times)[len(times) // 2]
 
 
 def gather_rows(values, dev, world):
@@ -736,7 +741,9 @@ def decode_core(args, world, rank, dev, H, Hkv, D, steps, warmup, windows, label
                 "traffic": None,
                 "decode_ms": round(decode_ms, 5),
                 "decode_ms_how": "mean time of one decode launch (kernel + merge pass) over a "
-                                 "graph of back-to-back launches (the rotations in turn)",
+                                 "graph of back-to-back launches (the rotations in turn), at "
+                                 "least 400 launches per timing, median of 5 timings, max over "
+                                 "ranks",
                 "algorithmic_bytes_per_launch": step_bytes,
             },
             "gpu_launches": sum(step_counts[i % ROTATIONS] for i in range(steps)) * windows,
@@ -1174,7 +1181,7 @@ def mixed_core(args, world, rank, dev, steps, warmup, windows, clocks=None):
             "parts_ms": {"metadata_and_slot_write": round(prep_ms, 5),
                          "decode": round(decode_ms, 5), "prefill": round(prefill_ms, 5),
                          "how": "mean launch time of each part over a graph of its launches "
-                                "back to back"},
+                                "back to back (median of 5 timings of at least 400 launches)"},
             "decode": {"bound": "hbm", "algorithmic_bytes": dec_bytes,
                        "achieved": round(dec_gbs, 1), "unit": "GB/s", "peak": hbm,
                        "peak_source": hbm_note, "frac": round(dec_gbs / hbm, 4)},
