@@ -736,7 +736,10 @@ int bs_prefill_attention(const void* query, int64_t query_token_stride, const in
     if (wsb < prefill_ws_bytes(items, p.splits, 0)) p.splits = 1;
     int64_t rts =
         prefill_plan_rts(num_rows, p.qtiles, num_tokens, num_heads, p.splits, d->sms);
-    if (wsb < prefill_ws_bytes(items, p.splits, rts * p.splits)) rts = 0;
+    // A batch with few enough (row, query tile) pairs ranks them in every CTA:
+    // no plan launch to wait for, and no plan in the workspace.
+    p.rank_in_cta = rts > 0 && p.splits == 1 && rts <= bsb::kMaxCtaRankedRts ? 1 : 0;
+    if (p.rank_in_cta || wsb < prefill_ws_bytes(items, p.splits, rts * p.splits)) rts = 0;
     float* records = reinterpret_cast<float*>(ws + prefill_split_offset());
     p.part_o = records;
     p.part_ml = records + items * p.splits * bsb::kPrefillRecordO;

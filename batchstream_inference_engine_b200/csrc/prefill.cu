@@ -216,6 +216,62 @@ __device__ __forceinline__ bool cta_work(const PrefillArgs& a, int b, Work& w) {
   return true;
 }
 
+// Work of CTA b when it ranks the (row, query tile) pairs itself: the plan
+// kernel's order for a batch without splits (one entry per pair, most key tiles
+// first, ties by index), computed by every CTA in shared memory that nothing
+// uses yet instead of by a launch ahead that the CTA would wait for.  All
+// threads call it.
+__device__ __forceinline__ void cta_work_ranked(const PrefillArgs& a, int b, Work& w,
+                                                uint8_t* scratch) {
+  static_assert(kMaxCtaRankedRts <= kThreads, "one pair per thread");
+  static_assert(kMaxCtaRankedRts * 20 + 4 <= kQBytes, "the scratch lies in the query tile");
+  int4* s_row = reinterpret_cast<int4*>(scratch);
+  int32_t* s_size = reinterpret_cast<int32_t*>(scratch + kMaxCtaRankedRts * 16);
+  int32_t* s_pick = s_size + kMaxCtaRankedRts;
+  const int tid = threadIdx.x;
+  const int R = a.num_rows, Q = a.qtiles, H = a.num_heads;
+  const int n_rt = R * Q;  // <= kMaxCtaRankedRts (host); the grid is n_rt * H
+  int size = 0;
+  if (tid < n_rt) {
+    const int rt = tid, r = rt % R, t0 = (Q - 1 - rt / R) * kRows;
+    const int tok0 = __ldcg(a.cu_q + r);
+    const int n = __ldcg(a.cu_q + r + 1) - tok0;
+    const int ctx = __ldcg(a.context_lens + r);
+    const int row_tab = a.seq_rows != nullptr ? __ldcg(a.seq_rows + r) : r;
+    s_row[rt] = make_int4(tok0, n, ctx, row_tab);
+    // Rows the kernel rejects or skips count as no work (they are checked below).
+    if (n > 0 && t0 < n && ctx >= n && ctx <= a.max_blocks * 16) {
+      const long long kv_end = min(static_cast<long long>(ctx),
+                                   static_cast<long long>(ctx - n) + t0 + kRows);
+      size = static_cast<int>((kv_end + kKeys - 1) / kKeys);
+    }
+    s_size[rt] = size;
+  }
+  __syncthreads();
+  if (tid < n_rt) {
+    int rank = 0;
+#pragma unroll 8
+    for (int f = 0; f < n_rt; ++f) {
+      const int g = s_size[f];
+      rank += (g > size || (g == size && f < tid)) ? 1 : 0;
+    }
+    if (rank == b / H) *s_pick = tid;  // the ranks are a permutation of 0 .. n_rt - 1
+  }
+  __syncthreads();
+  const int rt = *s_pick;
+  const int4 row = s_row[rt];
+  w.h = b % H;
+  w.sp = 0;
+  w.item = rt * H + w.h;
+  w.r = rt % R;
+  w.t0 = (Q - 1 - rt / R) * kRows;
+  w.tok0 = row.x;
+  w.n = row.y;
+  w.ctx = row.z;
+  w.row_tab = row.w;
+  __syncthreads();  // the scratch is the query tile's shared memory
+}
+
 __global__ void __launch_bounds__(kThreads, 2)
     prefill_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap kmap,
                    const __grid_constant__ CUtensorMap vmap, const PrefillArgs a) {
@@ -244,7 +300,11 @@ __global__ void __launch_bounds__(kThreads, 2)
   pdl_wait();
 
   Work wk;
-  if (!cta_work(a, blockIdx.x, wk)) return;
+  if (a.rank_in_cta) {
+    cta_work_ranked(a, blockIdx.x, wk, smem);
+  } else if (!cta_work(a, blockIdx.x, wk)) {
+    return;
+  }
   const int item = wk.item, h = wk.h, t0 = wk.t0, sp = wk.sp, tok0 = wk.tok0, n = wk.n;
   if (t0 == 0 && h == 0 && tid == 0 && n > a.qtiles * kRows) set_status(a.status, kStatusBadLength);
   if (t0 >= n) return;

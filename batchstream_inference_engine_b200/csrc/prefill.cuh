@@ -38,7 +38,14 @@ struct PrefillArgs {
   // ranked by key tiles, most first: when the grid is more than one wave of
   // resident CTAs, the longest ranges then start in the first.
   int4* plan;
+  // Non-zero (with plan null and splits 1, for at most kMaxCtaRankedRts rows x
+  // query tiles): every CTA ranks the (row, query tile) pairs itself, in the
+  // plan kernel's order, and takes entry b / H; no plan launch ahead.
+  int32_t rank_in_cta;
 };
+
+// Rows x query tiles a prefill CTA ranks itself (one per thread).
+constexpr int kMaxCtaRankedRts = 192;
 
 constexpr int kMinSplitTiles = 4;
 constexpr int kMaxPrefillSplits = 4;

@@ -245,16 +245,19 @@ def _prefill_launches(chunks, priors, max_query_len=None, seed=3):
 def test_prefill_launch_policy():
     # Query tiles (chunks x heads x 128-token tiles) below the SM count: key
     # ranges split, merged by a second kernel.  Up to one wave of resident CTAs
-    # (two per SM): the prefill kernel alone.  More than a wave: a planning
-    # kernel ranks the tiles first.
+    # (two per SM): the prefill kernel alone.  More than a wave: the tiles are
+    # ranked by key tiles first, inside every CTA for up to 192 (chunk, query
+    # tile) pairs, by a planning kernel launched ahead for more.
     sms = torch.cuda.get_device_properties(DEV).multi_processor_count
     small = ([300], [2000])                   # 14 x 3 = 42 tiles
     one_wave = ([200] * 8, [64 * i for i in range(8)])   # 8 x 14 x 2 = 224 tiles
-    large = ([512] * 8, [3485, 2609, 2094, 1105, 1261, 167, 308, 67])  # 448 tiles
+    large = ([512] * 8, [3485, 2609, 2094, 1105, 1261, 167, 308, 67])  # 32 pairs, 448 tiles
+    many = ([200] * 100, [37 * (i % 11) for i in range(100)])  # 200 pairs, 2800 tiles
     assert 42 < sms <= 224 <= 2 * sms < 448
     base = _prefill_launches(*one_wave)
     assert _prefill_launches(*small) == base + 1
-    assert _prefill_launches(*large) == base + 1
+    assert _prefill_launches(*large) == base
+    assert _prefill_launches(*many) == base + 1
 
 
 def test_planned_prefill_bad_table_sets_status():
