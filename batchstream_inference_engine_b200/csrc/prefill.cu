@@ -436,6 +436,15 @@ __global__ void __launch_bounds__(kThreads, 2)
     if ((!ok || !drained) && lane == 0) set_status(a.status, kStatusWaitTimeout);
   } else if (warp == 4) {
     // ---------------------------------------------------------------- MMA issuer
+    // Shared-memory descriptors of every operand, built once: a stage, buffer
+    // or 16-wide K slice only moves the start address, whose field is the
+    // address / 16 in the low 14 bits (every address here stays below 2^18),
+    // so each MMA's descriptors are one add away from these.
+    const uint64_t desc_q = umma_desc(smem_u32(sQ), 16, 1024);
+    const uint64_t desc_k = umma_desc(smem_u32(sK(0)), 16, 1024);
+    const uint64_t desc_v = umma_desc(smem_u32(sV(0)), 8192, 1024);
+    const uint64_t desc_p = umma_desc(smem_u32(sP(0)), 16, 1024);
+    constexpr uint64_t kStageStep = kTileBytes >> 4, kPStep = kPBytes >> 4;
     bool ok = wait_all(&q_full, 0);
     for (int u = 0; u < ntiles + 2 && ok; ++u) {
       // Step u: P V(j = u - 2) once softmax(j) has written P(j) (which also
@@ -451,21 +460,21 @@ __global__ void __launch_bounds__(kThreads, 2)
       tc_fence_after();
       if (lane == 0) {
         if (j >= 0) {
-          const uint32_t p0 = smem_u32(sP(j & 1));
-          const uint32_t v0 = smem_u32(sV(j % kVStages));
+          const uint64_t p0 = desc_p + (j & 1) * kPStep;
+          const uint64_t v0 = desc_v + (j % kVStages) * kStageStep;
 #pragma unroll
           for (int k = 0; k < kKeys / 16; ++k) {
-            umma_f16(tmem + kTmemO, umma_desc(p0 + 32 * k, 16, 1024),
-                     umma_desc(v0 + 2048 * k, 8192, 1024), kIdescO, (j > 0 || k > 0) ? 1u : 0u);
+            // P: 32 bytes per 16-key slice; V: 2048 bytes (16 key rows).
+            umma_f16(tmem + kTmemO, p0 + 2 * k, v0 + 128 * k, kIdescO, (j > 0 || k > 0) ? 1u : 0u);
           }
         }
         if (u < ntiles) {
           const uint32_t d = tmem + (u & 1) * kKeys;
-          const uint32_t k0 = smem_u32(sK(u % kKStages));
+          const uint64_t k0 = desc_k + (u % kKStages) * kStageStep;
 #pragma unroll
           for (int k = 0; k < kD / 16; ++k) {
-            umma_f16(d, umma_desc(smem_u32(sQ) + 32 * k, 16, 1024),
-                     umma_desc(k0 + 32 * k, 16, 1024), kIdescS, k > 0 ? 1u : 0u);
+            // Q and K: 32 bytes per 16-dim slice.
+            umma_f16(d, desc_q + 2 * k, k0 + 2 * k, kIdescS, k > 0 ? 1u : 0u);
           }
         }
         umma_commit(&step_done[u % kSteps]);
