@@ -93,8 +93,11 @@ def mixed_prefill_batch(chunks, priors, heads=14, kv_heads=2, head_dim=64, seed=
 
 
 def fp32_reference(q, k, v, tables, chunks, priors, groups, scale):
-    """Plain fp32 attention of every chunk token over its causal length, from
-    the bf16-rounded inputs: [T, H, D]."""
+    """fp32 attention of every chunk token over its causal length, from the
+    bf16-rounded inputs: [T, H, D].  The raw scores q . k are rounded to bf16
+    first, as the reference's bf16 matmul leaves them (its largest departure
+    from fp32: up to about 2% of the output's range on a token whose top
+    scores are large); softmax and P V stay in fp32."""
     kf, vf = k.bfloat16().float(), v.bfloat16().float()
     Hkv, _, bs, D = kf.shape
     outs, start = [], 0
@@ -104,7 +107,7 @@ def fp32_reference(q, k, v, tables, chunks, priors, groups, scale):
         ks = kf.view(Hkv, -1, D)[:, slots]  # [Hkv, total, D]
         vs = vf.view(Hkv, -1, D)[:, slots]
         qs = q[start: start + c].bfloat16().float().view(c, Hkv, groups, D)
-        scores = torch.einsum("thgd,hkd->hgtk", qs, ks) * scale
+        scores = torch.einsum("thgd,hkd->hgtk", qs, ks).bfloat16().float() * scale
         visible = torch.arange(total)[None, :] <= (p + torch.arange(c))[:, None]
         scores = scores.masked_fill(~visible, float("-inf"))
         o = torch.einsum("hgtk,hkd->thgd", torch.softmax(scores, dim=-1), vs)
@@ -258,6 +261,24 @@ def test_prefill_launch_policy():
     assert _prefill_launches(*small) == base + 1
     assert _prefill_launches(*large) == base
     assert _prefill_launches(*many) == base + 1
+
+
+@pytest.mark.parametrize("rows,plan_launches", [(96, 0), (97, 1)])
+def test_work_ranked_in_the_ctas_up_to_192_pairs(rows, plan_launches):
+    # Every chunk holds 129..256 tokens, two query tiles: 96 chunks are the
+    # largest batch the CTAs rank themselves (192 pairs), 97 take the planning
+    # kernel.  Both exceed a wave of CTAs; every token is checked against fp32
+    # and sampled tokens against the oracle.
+    chunks = [129 + (37 * i) % 128 for i in range(rows)]
+    priors = [(53 * i) % 700 for i in range(rows)]
+    base = _prefill_launches([200] * 8, [64 * i for i in range(8)])
+    assert _prefill_launches(chunks, priors, max_query_len=256, seed=17) == base + plan_launches
+    q, k, v, tables, bt, cu, ctx = mixed_prefill_batch(chunks, priors, seed=17)
+    out = ops.prefill_attention(q.bfloat16().to(DEV), k.bfloat16().to(DEV), v.bfloat16().to(DEV),
+                                bt.to(DEV), cu.to(DEV), ctx.to(DEV), 0.125, max_query_len=256)
+    assert ops.take_status() == 0
+    picks = [(r, i) for r in (0, rows // 2, rows - 1) for i in (0, 128, chunks[r] - 1)]
+    check_rows(out, q, k, v, tables, chunks, priors, 7, 0.125, picks)
 
 
 def test_planned_prefill_bad_table_sets_status():
