@@ -179,10 +179,14 @@ WsLayout ws_layout(int64_t segments, int64_t staging_ints, int64_t grid, int64_t
   return w;
 }
 
-// Split-KV factor of the tensor-core prefill: up to one CTA per SM.  A second
-// CTA on an SM adds less than a first, and every piece costs a CTA's set-up and
-// a merge, so only batches with fewer query tiles than SMs are split.
-int prefill_splits(int64_t items, int sms) {
+// Split-KV factor of the tensor-core prefill: up to one CTA per SM for the
+// query tiles that can hold tokens (at most ceil(num_tokens / 128) + num_rows
+// per head; the other tiles of a padded launch exit at once).  A second CTA on
+// an SM adds less than a first, and every piece costs a CTA's set-up and a
+// merge, so only batches with fewer such tiles than SMs are split.
+int prefill_splits(int64_t num_rows, int64_t qtiles, int64_t num_tokens, int64_t heads, int sms) {
+  const int64_t items =
+      std::min(num_rows * qtiles, (num_tokens + 127) / 128 + num_rows) * heads;
   if (items <= 0) return 1;
   const int64_t want = (static_cast<int64_t>(sms) + items - 1) / items;
   return static_cast<int>(std::min<int64_t>(std::max<int64_t>(want, 1), bsb::kMaxPrefillSplits));
@@ -644,7 +648,7 @@ int bs_prefill_attention_workspace_bytes(int64_t num_tokens, int64_t num_rows,
   if (int rc = current_device_info(&d)) return rc;
   const int64_t qtiles = (max_query_len + 127) / 128;
   const int64_t items = num_rows * num_heads * qtiles;
-  const int splits = prefill_splits(items, d->sms);
+  const int splits = prefill_splits(num_rows, qtiles, num_tokens, num_heads, d->sms);
   const int64_t rts = prefill_plan_rts(num_rows, qtiles, num_tokens, num_heads, splits, d->sms);
   need = std::max(need, prefill_ws_bytes(items, splits, rts * splits));
   *bytes_out = static_cast<uint64_t>(need);
@@ -732,7 +736,7 @@ int bs_prefill_attention(const void* query, int64_t query_token_stride, const in
     if ((rc = current_device_info(&d))) return rc;
     // Split and plan as far as the workspace holds them.
     const int64_t wsb = static_cast<int64_t>(workspace_bytes);
-    p.splits = prefill_splits(items, d->sms);
+    p.splits = prefill_splits(num_rows, p.qtiles, num_tokens, num_heads, d->sms);
     if (wsb < prefill_ws_bytes(items, p.splits, 0)) p.splits = 1;
     int64_t rts =
         prefill_plan_rts(num_rows, p.qtiles, num_tokens, num_heads, p.splits, d->sms);
@@ -757,7 +761,7 @@ int bs_prefill_attention(const void* query, int64_t query_token_stride, const in
     if (rc != 0) return cuda_fail(static_cast<cudaError_t>(rc), "prefill kernel launch");
     count_launches(1);
     if (p.splits > 1) {
-      rc = bsb::launch_prefill_merge(p, static_cast<int>(items), st);
+      rc = bsb::launch_prefill_merge(p, items, st);
       if (rc != 0) return cuda_fail(static_cast<cudaError_t>(rc), "prefill merge launch");
       count_launches(1);
     }

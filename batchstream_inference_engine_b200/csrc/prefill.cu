@@ -68,6 +68,9 @@ constexpr uint32_t kTmemCols = 256;  // S0 [0, 64), S1 [64, 128), O [128, 192)
 constexpr uint32_t kTmemO = 128;
 constexpr float kLog2eP = 1.4426950408889634f;
 constexpr float kRescaleSlack = 8.f;  // rescale O when a row max grows by > 2^8
+// Merge pass: query rows per CTA, eight threads per row.
+constexpr int kMergeRowsPerCta = 32;
+constexpr int kMergeThreads = kMergeRowsPerCta * 8;
 
 __device__ __forceinline__ uint64_t umma_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
   // sm100 shared-memory matrix descriptor: start, leading and stride byte
@@ -664,15 +667,20 @@ __global__ void __launch_bounds__(kThreads, 2)
   }
 }
 
-// Merges the split records of one work item per CTA, one query row per
-// thread: out = sum_s 2^(m_s - M) O_s / sum_s 2^(m_s - M) l_s in bf16.  Items
-// whose key range was not split were written by the prefill kernel itself.
-__global__ void __launch_bounds__(kRows) prefill_merge_kernel(const PrefillArgs a) {
+// Merges the split records of the work items, kMergeRowsPerCta query rows of
+// one item per CTA and eight threads per row (eight columns each), so that a
+// thread's loads are all independent: one round trip for the (max, sum) pairs
+// of its row, one for its columns of every record.  out = sum_s 2^(m_s - M) O_s /
+// sum_s 2^(m_s - M) l_s in bf16, summed in split order.  Items whose key range
+// was not split were written by the prefill kernel itself.
+__global__ void __launch_bounds__(kMergeThreads) prefill_merge_kernel(const PrefillArgs a) {
   pdl_wait();
+  constexpr int kCtasPerItem = kRows / kMergeRowsPerCta;
   Work wk;
-  item_work(a, blockIdx.x * a.splits, wk);
+  item_work(a, (blockIdx.x / kCtasPerItem) * a.splits, wk);
   const int item = wk.item, h = wk.h, t0 = wk.t0, tok0 = wk.tok0, n = wk.n;
-  const int row = threadIdx.x;
+  const int row = (blockIdx.x % kCtasPerItem) * kMergeRowsPerCta + threadIdx.x / 8;
+  const int c = (threadIdx.x % 8) * 8;
   if (t0 >= n || t0 + row >= n) return;
   const int ctx = wk.ctx;
   const int prior = ctx - n;
@@ -682,52 +690,51 @@ __global__ void __launch_bounds__(kRows) prefill_merge_kernel(const PrefillArgs 
   const int nsplit = prefill_tile_splits((kv_end + kKeys - 1) / kKeys, a.splits);
   if (nsplit <= 1) return;
   const int64_t rec0 = static_cast<int64_t>(item) * a.splits;
-  float m[kMaxPrefillSplits], w[kMaxPrefillSplits];
-  float M = -INFINITY;
+  float2 ml[kMaxPrefillSplits];
+  float4 x[kMaxPrefillSplits], y[kMaxPrefillSplits];
 #pragma unroll
   for (int s = 0; s < kMaxPrefillSplits; ++s) {
-    m[s] = -INFINITY;
-    w[s] = 0.f;
+    ml[s] = make_float2(-INFINITY, 0.f);
+    x[s] = y[s] = make_float4(0.f, 0.f, 0.f, 0.f);
     if (s < nsplit) {
-      const float2 ml =
-          *reinterpret_cast<const float2*>(a.part_ml + ((rec0 + s) * kRows + row) * 2);
-      m[s] = ml.x;
-      w[s] = ml.y;
-      M = fmaxf(M, ml.x);
+      const int64_t r = (rec0 + s) * kRows + row;
+      ml[s] = *reinterpret_cast<const float2*>(a.part_ml + r * 2);
+      const float* o = a.part_o + r * kD + c;
+      x[s] = *reinterpret_cast<const float4*>(o);
+      y[s] = *reinterpret_cast<const float4*>(o + 4);
     }
   }
+  float M = -INFINITY;
+#pragma unroll
+  for (int s = 0; s < kMaxPrefillSplits; ++s) M = fmaxf(M, ml[s].x);
+  float w[kMaxPrefillSplits];
   float L = 0.f;
 #pragma unroll
   for (int s = 0; s < kMaxPrefillSplits; ++s) {
     // A range none of whose keys this row sees has max -inf: weight 0, and its
-    // O (all zero) is not read.
-    const float f = m[s] == -INFINITY ? 0.f : fast_exp2(m[s] - M);
-    L += f * w[s];
+    // O (all zero) does not enter the sum.
+    const float f = ml[s].x == -INFINITY ? 0.f : fast_exp2(ml[s].x - M);
+    L += f * ml[s].y;
     w[s] = f;
   }
   const float inv = 1.f / L;
+  float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+  for (int s = 0; s < kMaxPrefillSplits; ++s) {
+    if (w[s] == 0.f) continue;  // also every s >= nsplit
+    acc[0] += w[s] * x[s].x; acc[1] += w[s] * x[s].y; acc[2] += w[s] * x[s].z;
+    acc[3] += w[s] * x[s].w; acc[4] += w[s] * y[s].x; acc[5] += w[s] * y[s].y;
+    acc[6] += w[s] * y[s].z; acc[7] += w[s] * y[s].w;
+  }
+  uint4 out;
+  out.x = pack_bf16x2(acc[0] * inv, acc[1] * inv);
+  out.y = pack_bf16x2(acc[2] * inv, acc[3] * inv);
+  out.z = pack_bf16x2(acc[4] * inv, acc[5] * inv);
+  out.w = pack_bf16x2(acc[6] * inv, acc[7] * inv);
   __nv_bfloat16* dst = static_cast<__nv_bfloat16*>(a.out) +
                        static_cast<int64_t>(tok0 + t0 + row) * a.o_stride_tok +
-                       static_cast<int64_t>(h) * kD;
-#pragma unroll 4
-  for (int c = 0; c < kD; c += 8) {
-    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-    for (int s = 0; s < kMaxPrefillSplits; ++s) {
-      if (w[s] == 0.f) continue;  // also every s >= nsplit
-      const float* o = a.part_o + ((rec0 + s) * kRows + row) * kD + c;
-      const float4 x = *reinterpret_cast<const float4*>(o);
-      const float4 y = *reinterpret_cast<const float4*>(o + 4);
-      acc[0] += w[s] * x.x; acc[1] += w[s] * x.y; acc[2] += w[s] * x.z; acc[3] += w[s] * x.w;
-      acc[4] += w[s] * y.x; acc[5] += w[s] * y.y; acc[6] += w[s] * y.z; acc[7] += w[s] * y.w;
-    }
-    uint4 out;
-    out.x = pack_bf16x2(acc[0] * inv, acc[1] * inv);
-    out.y = pack_bf16x2(acc[2] * inv, acc[3] * inv);
-    out.z = pack_bf16x2(acc[4] * inv, acc[5] * inv);
-    out.w = pack_bf16x2(acc[6] * inv, acc[7] * inv);
-    *reinterpret_cast<uint4*>(dst + c) = out;
-  }
+                       static_cast<int64_t>(h) * kD + c;
+  *reinterpret_cast<uint4*>(dst) = out;
 }
 
 
@@ -792,10 +799,12 @@ __global__ void __launch_bounds__(kPlanThreads) prefill_plan_kernel(const Prefil
 
 int prefill_smem_bytes() { return kSmemBytes; }
 
-int launch_prefill_merge(const PrefillArgs& a, int items, cudaStream_t stream) {
+int launch_prefill_merge(const PrefillArgs& a, int64_t items, cudaStream_t stream) {
+  const int64_t grid = items * (kRows / kMergeRowsPerCta);
+  if (grid > 0x7fffffff) return static_cast<int>(cudaErrorInvalidConfiguration);
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(items);
-  cfg.blockDim = dim3(kRows);
+  cfg.gridDim = dim3(static_cast<unsigned>(grid));
+  cfg.blockDim = dim3(kMergeThreads);
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;

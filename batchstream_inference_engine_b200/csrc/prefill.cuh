@@ -62,7 +62,7 @@ int prefill_smem_bytes();
 // Record floats per split CTA (O rows, then (max, sum) per row).
 constexpr int64_t kPrefillRecordO = 128 * 64;
 constexpr int64_t kPrefillRecordML = 128 * 2;
-int launch_prefill_merge(const PrefillArgs& a, int items, cudaStream_t stream);
+int launch_prefill_merge(const PrefillArgs& a, int64_t items, cudaStream_t stream);
 int launch_prefill_plan(const PrefillArgs& a, cudaStream_t stream);
 int prefill_ctas_per_sm();
 int launch_prefill_tc(const PrefillArgs& a, const CUtensorMap& qmap, const CUtensorMap& kmap,

@@ -261,6 +261,11 @@ def test_prefill_launch_policy():
     assert _prefill_launches(*small) == base + 1
     assert _prefill_launches(*large) == base
     assert _prefill_launches(*many) == base + 1
+    # A padded launch (a CUDA-graph bucket of 512 query tokens holding four
+    # 128-token chunks): 224 query tiles launched, at most 8 x 14 hold tokens,
+    # so the key ranges are split and merged.
+    padded = ([128] * 4, [2000, 500, 100, 1200])
+    assert _prefill_launches(*padded, max_query_len=512) == base + 1
 
 
 @pytest.mark.parametrize("rows,plan_launches", [(96, 0), (97, 1)])
