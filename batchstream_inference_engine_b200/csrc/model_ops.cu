@@ -63,6 +63,8 @@ __device__ __forceinline__ void round8<__nv_bfloat16>(float (&v)[8]) {
 // VEC: 8 elements per access (hidden and every row stride a multiple of 8,
 // 16-byte aligned rows).
 constexpr int kNormRowsPerCta = 4;
+// Rows up to kNormChunks x 256 elements (8 per lane and chunk) stay in registers.
+constexpr int kNormChunks = 4;
 
 template <typename T, bool VEC>
 __global__ void __launch_bounds__(32 * kNormRowsPerCta)
@@ -89,6 +91,51 @@ __global__ void __launch_bounds__(32 * kNormRowsPerCta)
   T* orow = out + static_cast<int64_t>(r) * out_stride;
   float ss = 0.f;
   if constexpr (VEC) {
+    if (hidden <= kNormChunks * 256) {
+      // The whole row in registers, every load issued before the first use
+      // (one round trip instead of one per chunk and pass); same arithmetic
+      // in the same order as the loops below.
+      float v[kNormChunks][8], a[kNormChunks][8], wt[kNormChunks][8];
+#pragma unroll
+      for (int k = 0; k < kNormChunks; ++k) {
+        const int32_t i = lane * 8 + k * 256;
+        if (i < hidden) {
+          load8(row + i, v[k]);
+          if (arow != nullptr) load8(arow + i, a[k]);
+          load8(w + i, wt[k]);
+        }
+      }
+#pragma unroll
+      for (int k = 0; k < kNormChunks; ++k) {
+        const int32_t i = lane * 8 + k * 256;
+        if (i < hidden) {
+          if (arow != nullptr) {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) v[k][j] = __fadd_rn(v[k][j], a[k][j]);
+            round8<T>(v[k]);
+          }
+          if (srow != nullptr) store8(srow + i, v[k]);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) ss = fmaf(v[k][j], v[k][j], ss);
+        }
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+      const float inv = rsqrtf(ss / static_cast<float>(hidden) + eps);
+#pragma unroll
+      for (int k = 0; k < kNormChunks; ++k) {
+        const int32_t i = lane * 8 + k * 256;
+        if (i < hidden) {
+#pragma unroll
+          for (int j = 0; j < 8; ++j) v[k][j] = __fmul_rn(v[k][j], inv);
+          round8<T>(v[k]);  // normalized.to(T)
+#pragma unroll
+          for (int j = 0; j < 8; ++j) v[k][j] = __fmul_rn(wt[k][j], v[k][j]);
+          store8(orow + i, v[k]);
+        }
+      }
+      return;
+    }
     for (int32_t i = lane * 8; i < hidden; i += 256) {
       float v[8];
       load8(row + i, v);
@@ -204,6 +251,76 @@ __global__ void __launch_bounds__(128)
       dst[d] = st<Tpool>(lo);
       dst[d + half] = st<Tpool>(hi);
     }
+  }
+}
+
+// rope_append_kernel for bf16 rows and pools with 16-byte accesses: one thread
+// per (token, head, 8-dim chunk of the head's first half), which also rotates
+// the partner dims half a head away; the per-element arithmetic is the scalar
+// kernel's.  Needs D a multiple of 16 and every row 16-byte aligned.
+__global__ void __launch_bounds__(128)
+    rope_append_vec_kernel(const __nv_bfloat16* __restrict__ qkv, int64_t qkv_stride,
+                           const __nv_bfloat16* __restrict__ cos_t,
+                           const __nv_bfloat16* __restrict__ sin_t, int32_t num_pos,
+                           const int32_t* __restrict__ pos, const int32_t* __restrict__ slots,
+                           int32_t ntok, int32_t H, int32_t Hkv, int32_t D,
+                           __nv_bfloat16* __restrict__ q_out, __nv_bfloat16* __restrict__ k_pool,
+                           __nv_bfloat16* __restrict__ v_pool, int64_t pool_slots,
+                           uint32_t* status) {
+  pdl_trigger();
+  pdl_wait();
+  const int32_t half = D >> 1, chunks = half >> 3;
+  const int32_t per_tok = (H + 2 * Hkv) * chunks;
+  const int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (idx >= static_cast<int64_t>(ntok) * per_tok) return;
+  const int32_t t = static_cast<int32_t>(idx / per_tok);
+  const int32_t rem = static_cast<int32_t>(idx - static_cast<int64_t>(t) * per_tok);
+  const int32_t hh = rem / chunks, d = (rem - hh * chunks) * 8;
+  const __nv_bfloat16* row = qkv + t * qkv_stride + hh * D;
+  float a[8], b[8];
+  load8(row + d, a);
+  load8(row + d + half, b);
+  const int32_t slot = hh >= H ? slots[t] : -1;
+  if (slot >= pool_slots) {
+    if (d == 0) set_status(status, kStatusBadSlot);
+    return;
+  }
+  if (hh >= H + Hkv) {  // v: copied into its slot
+    if (slot >= 0) {
+      __nv_bfloat16* dst = v_pool + (static_cast<int64_t>(hh - H - Hkv) * pool_slots + slot) * D;
+      store8(dst + d, a);
+      store8(dst + d + half, b);
+    }
+    return;
+  }
+  const int32_t p = pos[t];
+  if (p < 0 || p >= num_pos) {
+    if (d == 0 && hh == 0) set_status(status, kStatusBadPosition);
+    return;
+  }
+  float c0[8], c1[8], s0[8], s1[8];
+  const int64_t prow = static_cast<int64_t>(p) * D;
+  load8(cos_t + prow + d, c0);
+  load8(cos_t + prow + d + half, c1);
+  load8(sin_t + prow + d, s0);
+  load8(sin_t + prow + d + half, s1);
+  float lo[8], hi[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    lo[j] = round_bf16(__fadd_rn(round_bf16(__fmul_rn(a[j], c0[j])),
+                                 round_bf16(__fmul_rn(-b[j], s0[j]))));
+    hi[j] = round_bf16(__fadd_rn(round_bf16(__fmul_rn(b[j], c1[j])),
+                                 round_bf16(__fmul_rn(a[j], s1[j]))));
+  }
+  __nv_bfloat16* dst = nullptr;
+  if (hh < H) {
+    dst = q_out + (static_cast<int64_t>(t) * H + hh) * D;
+  } else if (slot >= 0) {
+    dst = k_pool + (static_cast<int64_t>(hh - H) * pool_slots + slot) * D;
+  }
+  if (dst != nullptr) {
+    store8(dst + d, lo);
+    store8(dst + d + half, hi);
   }
 }
 
@@ -359,6 +476,19 @@ int launch_rope_append(const void* qkv, int64_t qkv_stride, const void* cos_t, c
   if (ntok == 0) return 0;
   const int32_t pairs = (H + 2 * Hkv) * (D / 2);
   cudaLaunchAttribute attr[1];
+  auto a16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
+  if (bf16 && pool_bf16 && D % 16 == 0 && qkv_stride % 8 == 0 && a16(qkv) && a16(cos_t) &&
+      a16(sin_t) && a16(q_out) && a16(k_pool) && a16(v_pool)) {
+    const int64_t threads = static_cast<int64_t>(ntok) * (H + 2 * Hkv) * (D / 16);
+    cudaLaunchConfig_t cfg = cfg_of(dim3(static_cast<unsigned>((threads + 127) / 128)), 128,
+                                    stream, attr);
+    return static_cast<int>(cudaLaunchKernelEx(
+        &cfg, rope_append_vec_kernel, static_cast<const __nv_bfloat16*>(qkv), qkv_stride,
+        static_cast<const __nv_bfloat16*>(cos_t), static_cast<const __nv_bfloat16*>(sin_t),
+        num_pos, pos, slots, ntok, H, Hkv, D, static_cast<__nv_bfloat16*>(q_out),
+        static_cast<__nv_bfloat16*>(k_pool), static_cast<__nv_bfloat16*>(v_pool), pool_slots,
+        status));
+  }
   cudaLaunchConfig_t cfg =
       cfg_of(dim3((pairs + 127) / 128, ntok < kMaxGridY ? ntok : kMaxGridY), 128, stream, attr);
 #define BS_ROPE(T, TP)                                                                          \

@@ -45,7 +45,7 @@ def norm_bound(out, ref, dtype):
 
 
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
-@pytest.mark.parametrize("hidden", [896, 100], ids=["vector", "scalar"])
+@pytest.mark.parametrize("hidden", [896, 2048, 100], ids=["vector", "vector_long", "scalar"])
 def test_rms_norm_with_residual_add_in_place(dtype, hidden):
     g = torch.Generator(device=DEV).manual_seed(0)
     T = 37
@@ -133,9 +133,10 @@ def test_rope_append_matches_the_torch_ops_bit_for_bit(dtype, pool_dtype):
     assert torch.equal(vp, vp_ref)
 
 
-def test_rope_append_reports_bad_positions_and_slots():
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32], ids=["vector", "scalar"])
+def test_rope_append_reports_bad_positions_and_slots(dtype):
     qkv, cos, sin, positions, slots, kp, vp, (T, H, Hkv, D) = make_rope_case(
-        torch.bfloat16, torch.bfloat16)
+        dtype, torch.bfloat16)
     before_k, before_v = kp.clone(), vp.clone()
     bad_pos = positions.clone()
     bad_pos[0] = cos.shape[0]
