@@ -7,8 +7,8 @@
 // with _causal_mask (src/server/torch_model.py:39-64, 165-167, 295-297).
 //
 // One CTA per (chunk, query head, 128-token query tile, piece of its key
-// range; pieces only for batches with fewer query tiles than SMs, merged by
-// prefill_merge_kernel).  A CTA's time is its chain of key tiles, so when the
+// range; pieces only for batches with fewer query tiles that can hold tokens
+// than SMs, merged by prefill_merge_kernel).  A CTA's time is its chain of key tiles, so when the
 // grid is more than one wave of resident CTAs a one-CTA plan kernel runs first
 // and ranks the work by key tiles: the longest chains start in the first wave
 // instead of whenever their index comes up.  Three roles, one warp each for

@@ -201,9 +201,11 @@ int bs_prefill_attention(const void* query, int64_t query_token_stride, const in
 /*
  * Workspace for bs_prefill_attention over num_tokens tokens in num_rows chunks
  * of at most max_query_len tokens.  On the tensor-core path a small batch of
- * chunks (fewer query tiles than SMs) splits each tile's key range over up to
- * 4 CTAs whose partial results a second kernel merges, and a batch of more
- * than one wave of CTAs is ranked first (query tiles with the most keys start
+ * chunks (fewer query tiles than SMs, counting the at most
+ * ceil(num_tokens / 128) + num_rows per head that can hold tokens) splits
+ * each tile's key range over up to 4 CTAs whose partial results a second
+ * kernel merges, and a batch of more than one wave of CTAs is ranked first
+ * (query tiles with the most keys start
  * first): inside every CTA for up to 192 (chunk, query tile) pairs, by a
  * planning kernel launched ahead for more.  The split records and the plan
  * live in this workspace; a smaller one only turns them off.
