@@ -205,9 +205,8 @@ int bs_prefill_attention(const void* query, int64_t query_token_stride, const in
  * ceil(num_tokens / 128) + num_rows per head that can hold tokens) splits
  * each tile's key range over up to 4 CTAs whose partial results a second
  * kernel merges, and a batch of more than one wave of CTAs is ranked first
- * (query tiles with the most keys start
- * first): inside every CTA for up to 192 (chunk, query tile) pairs, by a
- * planning kernel launched ahead for more.  The split records and the plan
+ * (query tiles with the most keys start first): inside every CTA for up to 192
+ * (chunk, query tile) pairs, by a planning kernel launched ahead for more.  The split records and the plan
  * live in this workspace; a smaller one only turns them off.
  */
 int bs_prefill_attention_workspace_bytes(int64_t num_tokens, int64_t num_rows,
