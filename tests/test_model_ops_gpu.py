@@ -214,6 +214,11 @@ def test_argmax_rows_matches_torch(dtype, vocab):
     x[4] = -float("inf")                   # all -inf: index 0
     x[5, 77] = float("nan")                # NaN counts as the maximum
     x[6, 900] = x[6, 100] = float("nan")   # the first NaN
+    if vocab > 6 * 4096:
+        # Ties among one thread's elements (every 4096th column, 8 per chunk),
+        # loaded in the same round and in different rounds.
+        x[7, 8 + 2 * 4096] = x[7, 8] = x[7].max() + 1
+        x[8, 9 + 5 * 4096] = x[8, 9 + 4096] = x[8].max() + 1
     got = ops.argmax_rows(x)
     assert torch.equal(got.long(), x.float().argmax(dim=-1))
     assert got[3].item() == 10 and got[4].item() == 0 and got[5].item() == 77
