@@ -7,7 +7,6 @@ max-abs <= 2e-2 * max|ref| against fp32, and element-wise
 Both the tcgen05 path (bf16, head_dim 64) and the per-token path run.
 """
 
-import math
 from pathlib import Path
 
 import numpy as np

@@ -11,7 +11,6 @@ tolerance as the other bf16 decode tests.  This file is collected last on
 purpose and also passes on its own in a fresh process.
 """
 
-import ctypes
 import math
 
 import numpy as np
